@@ -1,0 +1,590 @@
+/* moe_layer.cu - one routed-expert MoE layer as a single call, with the
+ * expert resolve on the device.
+ *
+ * The reference engine (crates/engine/src/lib.rs:7537-8705, Ffn::Moe arm)
+ * runs the router on the GPU, syncs, reads the selected ids back, builds
+ * the per-(token, slot) pointer array on the host, writes it back and then
+ * launches pair / q8_K / down.  Here the whole layer stays on the device:
+ *
+ *   1 router logits (binary64 fixed-order GEMV) ........ router_q8k.cu
+ *   2 q8_K of the hidden rows ........................... router_q8k.cu
+ *   3 top-k per token (warp per token); the last CTA to finish groups the
+ *     (token, slot) pairs by expert into a CSR work list (ascending expert
+ *     id, pairs in (token, slot) order) and appends the shared experts
+ *   4 gate/up: one CTA per (expert work item, row tile) streams the
+ *     expert's rows once through a TMA ring and serves every token routed
+ *     to it; glu * route weight -> mid.  The last tile CTA of each 256-row
+ *     block quantizes that block of every pair's mid row to q8_K.
+ *   5 down + combine: one CTA per tile of output rows walks all work
+ *     items in order, streams each expert's rows once, accumulates per
+ *     (token, row) in shared memory (fixed order -> deterministic), then
+ *     adds the down bias (sum_s w_s b_s, cu:3601) and the residual.
+ *
+ * Nothing is allocated; all state lives in the caller's workspace and the
+ * call is capturable into a CUDA graph.
+ */
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/pulsar_moe.h"
+#include "pm_host.h"
+#include "pm_router.cuh"
+#include "pm_stream.cuh"
+
+int pm_launch_q8k(void *out, const float *x, uint32_t in_dim, uint32_t n_rows, cudaStream_t st);
+int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
+                            uint32_t in_dim, uint32_t n_tok, cudaStream_t st);
+int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32_t mode, uint32_t n_shexp,
+                      uint32_t n_group, uint32_t topk_group);
+
+__device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
+
+/* ------------------------------------------------------------ layout */
+
+struct pm_layout {
+    uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
+    size_t logits, sel, w, xq, n_items, item_expert, item_start, pairs, mid, midq, cnt, sel_done, err, total;
+};
+
+static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
+    pm_layout L;
+    L.T = T;
+    L.E = d->n_expert;
+    L.k = d->n_used;
+    L.S = d->n_shared;
+    L.n_slot = L.k + L.S;
+    L.H = d->n_embd;
+    L.Fr = d->n_ff;
+    L.Fs = L.S ? d->shared_n_ff : 0;
+    L.Fmax = L.Fr > L.Fs ? L.Fr : L.Fs;
+    L.hb = (L.H + 255) / 256;
+    L.fb = (L.Fmax + 255) / 256;
+    const uint64_t routed = (uint64_t)T * L.k;
+    L.max_items = (uint32_t)((routed < L.E ? routed : L.E) + L.S);
+    size_t o = 0;
+    L.logits = o, o = pm_al(o + (size_t)T * L.E * 4);
+    L.sel = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
+    L.w = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
+    L.xq = o, o = pm_al(o + (size_t)T * L.hb * PM_Q8_K_BYTES);
+    L.n_items = o, o = pm_al(o + 16);
+    L.item_expert = o, o = pm_al(o + (size_t)L.max_items * 4);
+    L.item_start = o, o = pm_al(o + (size_t)(L.max_items + 1) * 4);
+    L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
+    L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
+    L.midq = o, o = pm_al(o + (size_t)T * L.n_slot * L.fb * PM_Q8_K_BYTES);
+    L.cnt = o, o = pm_al(o + (size_t)L.max_items * L.fb * 4);
+    L.sel_done = o, o = pm_al(o + 4);
+    L.err = o, o = pm_al(o + 4);
+    L.total = o;
+    return L;
+}
+
+/* device-side view of the descriptor + workspace */
+struct pm_layer_args {
+    /* geometry */
+    uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
+    uint32_t lo, hi, act, mode, n_group, topk_group;
+    float scale;
+    uint64_t rb_gu_r, rb_dn_r, st_gu_r, st_dn_r, rb_gu_s, rb_dn_s;
+    const uint8_t *gate, *up, *down, *sgate, *sup, *sdown;
+    const float *gate_b, *up_b, *down_b, *router_sel_b;
+    /* workspace */
+    float *logits;
+    int32_t *sel;
+    float *w;
+    pm_block_q8K *xq;
+    uint32_t *n_items; /* [0] all items, [1] routed items */
+    uint32_t *item_expert, *item_start, *pairs;
+    float *mid;
+    pm_block_q8K *midq;
+    uint32_t *cnt, *sel_done, *err;
+    /* io */
+    float *out;
+    const float *residual;
+    uint32_t gu_rows, dn_rows; /* rows per CTA */
+};
+
+/* ============================================ 3: select + CSR build */
+
+__global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_constant__ pm_layer_args a) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ uint32_t is_last;
+    const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+    const uint32_t token = blockIdx.x * 4u + wid;
+    if (token < a.T) {
+        float *score = (float *)sm + (size_t)wid * 2 * a.E;
+        pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0, a.n_group,
+                        a.topk_group, score, score + a.E);
+    }
+    /* sel/w rows are n_slot wide here; pm_select_token wrote them k wide */
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const uint32_t prev = atomicAdd(a.sel_done, 1u);
+        is_last = prev == gridDim.x - 1u;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    /* ---- the last CTA: CSR by expert over routed pairs in [lo, hi) ---- */
+    uint32_t *cnt = (uint32_t *)sm;       /* [E] counts, then cursors */
+    uint32_t *item_of = cnt + a.E;        /* [E] item index */
+    for (uint32_t e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const uint32_t n_routed = a.T * a.k;
+    for (uint32_t p = threadIdx.x; p < n_routed; p += blockDim.x) {
+        const uint32_t e = (uint32_t)__ldcg(a.sel + p);
+        if (e >= a.lo && e < a.hi) atomicAdd(&cnt[e], 1u);
+    }
+    __syncthreads();
+    __shared__ uint32_t tot_pairs, tot_items;
+    if (wid == 0) {
+        /* exclusive scans over experts: pair offsets and item indices */
+        uint32_t carry_p = 0, carry_i = 0;
+        for (uint32_t c = 0; c < a.E; c += 32u) {
+            const uint32_t e = c + lane;
+            const uint32_t v = e < a.E ? cnt[e] : 0u;
+            uint32_t ip = v, ii = v ? 1u : 0u;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t up = __shfl_up_sync(0xffffffffu, ip, o);
+                const uint32_t ui = __shfl_up_sync(0xffffffffu, ii, o);
+                if (lane >= (uint32_t)o) ip += up, ii += ui;
+            }
+            const uint32_t start = carry_p + ip - v, item = carry_i + ii - (v ? 1u : 0u);
+            if (e < a.E) {
+                cnt[e] = start; /* becomes the cursor */
+                item_of[e] = v ? item : UINT32_MAX;
+                if (v) {
+                    a.item_expert[item] = e;
+                    a.item_start[item] = start;
+                }
+            }
+            carry_p += __shfl_sync(0xffffffffu, ip, 31);
+            carry_i += __shfl_sync(0xffffffffu, ii, 31);
+        }
+        if (lane == 0) {
+            tot_pairs = carry_p;
+            tot_items = carry_i;
+        }
+    }
+    __syncthreads();
+    if (wid == 0) {
+        /* stable fill: entries in (token, slot) order, ranks via match_any */
+        for (uint32_t c = 0; c < n_routed; c += 32u) {
+            const uint32_t p = c + lane;
+            uint32_t e = UINT32_MAX;
+            if (p < n_routed) {
+                const uint32_t v = (uint32_t)__ldcg(a.sel + p);
+                if (v >= a.lo && v < a.hi) e = v;
+            }
+            const uint32_t peers = __match_any_sync(0xffffffffu, e);
+            const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+            if (e != UINT32_MAX) {
+                const uint32_t t = p / a.k, s = p % a.k;
+                a.pairs[cnt[e] + rank] = t * a.n_slot + s;
+            }
+            __syncwarp();
+            if (e != UINT32_MAX && rank == 0) cnt[e] += __popc(peers);
+            __syncwarp();
+        }
+    }
+    /* repack sel/w from k-wide to n_slot-wide rows (in place, backwards) */
+    __syncthreads();
+    if (a.S) {
+        if (threadIdx.x == 0) {
+            for (int32_t t = (int32_t)a.T - 1; t >= 0; t--) {
+                for (int32_t s = (int32_t)a.k - 1; s >= 0; s--) {
+                    a.sel[(uint32_t)t * a.n_slot + s] = __ldcg(a.sel + (uint32_t)t * a.k + s);
+                    a.w[(uint32_t)t * a.n_slot + s] = __ldcg(a.w + (uint32_t)t * a.k + s);
+                }
+                for (uint32_t s = 0; s < a.S; s++) {
+                    a.sel[(uint32_t)t * a.n_slot + a.k + s] = (int32_t)(a.E + s);
+                    a.w[(uint32_t)t * a.n_slot + a.k + s] = 1.0f;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    /* shared experts: computed on the shard that owns expert 0 */
+    const uint32_t n_sh = a.lo == 0 ? a.S : 0u;
+    for (uint32_t s = 0; s < n_sh; s++) {
+        const uint32_t item = tot_items + s, base = tot_pairs + s * a.T;
+        if (threadIdx.x == 0) {
+            a.item_expert[item] = a.E + s;
+            a.item_start[item] = base;
+        }
+        for (uint32_t t = threadIdx.x; t < a.T; t += blockDim.x) a.pairs[base + t] = t * a.n_slot + a.k + s;
+    }
+    if (threadIdx.x == 0) {
+        a.item_start[tot_items + n_sh] = tot_pairs + n_sh * a.T;
+        a.n_items[0] = tot_items + n_sh;
+        a.n_items[1] = tot_items;
+        *a.sel_done = 0;
+    }
+    for (uint32_t i = threadIdx.x; i < a.max_items * a.fb; i += blockDim.x) a.cnt[i] = 0;
+}
+
+/* ====================================================== 4: gate / up */
+
+struct pm_seg_lgu {
+    const uint8_t *g, *u;
+    uint32_t row0;
+    uint64_t rb;
+    uint32_t nrows, n_units;
+    const uint32_t *pairs;
+    uint32_t n;
+    const pm_layer_args *a;
+    const float *gb, *ub;
+    __device__ uint32_t count() const { return 1; }
+    __device__ const uint8_t *base(uint32_t, int m) const { return m == 0 ? g : u; }
+    __device__ uint32_t ntok(uint32_t) const { return n; }
+    __device__ const pm_block_q8K *tok(uint32_t, uint32_t ti) const {
+        return a->xq + (uint64_t)(pairs[ti] / a->n_slot) * a->hb;
+    }
+    __device__ void epi(uint32_t, uint32_t row, uint32_t ti, const float *v) const {
+        const uint32_t p = pairs[ti];
+        float x0 = v[0], x1 = v[1];
+        if (gb) x0 += gb[row0 + row];
+        if (ub) x1 += ub[row0 + row];
+        a->mid[(uint64_t)p * a->Fmax + row0 + row] = pm_glu(x0, x1, a->act) * a->w[p];
+    }
+    __device__ void skip(uint32_t, uint32_t, uint32_t) const {}
+};
+
+template <int Q>
+__device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t e, uint32_t row0,
+                                 uint32_t F, uint32_t S, uint32_t stage, uint32_t rc) {
+    const bool routed = e < a.E;
+    const uint64_t rb = routed ? a.rb_gu_r : a.rb_gu_s;
+    const uint8_t *gbase = routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate;
+    const uint8_t *ubase = routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup;
+    uint64_t *grid;
+    pm_ring ring = pm_ring_setup(smem, S, stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
+    pm_seg_lgu seg;
+    seg.g = gbase + (uint64_t)row0 * rb;
+    seg.u = ubase + (uint64_t)row0 * rb;
+    seg.row0 = row0;
+    seg.rb = rb;
+    seg.nrows = F - row0 < a.gu_rows ? F - row0 : a.gu_rows;
+    seg.n_units = Q == PM_QUANT_MXFP4 || Q == PM_QUANT_Q8_0 ? a.H / 32u : a.H / 32u;
+    const uint32_t s0 = a.item_start[item], s1 = a.item_start[item + 1];
+    seg.pairs = a.pairs + s0;
+    seg.n = s1 - s0;
+    seg.a = &a;
+    seg.gb = routed && a.gate_b ? a.gate_b + (uint64_t)e * a.Fr : nullptr;
+    seg.ub = routed && a.up_b ? a.up_b + (uint64_t)e * a.Fr : nullptr;
+    return pm_stream_segments<Q, 2>(seg, ring, rc, grid, a.err);
+}
+
+template <int QR, int QS>
+__global__ void __launch_bounds__(PM_THREADS)
+    pm_layer_gu_kernel(const __grid_constant__ pm_layer_args a, uint32_t S_r, uint32_t stage_r, uint32_t rc_r, uint32_t S_s,
+                       uint32_t stage_s, uint32_t rc_s) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint32_t last;
+    const uint32_t item = blockIdx.x;
+    if (item >= __ldcg(a.n_items)) return;
+    const uint32_t e = __ldcg(a.item_expert + item);
+    const bool routed = e < a.E;
+    const uint32_t F = routed ? a.Fr : a.Fs;
+    const uint32_t row0 = blockIdx.y * a.gu_rows;
+    if (row0 >= F) return;
+    const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, e, row0, F, S_r, stage_r, rc_r)
+                           : pm_layer_gu_item<QS>(a, smem, item, e, row0, F, S_s, stage_s, rc_s);
+    if (!ok) return;
+    /* the last tile of each 256-row block quantizes that block of mid */
+    const uint32_t fb = row0 / 256u;
+    const uint32_t blk_rows = F - fb * 256u < 256u ? F - fb * 256u : 256u;
+    const uint32_t tiles = (blk_rows + a.gu_rows - 1) / a.gu_rows;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(a.cnt + (uint64_t)item * a.fb + fb, 1u) == tiles - 1u;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
+    for (uint32_t i = s0 + (threadIdx.x >> 5); i < s1; i += PM_WARPS) {
+        const uint32_t p = __ldcg(a.pairs + i);
+        const float *src = a.mid + (uint64_t)p * a.Fmax + fb * 256u;
+        /* read through L2: other CTAs wrote these rows */
+        float tmp[8];
+        const uint32_t lane = threadIdx.x & 31u;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const uint32_t el = lane * 8u + q;
+            tmp[q] = el < blk_rows ? __ldcg(src + el) : 0.0f;
+        }
+        /* pm_q8k_warp reads src[lane*8 + q]; hand it the private copy */
+        float *stage_v = (float *)smem + (threadIdx.x >> 5) * 256u;
+#pragma unroll
+        for (int q = 0; q < 8; q++) stage_v[lane * 8u + q] = tmp[q];
+        __syncwarp();
+        pm_q8k_warp(stage_v, blk_rows, a.midq + (uint64_t)p * a.fb + fb);
+        __syncwarp();
+    }
+}
+
+/* ======================================================= 5: down */
+
+struct pm_seg_ldn {
+    const pm_layer_args *a;
+    uint32_t item0, row0;
+    uint64_t rb, stride;
+    const uint8_t *base0;
+    bool routed;
+    uint32_t nitems, nrows, n_units;
+    float *acc; /* [T][nrows_cta] */
+    uint32_t acc_ld;
+    __device__ uint32_t count() const { return nitems; }
+    __device__ const uint8_t *base(uint32_t sg, int) const {
+        const uint32_t e = __ldcg(a->item_expert + item0 + sg);
+        const uint8_t *b = routed ? base0 + (uint64_t)e * stride : base0;
+        return b + (uint64_t)row0 * rb;
+    }
+    __device__ uint32_t ntok(uint32_t sg) const {
+        return __ldcg(a->item_start + item0 + sg + 1) - __ldcg(a->item_start + item0 + sg);
+    }
+    __device__ const pm_block_q8K *tok(uint32_t sg, uint32_t ti) const {
+        const uint32_t p = __ldcg(a->pairs + __ldcg(a->item_start + item0 + sg) + ti);
+        return a->midq + (uint64_t)p * a->fb;
+    }
+    __device__ void epi(uint32_t sg, uint32_t row, uint32_t ti, const float *v) const {
+        const uint32_t p = __ldcg(a->pairs + __ldcg(a->item_start + item0 + sg) + ti);
+        acc[(p / a->n_slot) * acc_ld + row] += v[0];
+    }
+    __device__ void skip(uint32_t, uint32_t, uint32_t) const {}
+};
+
+template <int Q>
+__device__ bool pm_layer_dn_pass(const pm_layer_args &a, uint8_t *smem, bool routed, uint32_t item0,
+                                 uint32_t nitems, uint32_t row0, uint32_t nrows, float *acc, uint32_t S,
+                                 uint32_t stage, uint32_t rc) {
+    if (nitems == 0) return true;
+    uint64_t *grid;
+    pm_ring ring = pm_ring_setup(smem, S, stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
+    pm_seg_ldn seg;
+    seg.a = &a;
+    seg.item0 = item0;
+    seg.row0 = row0;
+    seg.routed = routed;
+    seg.rb = routed ? a.rb_dn_r : a.rb_dn_s;
+    seg.stride = a.st_dn_r;
+    seg.base0 = routed ? a.down : a.sdown;
+    seg.nitems = nitems;
+    seg.nrows = nrows;
+    seg.n_units = Q == PM_QUANT_MXFP4 || Q == PM_QUANT_Q8_0 ? ((routed ? a.Fr : a.Fs) + 31u) / 32u
+                                                            : (routed ? a.Fr : a.Fs) / 32u;
+    seg.acc = acc;
+    seg.acc_ld = a.dn_rows;
+    const bool ok = pm_stream_segments<Q, 1>(seg, ring, rc, grid, a.err);
+    pm_ring_teardown(ring);
+    return ok;
+}
+
+template <int QR, int QS>
+__global__ void __launch_bounds__(PM_THREADS)
+    pm_layer_dn_kernel(const __grid_constant__ pm_layer_args a, uint32_t S_r, uint32_t stage_r, uint32_t rc_r, uint32_t S_s,
+                       uint32_t stage_s, uint32_t rc_s, uint32_t ring_bytes) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t row0 = blockIdx.x * a.dn_rows;
+    const uint32_t nrows = a.H - row0 < a.dn_rows ? a.H - row0 : a.dn_rows;
+    float *acc = (float *)(smem + ring_bytes);
+    for (uint32_t i = threadIdx.x; i < a.T * a.dn_rows; i += blockDim.x) acc[i] = 0.0f;
+    __syncthreads();
+    const uint32_t n_all = __ldcg(a.n_items), n_r = __ldcg(a.n_items + 1);
+    if (!pm_layer_dn_pass<QR>(a, smem, true, 0, n_r, row0, nrows, acc, S_r, stage_r, rc_r)) return;
+    if (!pm_layer_dn_pass<QS>(a, smem, false, n_r, n_all - n_r, row0, nrows, acc, S_s, stage_s, rc_s)) return;
+    /* combine: + down bias of the routed slots (sum_s w_s b_s, cu:3601-3620) + residual */
+    for (uint32_t i = threadIdx.x; i < a.T * nrows; i += blockDim.x) {
+        const uint32_t t = i / nrows, j = i % nrows, r = row0 + j;
+        float v = acc[t * a.dn_rows + j];
+        if (a.down_b) {
+            float b = 0.0f;
+            for (uint32_t s = 0; s < a.k; s++) {
+                const uint32_t e = (uint32_t)a.sel[t * a.n_slot + s];
+                if (e >= a.lo && e < a.hi) b += a.w[t * a.n_slot + s] * a.down_b[(uint64_t)e * a.H + r];
+            }
+            if (b != 0.0f) v += b;
+        }
+        if (a.residual) v += a.residual[(uint64_t)t * a.H + r];
+        a.out[(uint64_t)t * a.H + r] = v;
+    }
+}
+
+/* ============================================================= host */
+
+struct pm_ring_geo {
+    uint32_t S, stage, rc, bytes;
+};
+
+static pm_ring_geo pm_ring_for(uint32_t nmat, uint64_t rb, uint32_t rows_cta, bool grid, uint32_t target) {
+    pm_ring_geo g;
+    uint64_t rc = target / (nmat * rb);
+    if (rc < 1) rc = 1;
+    if (rc > rows_cta) rc = rows_cta;
+    while (rows_cta % rc) rc--;
+    g.rc = (uint32_t)rc;
+    g.stage = pm_stage_bytes(nmat, rb, g.rc);
+    uint32_t S = 65536u / g.stage;
+    g.S = S < 2 ? 2 : (S > 8 ? 8 : S);
+    g.bytes = pm_ring_offset(grid) + g.S * g.stage;
+    return g;
+}
+
+static bool pm_fmt_ok(uint32_t q, uint32_t n) { return pm_row_bytes(q, n) != 0; }
+
+static int pm_desc_ok(const pulsar_moe_layer_desc *d) {
+    if (!d || !d->n_embd || !d->n_ff || !d->n_expert || !d->n_used || d->n_used > d->n_expert) return 0;
+    if (!d->gate || !d->up || !d->down || !d->router_w) return 0;
+    if (!pm_fmt_ok(d->quant, d->n_embd) || !pm_fmt_ok(d->quant, d->n_ff)) return 0;
+    if (d->row_bytes_gu < pm_row_bytes(d->quant, d->n_embd) || d->row_bytes_down < pm_row_bytes(d->quant, d->n_ff))
+        return 0;
+    if (d->n_shared > 1) return 0;
+    if (d->n_shared) {
+        if (!d->shared_gate || !d->shared_up || !d->shared_down || !d->shared_n_ff) return 0;
+        if (!pm_fmt_ok(d->shared_quant, d->n_embd) || !pm_fmt_ok(d->shared_quant, d->shared_n_ff)) return 0;
+        if (d->shared_row_bytes_gu < pm_row_bytes(d->shared_quant, d->n_embd) ||
+            d->shared_row_bytes_down < pm_row_bytes(d->shared_quant, d->shared_n_ff))
+            return 0;
+    }
+    if (d->router_mode > 1) return 0;
+    if (d->expert_hi && (d->expert_lo >= d->expert_hi || d->expert_hi > d->n_expert)) return 0;
+    return 1;
+}
+
+extern "C" size_t pulsar_moe_layer_workspace(const pulsar_moe_layer_desc *d, uint32_t max_tok) {
+    if (!pm_desc_ok(d) || max_tok == 0) return 0;
+    return pm_make_layout(d, max_tok).total;
+}
+
+extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t n_tok, void *ws,
+                                        pulsar_moe_ws_view *v) {
+    if (!pm_desc_ok(d) || !ws || !v || n_tok == 0) return 0;
+    const pm_layout L = pm_make_layout(d, n_tok);
+    uint8_t *b = (uint8_t *)ws;
+    v->logits = (float *)(b + L.logits);
+    v->selected = (int32_t *)(b + L.sel);
+    v->weights = (float *)(b + L.w);
+    v->xq = b + L.xq;
+    v->mid = (float *)(b + L.mid);
+    v->midq = b + L.midq;
+    v->err = (uint32_t *)(b + L.err);
+    v->n_slot = L.n_slot;
+    v->f_max = L.Fmax;
+    return 1;
+}
+
+static uint32_t pm_pow2_rows(uint64_t nrows_total, uint64_t ctas_other, uint32_t lo, uint32_t hi) {
+    /* largest power-of-two row count in [lo, hi] that still gives ~2 waves */
+    uint32_t r = hi;
+    while (r > lo && ((nrows_total + r - 1) / r) * ctas_other < 2ull * 148ull) r >>= 1;
+    return r;
+}
+
+template <int QR, int QS>
+static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st) {
+    static uint64_t done_gu = 0, done_dn = 0;
+    /* 4: gate/up */
+    const pm_ring_geo gr = pm_ring_for(2, a.rb_gu_r, a.gu_rows, QR == PM_QUANT_IQ2_XXS, 16384);
+    const pm_ring_geo gs = a.S ? pm_ring_for(2, a.rb_gu_s, a.gu_rows, QS == PM_QUANT_IQ2_XXS, 16384) : gr;
+    uint32_t smem_gu = gr.bytes > gs.bytes ? gr.bytes : gs.bytes;
+    if (smem_gu < PM_WARPS * 1024u) smem_gu = PM_WARPS * 1024u;
+    if (!pm_smem_attr(pm_layer_gu_kernel<QR, QS>, smem_gu, &done_gu)) return 0;
+    dim3 ggrid(L.max_items, (L.Fmax + a.gu_rows - 1) / a.gu_rows);
+    pm_layer_gu_kernel<QR, QS><<<ggrid, PM_THREADS, smem_gu, st>>>(a, gr.S, gr.stage, gr.rc, gs.S, gs.stage, gs.rc);
+    if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
+    /* 5: down + combine */
+    const pm_ring_geo dr = pm_ring_for(1, a.rb_dn_r, a.dn_rows, QR == PM_QUANT_IQ2_XXS, 8192);
+    const pm_ring_geo ds = a.S ? pm_ring_for(1, a.rb_dn_s, a.dn_rows, QS == PM_QUANT_IQ2_XXS, 8192) : dr;
+    const uint32_t ring = ((dr.bytes > ds.bytes ? dr.bytes : ds.bytes) + 15u) & ~15u;
+    const uint32_t smem_dn = ring + a.T * a.dn_rows * 4u;
+    if (!pm_smem_attr(pm_layer_dn_kernel<QR, QS>, smem_dn, &done_dn)) return 0;
+    pm_layer_dn_kernel<QR, QS><<<(a.H + a.dn_rows - 1) / a.dn_rows, PM_THREADS, smem_dn, st>>>(
+        a, dr.S, dr.stage, dr.rc, ds.S, ds.stage, ds.rc, ring);
+    return pm_ok(cudaGetLastError(), "moe layer down launch");
+}
+
+#define PM_Q2(QR)                                                                      \
+    switch (qs) {                                                                      \
+    case PM_QUANT_Q4_K: return pm_layer_launch<QR, PM_QUANT_Q4_K>(a, L, st);           \
+    case PM_QUANT_Q2_K: return pm_layer_launch<QR, PM_QUANT_Q2_K>(a, L, st);           \
+    case PM_QUANT_IQ2_XXS: return pm_layer_launch<QR, PM_QUANT_IQ2_XXS>(a, L, st);     \
+    case PM_QUANT_MXFP4: return pm_layer_launch<QR, PM_QUANT_MXFP4>(a, L, st);         \
+    case PM_QUANT_Q8_0: return pm_layer_launch<QR, PM_QUANT_Q8_0>(a, L, st);           \
+    default: return 0;                                                                 \
+    }
+
+static int pm_layer_dispatch(uint32_t qr, uint32_t qs, const pm_layer_args &a, const pm_layout &L, cudaStream_t st) {
+    switch (qr) {
+    case PM_QUANT_Q4_K: PM_Q2(PM_QUANT_Q4_K)
+    case PM_QUANT_Q2_K: PM_Q2(PM_QUANT_Q2_K)
+    case PM_QUANT_IQ2_XXS: PM_Q2(PM_QUANT_IQ2_XXS)
+    case PM_QUANT_MXFP4: PM_Q2(PM_QUANT_MXFP4)
+    case PM_QUANT_Q8_0: PM_Q2(PM_QUANT_Q8_0)
+    default: return 0;
+    }
+}
+
+extern "C" int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
+                                uint32_t n_tok, void *ws, size_t ws_bytes, void *stream) {
+    if (!pm_desc_ok(d) || !out || !x || !ws || n_tok == 0) return 0;
+    if (!pm_router_args_ok(d->n_expert, d->n_used, n_tok, d->router_mode, 0, d->n_group, d->topk_group)) return 0;
+    const pm_layout L = pm_make_layout(d, n_tok);
+    if (L.total > ws_bytes) return 0;
+    if ((uint64_t)n_tok * 64u * 4u > 160u * 1024u) return 0; /* down accumulator bound (decode path) */
+    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
+    uint8_t *b = (uint8_t *)ws;
+    pm_layer_args a;
+    memset(&a, 0, sizeof(a));
+    a.T = L.T, a.E = L.E, a.k = L.k, a.S = L.S, a.n_slot = L.n_slot, a.H = L.H, a.Fr = L.Fr, a.Fs = L.Fs;
+    a.Fmax = L.Fmax, a.hb = L.hb, a.fb = L.fb, a.max_items = L.max_items;
+    a.lo = d->expert_hi ? d->expert_lo : 0;
+    a.hi = d->expert_hi ? d->expert_hi : d->n_expert;
+    a.act = d->act_op, a.mode = d->router_mode, a.n_group = d->n_group, a.topk_group = d->topk_group;
+    a.scale = d->weight_scale;
+    a.rb_gu_r = d->row_bytes_gu, a.rb_dn_r = d->row_bytes_down;
+    a.st_gu_r = d->expert_stride_gu ? d->expert_stride_gu : (uint64_t)d->n_ff * d->row_bytes_gu;
+    a.st_dn_r = d->expert_stride_down ? d->expert_stride_down : (uint64_t)d->n_embd * d->row_bytes_down;
+    a.rb_gu_s = d->shared_row_bytes_gu, a.rb_dn_s = d->shared_row_bytes_down;
+    a.gate = (const uint8_t *)d->gate, a.up = (const uint8_t *)d->up, a.down = (const uint8_t *)d->down;
+    a.sgate = (const uint8_t *)d->shared_gate, a.sup = (const uint8_t *)d->shared_up;
+    a.sdown = (const uint8_t *)d->shared_down;
+    a.gate_b = d->gate_b, a.up_b = d->up_b, a.down_b = d->down_b, a.router_sel_b = d->router_select_b;
+    a.logits = (float *)(b + L.logits);
+    a.sel = (int32_t *)(b + L.sel);
+    a.w = (float *)(b + L.w);
+    a.xq = (pm_block_q8K *)(b + L.xq);
+    a.n_items = (uint32_t *)(b + L.n_items);
+    a.item_expert = (uint32_t *)(b + L.item_expert);
+    a.item_start = (uint32_t *)(b + L.item_start);
+    a.pairs = (uint32_t *)(b + L.pairs);
+    a.mid = (float *)(b + L.mid);
+    a.midq = (pm_block_q8K *)(b + L.midq);
+    a.cnt = (uint32_t *)(b + L.cnt);
+    a.sel_done = (uint32_t *)(b + L.sel_done);
+    a.err = (uint32_t *)(b + L.err);
+    a.out = out;
+    a.residual = residual;
+    const uint64_t items_est = L.max_items;
+    a.gu_rows = pm_pow2_rows(L.Fmax, items_est, 8, 64);
+    a.dn_rows = pm_pow2_rows(L.H, 1, 8, 64);
+    while (a.dn_rows > 8 && (uint64_t)a.T * a.dn_rows * 4u > 64u * 1024u) a.dn_rows >>= 1;
+
+    /* 1, 2: logits and q8_K(x) */
+    if (!pm_launch_router_logits(a.logits, d->router_w, x, d->router_logit_b, L.E, L.H, L.T, st)) return 0;
+    if (!pm_launch_q8k(a.xq, x, L.H, L.T, st)) return 0;
+    /* 3: select + CSR */
+    uint32_t smem_sel = 4u * 2u * L.E * 4u;
+    if (smem_sel < 2u * L.E * 4u) smem_sel = 2u * L.E * 4u;
+    static uint64_t done_sel = 0;
+    if (!pm_smem_attr(pm_layer_select_kernel, smem_sel, &done_sel)) return 0;
+    pm_layer_select_kernel<<<(L.T + 3u) / 4u, 128, smem_sel, st>>>(a);
+    if (!pm_ok(cudaGetLastError(), "moe layer select launch")) return 0;
+    return pm_layer_dispatch(d->quant, d->n_shared ? d->shared_quant : d->quant, a, L, st);
+}

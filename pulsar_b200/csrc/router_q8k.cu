@@ -1,0 +1,189 @@
+/* router_q8k.cu - q8_K activation quantizer and the router (logits, top-k
+ * selection, route weights) on sm_100a.
+ *
+ * Both are bit-exact with the CPU restatement of the reference:
+ *  - q8_K follows the CPU lane's quantize_row_q8_k
+ *    (crates/quant/src/cpu_dot.rs:26-50: d = amax/127, q = round half away
+ *    from zero of x*127/amax, clamp +-127), not the reference GPU
+ *    quantizer (cu:1498, signed-max iscale with rint), because the CPU
+ *    lane's bytes are the parity target.  Layout: the reference's
+ *    292-byte block_q8_K (cu:1492), tail elements beyond in_dim zero.
+ *  - logits are a binary64 dot in a fixed order (32 lane partials over
+ *    i = 128 j + 4 lane + c, then an xor butterfly), rounded once to f32;
+ *    selection scores use pm_expf, so top-k indices and route weights
+ *    reproduce exactly on the host.
+ */
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "pm_host.h"
+#include "pm_device.cuh"
+
+/* ------------------------------------------------------------- q8_K */
+
+/* one warp per 256-value block */
+__global__ void pm_q8k_kernel(pm_block_q8K *out, const float *x, uint32_t in_dim, uint32_t n_rows) {
+    const uint32_t nb = (in_dim + 255u) / 256u;
+    const uint64_t gw = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= (uint64_t)nb * n_rows) return;
+    const uint64_t row = gw / nb;
+    const uint32_t b = (uint32_t)(gw % nb);
+    const uint32_t bn = in_dim - b * 256u < 256u ? in_dim - b * 256u : 256u;
+    pm_q8k_warp(x + row * in_dim + (uint64_t)b * 256u, bn, out + gw);
+}
+
+int pm_launch_q8k(void *out, const float *x, uint32_t in_dim, uint32_t n_rows, cudaStream_t st) {
+    const uint64_t warps = (uint64_t)((in_dim + 255u) / 256u) * n_rows;
+    const uint32_t blocks = (uint32_t)((warps * 32 + 255) / 256);
+    pm_q8k_kernel<<<blocks, 256, 0, st>>>((pm_block_q8K *)out, x, in_dim, n_rows);
+    return pm_ok(cudaGetLastError(), "q8_K quantize launch");
+}
+
+/* cu:1552 pulsar_quantize_q8_K */
+extern "C" int pulsar_quantize_q8_K(void *out_dev, const void *x_dev, uint32_t in_dim, uint32_t n_rows) {
+    if (!out_dev || !x_dev || in_dim == 0 || n_rows == 0) return 0;
+    return pm_launch_q8k(out_dev, (const float *)x_dev, in_dim, n_rows, cudaStreamPerThread);
+}
+
+/* ----------------------------------------------------------- logits */
+
+/* warp per (expert, token group of 4): binary64 partials in the fixed
+ * order, xor butterfly, one rounding.  W rows may be any length; the
+ * float4 path needs in_dim % 4 == 0 (16-byte aligned rows). */
+#define PM_RT_TOK 4
+__global__ void pm_router_logits_kernel(float *logits, const float *w, const float *x, const float *lbias,
+                                        uint32_t n_expert, uint32_t in_dim, uint32_t n_tok) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const uint32_t t0 = blockIdx.y * PM_RT_TOK;
+    if (e >= n_expert) return;
+    const float *wr = w + (uint64_t)e * in_dim;
+    double p[PM_RT_TOK];
+#pragma unroll
+    for (int t = 0; t < PM_RT_TOK; t++) p[t] = 0.0;
+    const uint32_t nj = (in_dim + 127u) / 128u;
+    const bool vec = (in_dim & 3u) == 0;
+    for (uint32_t j = 0; j < nj; j++) {
+        const uint32_t i0 = 128u * j + 4u * lane;
+        float wv[4];
+        if (vec && i0 + 3 < in_dim) {
+            const float4 q = __ldg((const float4 *)(wr + i0));
+            wv[0] = q.x, wv[1] = q.y, wv[2] = q.z, wv[3] = q.w;
+        } else {
+#pragma unroll
+            for (int c = 0; c < 4; c++) wv[c] = i0 + c < in_dim ? wr[i0 + c] : 0.0f;
+        }
+#pragma unroll
+        for (int t = 0; t < PM_RT_TOK; t++) {
+            if (t0 + t >= n_tok) break;
+            const float *xr = x + (uint64_t)(t0 + t) * in_dim;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                if (i0 + c < in_dim) p[t] = fma((double)wv[c], (double)__ldg(xr + i0 + c), p[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < PM_RT_TOK; t++) {
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) p[t] = p[t] + __shfl_xor_sync(0xffffffffu, p[t], m);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < PM_RT_TOK; t++) {
+            if (t0 + t >= n_tok) break;
+            float l = __double2float_rn(p[t]);
+            if (lbias) l = __fadd_rn(l, lbias[e]);
+            logits[(uint64_t)(t0 + t) * n_expert + e] = l;
+        }
+    }
+}
+
+int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
+                            uint32_t in_dim, uint32_t n_tok, cudaStream_t st) {
+    dim3 grid((n_expert + 3u) / 4u, (n_tok + PM_RT_TOK - 1) / PM_RT_TOK);
+    pm_router_logits_kernel<<<grid, 128, 0, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok);
+    return pm_ok(cudaGetLastError(), "router logits launch");
+}
+
+/* cu:6526 pulsar_matmul_f32: out[t][r] = W[r] . x[t], here in the fixed
+ * binary64 order above (deterministic; equal to the f32 dot within f32
+ * rounding) */
+extern "C" int pulsar_matmul_f32(void *out_dev, const void *w_dev, const void *x_dev, uint32_t in_dim,
+                                 uint32_t out_dim, uint32_t n_tok) {
+    if (!out_dev || !w_dev || !x_dev || in_dim == 0 || out_dim == 0 || n_tok == 0) return 0;
+    return pm_launch_router_logits((float *)out_dev, (const float *)w_dev, (const float *)x_dev, nullptr, out_dim,
+                                   in_dim, n_tok, cudaStreamPerThread);
+}
+
+#include "pm_router.cuh"
+
+/* one warp per token; scores and probabilities staged in shared memory
+ * (4 warps x 2 x n_expert floats) */
+__global__ void pm_router_select_kernel(int32_t *selected, float *weights, const float *logits, const float *bias,
+                                        uint32_t n_expert, uint32_t k_used, float weight_scale, uint32_t n_tok,
+                                        uint32_t mode, uint32_t n_shexp, uint32_t n_group, uint32_t topk_group) {
+    extern __shared__ float rs[];
+    const uint32_t wid = threadIdx.x >> 5;
+    const uint32_t token = blockIdx.x * (blockDim.x >> 5) + wid;
+    if (token >= n_tok) return;
+    float *score = rs + (size_t)wid * 2 * n_expert;
+    pm_select_token(selected, weights, logits, bias, n_expert, k_used, weight_scale, token, mode, n_shexp, n_group,
+                    topk_group, score, score + n_expert);
+}
+
+int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32_t mode, uint32_t n_shexp,
+                      uint32_t n_group, uint32_t topk_group) {
+    if (n_expert == 0 || k_used == 0 || k_used > n_expert || n_tok == 0 || mode > 2u) return 0;
+    if (mode != 2u && n_shexp != 0) return 0;
+    if (n_expert + (mode == 2u ? n_shexp : 0u) > 4096u) return 0;
+    if (n_group > 1u) {
+        if (n_group > 32u || n_expert % n_group || topk_group == 0 || topk_group > n_group || mode == 2u) return 0;
+        if (n_expert / n_group < 2u) return 0;
+        if ((uint64_t)(n_expert / n_group) * topk_group < k_used) return 0;
+    }
+    return 1;
+}
+
+int pm_launch_router_select(int32_t *sel, float *w, const float *logits, const float *bias, uint32_t n_expert,
+                            uint32_t k_used, float scale, uint32_t n_tok, uint32_t mode, uint32_t n_shexp,
+                            uint32_t n_group, uint32_t topk_group, cudaStream_t st) {
+    const uint32_t smem = 4u * 2u * n_expert * 4u;
+    static uint64_t done = 0;
+    if (!pm_smem_attr(pm_router_select_kernel, smem, &done)) return 0;
+    pm_router_select_kernel<<<(n_tok + 3u) / 4u, 128, smem, st>>>(sel, w, logits, bias, n_expert, k_used, scale,
+                                                                  n_tok, mode, n_shexp, n_group, topk_group);
+    return pm_ok(cudaGetLastError(), "router select launch");
+}
+
+/* cu:1052 pulsar_router_select (modes 0/1/2; n_expert up to 4096) */
+extern "C" int pulsar_router_select(void *selected_dev, void *weights_dev, const void *logits_dev,
+                                    const void *bias_dev, uint32_t n_expert, uint32_t k_used, float weight_scale,
+                                    uint32_t n_tok, uint32_t softmax_mode, uint32_t n_shexp) {
+    if (!selected_dev || !weights_dev || !logits_dev ||
+        !pm_router_args_ok(n_expert, k_used, n_tok, softmax_mode, n_shexp, 0, 0))
+        return 0;
+    return pm_launch_router_select((int32_t *)selected_dev, (float *)weights_dev, (const float *)logits_dev,
+                                   (const float *)bias_dev, n_expert, k_used, weight_scale, n_tok, softmax_mode,
+                                   n_shexp, 0, 0, cudaStreamPerThread);
+}
+
+/* New entry point: logits + optional logit bias + group-limited top-k in
+ * one call (router GEMV fused with selection).  No reference counterpart
+ * as one call; equals pulsar_matmul_f32 + pulsar_add_bias_rows +
+ * pulsar_router_select when n_group <= 1. */
+extern "C" int pulsar_router_logits_select(void *selected_dev, void *weights_dev, void *logits_dev,
+                                           const void *x_dev, const void *w_dev, const void *logit_bias_dev,
+                                           const void *select_bias_dev, uint32_t in_dim, uint32_t n_expert,
+                                           uint32_t k_used, float weight_scale, uint32_t n_tok, uint32_t mode,
+                                           uint32_t n_group, uint32_t topk_group, void *stream) {
+    if (!selected_dev || !weights_dev || !logits_dev || !x_dev || !w_dev || in_dim == 0 || mode == 2u ||
+        !pm_router_args_ok(n_expert, k_used, n_tok, mode, 0, n_group, topk_group))
+        return 0;
+    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
+    return pm_launch_router_logits((float *)logits_dev, (const float *)w_dev, (const float *)x_dev,
+                                   (const float *)logit_bias_dev, n_expert, in_dim, n_tok, st) &&
+           pm_launch_router_select((int32_t *)selected_dev, (float *)weights_dev, (const float *)logits_dev,
+                                   (const float *)select_bias_dev, n_expert, k_used, weight_scale, n_tok, mode, 0,
+                                   n_group, topk_group, st);
+}

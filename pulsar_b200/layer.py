@@ -1,0 +1,205 @@
+"""MoE layers on the device: weights, descriptor, the one-call forward.
+
+MoeLayer holds one routed-expert FFN layer the way the reference engine
+holds it (expert slabs per tensor, slab e at base + e * rows * row_bytes,
+crates/engine/src/lib.rs:576-592; router weight as f32, elib:2884-2921),
+builds the pulsar_moe_layer_desc and runs the layer through
+pulsar_moe_layer (router -> q8_K -> gate/up + glu -> q8_K -> down ->
+combine, all on the GPU).  make_layer() creates seeded synthetic layers:
+f32 N(0, std) weights generated on the device and quantized with the GPU
+block encoders (byte-identical to the crates/quant encoders).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from ._lib import LayerDesc, WsView, check, lib, ptr, row_bytes
+from .ops import quantize_rows
+
+SLAB_SLACK = 256  # tail slack after every slab (crates/engine/src/lib.rs:594-600)
+
+
+@dataclass
+class LayerSpec:
+    n_embd: int
+    n_ff: int
+    n_expert: int
+    n_used: int
+    quant: int
+    act_op: int = 0
+    router_mode: int = 1          # 0 sigmoid + selection bias, 1 softmax
+    n_group: int = 0
+    topk_group: int = 0
+    weight_scale: float = 1.0
+    zipf_s: float = 0.0           # router bias skew (0 = none)
+    zipf_kind: str = "logit"      # "logit" (added to logits) or "select" (selection score only)
+    shared_quant: int | None = None
+    shared_n_ff: int = 0
+    biases: bool = False          # per-expert gate/up/down biases + router logit bias
+    weight_std: float = 0.02
+    bias_std: float = 0.01
+
+
+@dataclass
+class MoeLayer:
+    spec: LayerSpec
+    gate: torch.Tensor
+    up: torch.Tensor
+    down: torch.Tensor
+    router_w: torch.Tensor
+    router_logit_b: torch.Tensor | None = None
+    router_select_b: torch.Tensor | None = None
+    gate_b: torch.Tensor | None = None
+    up_b: torch.Tensor | None = None
+    down_b: torch.Tensor | None = None
+    shared_gate: torch.Tensor | None = None
+    shared_up: torch.Tensor | None = None
+    shared_down: torch.Tensor | None = None
+    expert_lo: int = 0
+    expert_hi: int = 0
+    _desc: LayerDesc | None = field(default=None, repr=False)
+
+    # ---------------------------------------------------------- geometry
+    @property
+    def rb_gu(self) -> int:
+        return row_bytes(self.spec.quant, self.spec.n_embd)
+
+    @property
+    def rb_down(self) -> int:
+        return row_bytes(self.spec.quant, self.spec.n_ff)
+
+    def weight_bytes_per_expert(self) -> int:
+        s = self.spec
+        return 2 * s.n_ff * self.rb_gu + s.n_embd * self.rb_down
+
+    def shared_bytes(self) -> int:
+        s = self.spec
+        if s.shared_quant is None:
+            return 0
+        return (2 * s.shared_n_ff * row_bytes(s.shared_quant, s.n_embd)
+                + s.n_embd * row_bytes(s.shared_quant, s.shared_n_ff))
+
+    # -------------------------------------------------------------- desc
+    def desc(self) -> LayerDesc:
+        if self._desc is not None:
+            return self._desc
+        s = self.spec
+        d = LayerDesc()
+        d.n_embd, d.n_ff, d.n_expert, d.n_used = s.n_embd, s.n_ff, s.n_expert, s.n_used
+        d.quant, d.act_op, d.router_mode = s.quant, s.act_op, s.router_mode
+        d.n_group, d.topk_group, d.weight_scale = s.n_group, s.topk_group, s.weight_scale
+        d.row_bytes_gu, d.row_bytes_down = self.rb_gu, self.rb_down
+        d.expert_stride_gu = s.n_ff * self.rb_gu
+        d.expert_stride_down = s.n_embd * self.rb_down
+        d.gate, d.up, d.down = ptr(self.gate), ptr(self.up), ptr(self.down)
+        d.gate_b, d.up_b, d.down_b = ptr(self.gate_b), ptr(self.up_b), ptr(self.down_b)
+        d.router_w = ptr(self.router_w)
+        d.router_logit_b, d.router_select_b = ptr(self.router_logit_b), ptr(self.router_select_b)
+        if s.shared_quant is not None:
+            d.n_shared, d.shared_quant, d.shared_n_ff = 1, s.shared_quant, s.shared_n_ff
+            d.shared_row_bytes_gu = row_bytes(s.shared_quant, s.n_embd)
+            d.shared_row_bytes_down = row_bytes(s.shared_quant, s.shared_n_ff)
+            d.shared_gate, d.shared_up, d.shared_down = ptr(self.shared_gate), ptr(self.shared_up), ptr(self.shared_down)
+        d.expert_lo, d.expert_hi = self.expert_lo, self.expert_hi
+        self._desc = d
+        return d
+
+    def workspace_bytes(self, max_tok: int) -> int:
+        n = int(lib().pulsar_moe_layer_workspace(ctypes.byref(self.desc()), max_tok))
+        if n == 0:
+            raise ValueError("layer descriptor rejected by pulsar_moe_layer_workspace")
+        return n
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor, residual: torch.Tensor | None = None,
+                stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """out = residual + moe(x) (or moe(x)); x, out f32 [T][H] on the device."""
+        T = x.shape[0]
+        st = torch.cuda.current_stream() if stream is None else stream
+        check(lib().pulsar_moe_layer(ctypes.byref(self.desc()), ptr(out), ptr(x), ptr(residual), T, ptr(ws),
+                                     ws.numel(), st.cuda_stream), "moe_layer")
+        return out
+
+    def ws_view(self, ws: torch.Tensor, n_tok: int) -> WsView:
+        v = WsView()
+        check(lib().pulsar_moe_layer_ws_view(ctypes.byref(self.desc()), n_tok, ptr(ws), ctypes.byref(v)), "ws_view")
+        return v
+
+    def expert_rows(self, e: int):
+        """(gate, up, down) byte views of expert e (device tensors)."""
+        s = self.spec
+        g = self.gate[e * s.n_ff * self.rb_gu:(e + 1) * s.n_ff * self.rb_gu]
+        u = self.up[e * s.n_ff * self.rb_gu:(e + 1) * s.n_ff * self.rb_gu]
+        d = self.down[e * s.n_embd * self.rb_down:(e + 1) * s.n_embd * self.rb_down]
+        return g, u, d
+
+
+# ------------------------------------------------------------------ builders
+
+def zipf_bias(n_expert: int, s: float, kind: str, seed: int) -> torch.Tensor:
+    """Zipf(s) expert skew: a seeded permutation gives each expert a rank
+    r = 1..E; selection-score bias r^-s (sigmoid routers) or logit bias
+    -s ln r (softmax routers)."""
+    g = torch.Generator().manual_seed(seed)
+    rank = torch.randperm(n_expert, generator=g).to(torch.float64) + 1.0
+    if kind == "select":
+        return rank.pow(-s).to(torch.float32)
+    return (-s * torch.log(rank)).to(torch.float32)
+
+
+def _quantized(rows: int, n: int, quant: int, std: float, gen: torch.Generator, device, chunk_rows: int = 1 << 16,
+               qw: torch.Tensor | None = None) -> torch.Tensor:
+    """rows x n f32 N(0, std) generated on the device, encoded to `quant`."""
+    rb = row_bytes(quant, n)
+    out = torch.empty(rows * rb + SLAB_SLACK, dtype=torch.uint8, device=device)
+    out[rows * rb:].zero_()
+    for r0 in range(0, rows, chunk_rows):
+        r1 = min(rows, r0 + chunk_rows)
+        x = torch.randn((r1 - r0, n), generator=gen, device=device, dtype=torch.float32) * std
+        quantize_rows(out[r0 * rb:r1 * rb], x.contiguous(), quant, qw=qw)
+    return out
+
+
+def make_layer(spec: LayerSpec, seed: int, device="cuda") -> MoeLayer:
+    """Seeded synthetic layer: every tensor from its own generator stream."""
+    dev = torch.device(device)
+    s = spec
+
+    def gen(k: int) -> torch.Generator:
+        return torch.Generator(device=dev).manual_seed(seed * 1000 + k)
+
+    qw = torch.ones(s.n_embd, device=dev) if s.quant == 1 else None
+    qw_f = torch.ones(s.n_ff, device=dev) if s.quant == 1 else None
+    gate = _quantized(s.n_expert * s.n_ff, s.n_embd, s.quant, s.weight_std, gen(1), dev, qw=qw)
+    up = _quantized(s.n_expert * s.n_ff, s.n_embd, s.quant, s.weight_std, gen(2), dev, qw=qw)
+    down = _quantized(s.n_expert * s.n_embd, s.n_ff, s.quant, s.weight_std, gen(3), dev, qw=qw_f)
+    router_w = torch.randn((s.n_expert, s.n_embd), generator=gen(4), device=dev) * s.weight_std
+    layer = MoeLayer(spec=s, gate=gate, up=up, down=down, router_w=router_w.contiguous())
+    if s.zipf_s > 0:
+        b = zipf_bias(s.n_expert, s.zipf_s, s.zipf_kind, seed).to(dev)
+        if s.zipf_kind == "select":
+            layer.router_select_b = b
+        else:
+            layer.router_logit_b = b
+    if s.biases:
+        layer.gate_b = (torch.randn((s.n_expert, s.n_ff), generator=gen(5), device=dev) * s.bias_std).contiguous()
+        layer.up_b = (torch.randn((s.n_expert, s.n_ff), generator=gen(6), device=dev) * s.bias_std).contiguous()
+        layer.down_b = (torch.randn((s.n_expert, s.n_embd), generator=gen(7), device=dev) * s.bias_std).contiguous()
+        rb = torch.randn((s.n_expert,), generator=gen(8), device=dev) * s.bias_std
+        layer.router_logit_b = rb if layer.router_logit_b is None else (layer.router_logit_b + rb).contiguous()
+    if s.shared_quant is not None:
+        sq = s.shared_quant
+        qs = torch.ones(s.n_embd, device=dev) if sq == 1 else None
+        qsf = torch.ones(s.shared_n_ff, device=dev) if sq == 1 else None
+        layer.shared_gate = _quantized(s.shared_n_ff, s.n_embd, sq, s.weight_std, gen(9), dev, qw=qs)
+        layer.shared_up = _quantized(s.shared_n_ff, s.n_embd, sq, s.weight_std, gen(10), dev, qw=qs)
+        layer.shared_down = _quantized(s.n_embd, s.shared_n_ff, sq, s.weight_std, gen(11), dev, qw=qsf)
+    return layer
+
+
+def seeded_hidden(n_tok: int, n_embd: int, seed: int, device="cuda") -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randn((n_tok, n_embd), generator=g, device=device, dtype=torch.float32)
