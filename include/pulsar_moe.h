@@ -187,8 +187,16 @@ typedef struct pulsar_moe_ws_view {
     float *mid;           /* [n_tok * n_slot][F_max] */
     void *midq;           /* q8_K [n_tok * n_slot][ceil(F_max/256)] */
     uint32_t *err;        /* error word: bit 0 wait timeout */
+    uint32_t *n_items;    /* [0] expert work items, [1] routed ones (distinct experts) */
     uint32_t n_slot, f_max;
 } pulsar_moe_ws_view;
+/* pulsar_moe_layer that also records events[0..5] (cudaEvent_t, NULL
+ * entries skipped) around its kernels: before the router, after the
+ * logits, after q8_K(x), after selection, after gate/up, after down and
+ * combine.  For per-kernel timing; otherwise identical to pulsar_moe_layer. */
+int pulsar_moe_layer_profiled(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
+                              uint32_t n_tok, void *ws, size_t ws_bytes, void *stream, void *const *events);
+
 int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t max_tok, void *ws, pulsar_moe_ws_view *v);
 
 /* GPU block encoders (crates/quant/src/lib.rs:251 q8_0, :271 q2_K,

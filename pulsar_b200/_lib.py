@@ -59,7 +59,8 @@ class LayerDesc(ctypes.Structure):
 class WsView(ctypes.Structure):
     _fields_ = [("logits", ctypes.c_void_p), ("selected", ctypes.c_void_p), ("weights", ctypes.c_void_p),
                 ("xq", ctypes.c_void_p), ("mid", ctypes.c_void_p), ("midq", ctypes.c_void_p),
-                ("err", ctypes.c_void_p), ("n_slot", ctypes.c_uint32), ("f_max", ctypes.c_uint32)]
+                ("err", ctypes.c_void_p), ("n_items", ctypes.c_void_p), ("n_slot", ctypes.c_uint32),
+                ("f_max", ctypes.c_uint32)]
 
 
 # (name, argtypes) of every C entry point, in header order
@@ -79,6 +80,8 @@ _SIGS = {
     "pulsar_add": [_P, _P, _P, _U32],
     "pulsar_router_logits_select": [_P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32, _U32, _U32, _P],
     "pulsar_moe_layer": [ctypes.POINTER(LayerDesc), _P, _P, _P, _U32, _P, ctypes.c_size_t, _P],
+    "pulsar_moe_layer_profiled": [ctypes.POINTER(LayerDesc), _P, _P, _P, _U32, _P, ctypes.c_size_t, _P,
+                                  ctypes.POINTER(ctypes.c_void_p)],
     "pulsar_moe_layer_ws_view": [ctypes.POINTER(LayerDesc), _U32, _P, ctypes.POINTER(WsView)],
     "pulsar_quantize_rows": [_P, _P, _P, _U32, _U64, _U32, _P],
 }
@@ -86,10 +89,10 @@ _SIGS = {
 
 def build(force: bool = False) -> str:
     """Compile the CUDA library for sm_100a in-tree (nvcc; no GPU needed)."""
-    if force or not os.path.exists(LIB_PATH):
-        subprocess.run(["make", "-s", "-j8", "-C", os.path.join(_HERE, "csrc")], check=True)
-    else:
-        subprocess.run(["make", "-s", "-j8", "-C", os.path.join(_HERE, "csrc")], check=True)
+    csrc = os.path.join(_HERE, "csrc")
+    if force:
+        subprocess.run(["make", "-s", "-C", csrc, "clean"], check=True)
+    subprocess.run(["make", "-s", "-j8", "-C", csrc], check=True)
     return LIB_PATH
 
 

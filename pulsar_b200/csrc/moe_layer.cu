@@ -15,10 +15,12 @@
  *     expert's rows once through a TMA ring and serves every token routed
  *     to it; glu * route weight -> mid.  The last tile CTA of each 256-row
  *     block quantizes that block of every pair's mid row to q8_K.
- *   5 down + combine: one CTA per tile of output rows walks all work
- *     items in order, streams each expert's rows once, accumulates per
- *     (token, row) in shared memory (fixed order -> deterministic), then
- *     adds the down bias (sum_s w_s b_s, cu:3601) and the residual.
+ *   5 down: one CTA per (expert work item, tile of output rows), the same
+ *     engine, writing one partial row per (token, slot)
+ *   6 combine: per (token, row) the partials in slot order, + the down
+ *     bias (sum_s w_s b_s, cu:3601) + the residual (deterministic)
+ * Both expert kernels stage each token tile's q8_K rows in shared memory
+ * and decode every weight unit once for the whole tile (pm_gemv.cuh).
  *
  * Nothing is allocated; all state lives in the caller's workspace and the
  * call is capturable into a CUDA graph.
@@ -30,7 +32,7 @@
 #include "../../include/pulsar_moe.h"
 #include "pm_host.h"
 #include "pm_router.cuh"
-#include "pm_stream.cuh"
+#include "pm_gemv.cuh"
 
 int pm_launch_q8k(void *out, const float *x, uint32_t in_dim, uint32_t n_rows, cudaStream_t st);
 int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
@@ -44,7 +46,7 @@ __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
-    size_t logits, sel, w, xq, n_items, item_expert, item_start, pairs, mid, midq, cnt, sel_done, err, total;
+    size_t logits, sel, w, xq, n_items, item_expert, item_start, pairs, mid, midq, partial, cnt, sel_done, err, total;
 };
 
 static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -75,6 +77,7 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
     L.midq = o, o = pm_al(o + (size_t)T * L.n_slot * L.fb * PM_Q8_K_BYTES);
+    L.partial = o, o = pm_al(o + (size_t)T * L.n_slot * L.H * 4);
     L.cnt = o, o = pm_al(o + (size_t)L.max_items * L.fb * 4);
     L.sel_done = o, o = pm_al(o + 4);
     L.err = o, o = pm_al(o + 4);
@@ -100,6 +103,7 @@ struct pm_layer_args {
     uint32_t *item_expert, *item_start, *pairs;
     float *mid;
     pm_block_q8K *midq;
+    float *partial; /* [T * n_slot][H] down outputs before the combine */
     uint32_t *cnt, *sel_done, *err;
     /* io */
     float *out;
@@ -230,60 +234,58 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
 
 /* ====================================================== 4: gate / up */
 
-struct pm_seg_lgu {
+#define PM_TT 8 /* tokens per register tile */
+
+struct pm_seg_gu2 {
     const uint8_t *g, *u;
-    uint32_t row0;
-    uint64_t rb;
-    uint32_t nrows, n_units;
     const uint32_t *pairs;
-    uint32_t n;
+    uint32_t n, row0;
     const pm_layer_args *a;
     const float *gb, *ub;
-    __device__ uint32_t count() const { return 1; }
-    __device__ const uint8_t *base(uint32_t, int m) const { return m == 0 ? g : u; }
-    __device__ uint32_t ntok(uint32_t) const { return n; }
-    __device__ const pm_block_q8K *tok(uint32_t, uint32_t ti) const {
-        return a->xq + (uint64_t)(pairs[ti] / a->n_slot) * a->hb;
+    __device__ const uint8_t *base(int m) const { return m == 0 ? g : u; }
+    __device__ uint32_t ntok() const { return n; }
+    __device__ const pm_block_q8K *tok(uint32_t ti) const {
+        return a->xq + (uint64_t)(__ldcg(pairs + ti) / a->n_slot) * a->hb;
     }
-    __device__ void epi(uint32_t, uint32_t row, uint32_t ti, const float *v) const {
-        const uint32_t p = pairs[ti];
+    __device__ void epi(uint32_t row, uint32_t ti, const float *v) const {
+        const uint32_t p = __ldcg(pairs + ti);
         float x0 = v[0], x1 = v[1];
         if (gb) x0 += gb[row0 + row];
         if (ub) x1 += ub[row0 + row];
         a->mid[(uint64_t)p * a->Fmax + row0 + row] = pm_glu(x0, x1, a->act) * a->w[p];
     }
-    __device__ void skip(uint32_t, uint32_t, uint32_t) const {}
+};
+
+/* geometry of one engine pass, computed on the host */
+struct pm_pass {
+    uint32_t S, stage, rc, lpr, ring_bytes, act_off;
 };
 
 template <int Q>
 __device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t e, uint32_t row0,
-                                 uint32_t F, uint32_t S, uint32_t stage, uint32_t rc) {
+                                 uint32_t nrows, const pm_pass &ps) {
     const bool routed = e < a.E;
     const uint64_t rb = routed ? a.rb_gu_r : a.rb_gu_s;
-    const uint8_t *gbase = routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate;
-    const uint8_t *ubase = routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup;
     uint64_t *grid;
-    pm_ring ring = pm_ring_setup(smem, S, stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
-    pm_seg_lgu seg;
-    seg.g = gbase + (uint64_t)row0 * rb;
-    seg.u = ubase + (uint64_t)row0 * rb;
-    seg.row0 = row0;
-    seg.rb = rb;
-    seg.nrows = F - row0 < a.gu_rows ? F - row0 : a.gu_rows;
-    seg.n_units = Q == PM_QUANT_MXFP4 || Q == PM_QUANT_Q8_0 ? a.H / 32u : a.H / 32u;
-    const uint32_t s0 = a.item_start[item], s1 = a.item_start[item + 1];
+    pm_ring ring = pm_ring_setup(smem, ps.S, ps.stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
+    pm_seg_gu2 seg;
+    seg.g = (routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate) + (uint64_t)row0 * rb;
+    seg.u = (routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup) + (uint64_t)row0 * rb;
+    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
     seg.pairs = a.pairs + s0;
     seg.n = s1 - s0;
+    seg.row0 = row0;
     seg.a = &a;
     seg.gb = routed && a.gate_b ? a.gate_b + (uint64_t)e * a.Fr : nullptr;
     seg.ub = routed && a.up_b ? a.up_b + (uint64_t)e * a.Fr : nullptr;
-    return pm_stream_segments<Q, 2>(seg, ring, rc, grid, a.err);
+    const pm_block_q8K **tokrows = (const pm_block_q8K **)(smem + ps.act_off - 128);
+    return pm_gemv_tile<Q, 2, PM_TT>(seg, ring, smem + ps.act_off, tokrows, nrows, ps.rc, rb, a.H / 32u, ps.lpr,
+                                     grid, a.err);
 }
 
 template <int QR, int QS>
 __global__ void __launch_bounds__(PM_THREADS)
-    pm_layer_gu_kernel(const __grid_constant__ pm_layer_args a, uint32_t S_r, uint32_t stage_r, uint32_t rc_r, uint32_t S_s,
-                       uint32_t stage_s, uint32_t rc_s) {
+    pm_layer_gu_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t last;
     const uint32_t item = blockIdx.x;
@@ -293,8 +295,9 @@ __global__ void __launch_bounds__(PM_THREADS)
     const uint32_t F = routed ? a.Fr : a.Fs;
     const uint32_t row0 = blockIdx.y * a.gu_rows;
     if (row0 >= F) return;
-    const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, e, row0, F, S_r, stage_r, rc_r)
-                           : pm_layer_gu_item<QS>(a, smem, item, e, row0, F, S_s, stage_s, rc_s);
+    const uint32_t nrows = F - row0 < a.gu_rows ? F - row0 : a.gu_rows;
+    const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, e, row0, nrows, pr)
+                           : pm_layer_gu_item<QS>(a, smem, item, e, row0, nrows, psh);
     if (!ok) return;
     /* the last tile of each 256-row block quantizes that block of mid */
     const uint32_t fb = row0 / 256u;
@@ -309,21 +312,16 @@ __global__ void __launch_bounds__(PM_THREADS)
     if (!last) return;
     __threadfence();
     const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
+    const uint32_t lane = threadIdx.x & 31u;
+    float *stage_v = (float *)smem + (threadIdx.x >> 5) * 256u;
     for (uint32_t i = s0 + (threadIdx.x >> 5); i < s1; i += PM_WARPS) {
         const uint32_t p = __ldcg(a.pairs + i);
         const float *src = a.mid + (uint64_t)p * a.Fmax + fb * 256u;
-        /* read through L2: other CTAs wrote these rows */
-        float tmp[8];
-        const uint32_t lane = threadIdx.x & 31u;
 #pragma unroll
         for (int q = 0; q < 8; q++) {
             const uint32_t el = lane * 8u + q;
-            tmp[q] = el < blk_rows ? __ldcg(src + el) : 0.0f;
+            stage_v[el] = el < blk_rows ? __ldcg(src + el) : 0.0f; /* written by other CTAs: read via L2 */
         }
-        /* pm_q8k_warp reads src[lane*8 + q]; hand it the private copy */
-        float *stage_v = (float *)smem + (threadIdx.x >> 5) * 256u;
-#pragma unroll
-        for (int q = 0; q < 8; q++) stage_v[lane * 8u + q] = tmp[q];
         __syncwarp();
         pm_q8k_warp(stage_v, blk_rows, a.midq + (uint64_t)p * a.fb + fb);
         __syncwarp();
@@ -332,110 +330,80 @@ __global__ void __launch_bounds__(PM_THREADS)
 
 /* ======================================================= 5: down */
 
-struct pm_seg_ldn {
+struct pm_seg_dn2 {
+    const uint8_t *d;
+    const uint32_t *pairs;
+    uint32_t n, row0;
     const pm_layer_args *a;
-    uint32_t item0, row0;
-    uint64_t rb, stride;
-    const uint8_t *base0;
-    bool routed;
-    uint32_t nitems, nrows, n_units;
-    float *acc; /* [T][nrows_cta] */
-    uint32_t acc_ld;
-    __device__ uint32_t count() const { return nitems; }
-    __device__ const uint8_t *base(uint32_t sg, int) const {
-        const uint32_t e = __ldcg(a->item_expert + item0 + sg);
-        const uint8_t *b = routed ? base0 + (uint64_t)e * stride : base0;
-        return b + (uint64_t)row0 * rb;
+    __device__ const uint8_t *base(int) const { return d; }
+    __device__ uint32_t ntok() const { return n; }
+    __device__ const pm_block_q8K *tok(uint32_t ti) const {
+        return a->midq + (uint64_t)__ldcg(pairs + ti) * a->fb;
     }
-    __device__ uint32_t ntok(uint32_t sg) const {
-        return __ldcg(a->item_start + item0 + sg + 1) - __ldcg(a->item_start + item0 + sg);
+    __device__ void epi(uint32_t row, uint32_t ti, const float *v) const {
+        a->partial[(uint64_t)__ldcg(pairs + ti) * a->H + row0 + row] = v[0];
     }
-    __device__ const pm_block_q8K *tok(uint32_t sg, uint32_t ti) const {
-        const uint32_t p = __ldcg(a->pairs + __ldcg(a->item_start + item0 + sg) + ti);
-        return a->midq + (uint64_t)p * a->fb;
-    }
-    __device__ void epi(uint32_t sg, uint32_t row, uint32_t ti, const float *v) const {
-        const uint32_t p = __ldcg(a->pairs + __ldcg(a->item_start + item0 + sg) + ti);
-        acc[(p / a->n_slot) * acc_ld + row] += v[0];
-    }
-    __device__ void skip(uint32_t, uint32_t, uint32_t) const {}
 };
 
 template <int Q>
-__device__ bool pm_layer_dn_pass(const pm_layer_args &a, uint8_t *smem, bool routed, uint32_t item0,
-                                 uint32_t nitems, uint32_t row0, uint32_t nrows, float *acc, uint32_t S,
-                                 uint32_t stage, uint32_t rc) {
-    if (nitems == 0) return true;
+__device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t e, uint32_t row0,
+                                 uint32_t nrows, const pm_pass &ps) {
+    const bool routed = e < a.E;
+    const uint64_t rb = routed ? a.rb_dn_r : a.rb_dn_s;
     uint64_t *grid;
-    pm_ring ring = pm_ring_setup(smem, S, stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
-    pm_seg_ldn seg;
-    seg.a = &a;
-    seg.item0 = item0;
+    pm_ring ring = pm_ring_setup(smem, ps.S, ps.stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
+    pm_seg_dn2 seg;
+    seg.d = (routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown) + (uint64_t)row0 * rb;
+    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
+    seg.pairs = a.pairs + s0;
+    seg.n = s1 - s0;
     seg.row0 = row0;
-    seg.routed = routed;
-    seg.rb = routed ? a.rb_dn_r : a.rb_dn_s;
-    seg.stride = a.st_dn_r;
-    seg.base0 = routed ? a.down : a.sdown;
-    seg.nitems = nitems;
-    seg.nrows = nrows;
-    seg.n_units = Q == PM_QUANT_MXFP4 || Q == PM_QUANT_Q8_0 ? ((routed ? a.Fr : a.Fs) + 31u) / 32u
-                                                            : (routed ? a.Fr : a.Fs) / 32u;
-    seg.acc = acc;
-    seg.acc_ld = a.dn_rows;
-    const bool ok = pm_stream_segments<Q, 1>(seg, ring, rc, grid, a.err);
-    pm_ring_teardown(ring);
-    return ok;
+    seg.a = &a;
+    const uint32_t F = routed ? a.Fr : a.Fs;
+    const pm_block_q8K **tokrows = (const pm_block_q8K **)(smem + ps.act_off - 128);
+    pm_gemv_tile<Q, 1, PM_TT>(seg, ring, smem + ps.act_off, tokrows, nrows, ps.rc, rb, (F + 31u) / 32u, ps.lpr,
+                              grid, a.err);
 }
 
 template <int QR, int QS>
 __global__ void __launch_bounds__(PM_THREADS)
-    pm_layer_dn_kernel(const __grid_constant__ pm_layer_args a, uint32_t S_r, uint32_t stage_r, uint32_t rc_r, uint32_t S_s,
-                       uint32_t stage_s, uint32_t rc_s, uint32_t ring_bytes) {
+    pm_layer_dn_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t row0 = blockIdx.x * a.dn_rows;
+    const uint32_t item = blockIdx.x;
+    if (item >= __ldcg(a.n_items)) return;
+    const uint32_t e = __ldcg(a.item_expert + item);
+    const uint32_t row0 = blockIdx.y * a.dn_rows;
     const uint32_t nrows = a.H - row0 < a.dn_rows ? a.H - row0 : a.dn_rows;
-    float *acc = (float *)(smem + ring_bytes);
-    for (uint32_t i = threadIdx.x; i < a.T * a.dn_rows; i += blockDim.x) acc[i] = 0.0f;
-    __syncthreads();
-    const uint32_t n_all = __ldcg(a.n_items), n_r = __ldcg(a.n_items + 1);
-    if (!pm_layer_dn_pass<QR>(a, smem, true, 0, n_r, row0, nrows, acc, S_r, stage_r, rc_r)) return;
-    if (!pm_layer_dn_pass<QS>(a, smem, false, n_r, n_all - n_r, row0, nrows, acc, S_s, stage_s, rc_s)) return;
-    /* combine: + down bias of the routed slots (sum_s w_s b_s, cu:3601-3620) + residual */
-    for (uint32_t i = threadIdx.x; i < a.T * nrows; i += blockDim.x) {
-        const uint32_t t = i / nrows, j = i % nrows, r = row0 + j;
-        float v = acc[t * a.dn_rows + j];
-        if (a.down_b) {
-            float b = 0.0f;
-            for (uint32_t s = 0; s < a.k; s++) {
-                const uint32_t e = (uint32_t)a.sel[t * a.n_slot + s];
-                if (e >= a.lo && e < a.hi) b += a.w[t * a.n_slot + s] * a.down_b[(uint64_t)e * a.H + r];
-            }
-            if (b != 0.0f) v += b;
+    if (e < a.E)
+        pm_layer_dn_item<QR>(a, smem, item, e, row0, nrows, pr);
+    else
+        pm_layer_dn_item<QS>(a, smem, item, e, row0, nrows, psh);
+}
+
+/* ================================================= 6: combine */
+
+/* out[t][r] = sum over the token's local slots (slot order) of the down
+ * partials + down bias (sum_s w_s b_s, cu:3601-3620) + residual */
+__global__ void pm_layer_combine_kernel(const __grid_constant__ pm_layer_args a) {
+    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (uint64_t)a.T * a.H) return;
+    const uint32_t t = (uint32_t)(gid / a.H), r = (uint32_t)(gid % a.H);
+    float v = 0.0f, b = 0.0f;
+    for (uint32_t s = 0; s < a.k; s++) {
+        const uint32_t e = (uint32_t)a.sel[t * a.n_slot + s];
+        if (e >= a.lo && e < a.hi) {
+            v += a.partial[(uint64_t)(t * a.n_slot + s) * a.H + r];
+            if (a.down_b) b += a.w[t * a.n_slot + s] * a.down_b[(uint64_t)e * a.H + r];
         }
-        if (a.residual) v += a.residual[(uint64_t)t * a.H + r];
-        a.out[(uint64_t)t * a.H + r] = v;
     }
+    if (a.lo == 0)
+        for (uint32_t s = a.k; s < a.n_slot; s++) v += a.partial[(uint64_t)(t * a.n_slot + s) * a.H + r];
+    if (b != 0.0f) v += b;
+    if (a.residual) v += a.residual[gid];
+    a.out[gid] = v;
 }
 
 /* ============================================================= host */
-
-struct pm_ring_geo {
-    uint32_t S, stage, rc, bytes;
-};
-
-static pm_ring_geo pm_ring_for(uint32_t nmat, uint64_t rb, uint32_t rows_cta, bool grid, uint32_t target) {
-    pm_ring_geo g;
-    uint64_t rc = target / (nmat * rb);
-    if (rc < 1) rc = 1;
-    if (rc > rows_cta) rc = rows_cta;
-    while (rows_cta % rc) rc--;
-    g.rc = (uint32_t)rc;
-    g.stage = pm_stage_bytes(nmat, rb, g.rc);
-    uint32_t S = 65536u / g.stage;
-    g.S = S < 2 ? 2 : (S > 8 ? 8 : S);
-    g.bytes = pm_ring_offset(grid) + g.S * g.stage;
-    return g;
-}
 
 static bool pm_fmt_ok(uint32_t q, uint32_t n) { return pm_row_bytes(q, n) != 0; }
 
@@ -475,52 +443,92 @@ extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t
     v->mid = (float *)(b + L.mid);
     v->midq = b + L.midq;
     v->err = (uint32_t *)(b + L.err);
+    v->n_items = (uint32_t *)(b + L.n_items);
     v->n_slot = L.n_slot;
     v->f_max = L.Fmax;
     return 1;
 }
 
+/* largest power-of-two row count in [lo, hi] that still gives ~2 waves */
 static uint32_t pm_pow2_rows(uint64_t nrows_total, uint64_t ctas_other, uint32_t lo, uint32_t hi) {
-    /* largest power-of-two row count in [lo, hi] that still gives ~2 waves */
     uint32_t r = hi;
     while (r > lo && ((nrows_total + r - 1) / r) * ctas_other < 2ull * 148ull) r >>= 1;
     return r;
 }
 
+/* pass geometry: ring chunks of at least one row per warp slot and about
+ * 16 KB, as many stages as the shared-memory budget left by the token tile
+ * allows (two CTAs per SM) */
+static pm_pass pm_pass_for(uint32_t nmat, uint64_t rb, uint32_t n_units, uint32_t rows_cta, bool grid) {
+    pm_pass p;
+    p.lpr = n_units >= 32 ? 32u : (n_units >= 16 ? 16u : 8u);
+    const uint32_t step = PM_WARPS * (32u / p.lpr);
+    uint64_t rc = 16384u / (nmat * rb);
+    if (rc < step) rc = step;
+    rc = (rc / step) * step;
+    if (rc > rows_cta) rc = rows_cta;
+    while (rows_cta % rc) rc--;
+    p.rc = (uint32_t)rc;
+    p.stage = pm_stage_bytes(nmat, rb, p.rc);
+    const uint32_t acts = pm_acts_bytes(PM_TT, n_units);
+    const uint32_t budget = 110u * 1024u;
+    const uint32_t fixed = pm_ring_offset(grid) + acts + 128u;
+    const uint32_t S = budget > fixed + 2 * p.stage ? (budget - fixed) / p.stage : 2u;
+    p.S = S < 2 ? 2 : (S > 8 ? 8 : S);
+    p.ring_bytes = (pm_ring_offset(grid) + p.S * p.stage + 15u) & ~15u;
+    p.act_off = p.ring_bytes + 128u; /* 128 bytes of token-row pointers precede the planes */
+    return p;
+}
+
+static uint32_t pm_pass_smem(const pm_pass &p, uint32_t n_units) { return p.act_off + pm_acts_bytes(PM_TT, n_units); }
+
+static inline void pm_ev(void *const *ev, int i, cudaStream_t st) {
+    if (ev && ev[i]) cudaEventRecord((cudaEvent_t)ev[i], st);
+}
+
 template <int QR, int QS>
-static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st) {
+static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st, void *const *ev) {
     static uint64_t done_gu = 0, done_dn = 0;
-    /* 4: gate/up */
-    const pm_ring_geo gr = pm_ring_for(2, a.rb_gu_r, a.gu_rows, QR == PM_QUANT_IQ2_XXS, 16384);
-    const pm_ring_geo gs = a.S ? pm_ring_for(2, a.rb_gu_s, a.gu_rows, QS == PM_QUANT_IQ2_XXS, 16384) : gr;
-    uint32_t smem_gu = gr.bytes > gs.bytes ? gr.bytes : gs.bytes;
+    /* 4: gate/up (+ q8_K of mid) */
+    const uint32_t hu = a.H / 32u;
+    const pm_pass gr = pm_pass_for(2, a.rb_gu_r, hu, a.gu_rows, QR == PM_QUANT_IQ2_XXS);
+    const pm_pass gs = a.S ? pm_pass_for(2, a.rb_gu_s, hu, a.gu_rows, QS == PM_QUANT_IQ2_XXS) : gr;
+    uint32_t smem_gu = pm_pass_smem(gr, hu) > pm_pass_smem(gs, hu) ? pm_pass_smem(gr, hu) : pm_pass_smem(gs, hu);
     if (smem_gu < PM_WARPS * 1024u) smem_gu = PM_WARPS * 1024u;
     if (!pm_smem_attr(pm_layer_gu_kernel<QR, QS>, smem_gu, &done_gu)) return 0;
     dim3 ggrid(L.max_items, (L.Fmax + a.gu_rows - 1) / a.gu_rows);
-    pm_layer_gu_kernel<QR, QS><<<ggrid, PM_THREADS, smem_gu, st>>>(a, gr.S, gr.stage, gr.rc, gs.S, gs.stage, gs.rc);
+    pm_layer_gu_kernel<QR, QS><<<ggrid, PM_THREADS, smem_gu, st>>>(a, gr, gs);
     if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
-    /* 5: down + combine */
-    const pm_ring_geo dr = pm_ring_for(1, a.rb_dn_r, a.dn_rows, QR == PM_QUANT_IQ2_XXS, 8192);
-    const pm_ring_geo ds = a.S ? pm_ring_for(1, a.rb_dn_s, a.dn_rows, QS == PM_QUANT_IQ2_XXS, 8192) : dr;
-    const uint32_t ring = ((dr.bytes > ds.bytes ? dr.bytes : ds.bytes) + 15u) & ~15u;
-    const uint32_t smem_dn = ring + a.T * a.dn_rows * 4u;
+    pm_ev(ev, 4, st);
+    /* 5: down -> partial rows */
+    const uint32_t fr = (a.Fr + 31u) / 32u, fs = a.S ? (a.Fs + 31u) / 32u : fr;
+    const pm_pass dr = pm_pass_for(1, a.rb_dn_r, fr, a.dn_rows, QR == PM_QUANT_IQ2_XXS);
+    const pm_pass ds = a.S ? pm_pass_for(1, a.rb_dn_s, fs, a.dn_rows, QS == PM_QUANT_IQ2_XXS) : dr;
+    const uint32_t smem_dn = pm_pass_smem(dr, fr) > pm_pass_smem(ds, fs) ? pm_pass_smem(dr, fr) : pm_pass_smem(ds, fs);
     if (!pm_smem_attr(pm_layer_dn_kernel<QR, QS>, smem_dn, &done_dn)) return 0;
-    pm_layer_dn_kernel<QR, QS><<<(a.H + a.dn_rows - 1) / a.dn_rows, PM_THREADS, smem_dn, st>>>(
-        a, dr.S, dr.stage, dr.rc, ds.S, ds.stage, ds.rc, ring);
-    return pm_ok(cudaGetLastError(), "moe layer down launch");
+    dim3 dgrid(L.max_items, (a.H + a.dn_rows - 1) / a.dn_rows);
+    pm_layer_dn_kernel<QR, QS><<<dgrid, PM_THREADS, smem_dn, st>>>(a, dr, ds);
+    if (!pm_ok(cudaGetLastError(), "moe layer down launch")) return 0;
+    /* 6: combine */
+    const uint64_t tot = (uint64_t)a.T * a.H;
+    pm_layer_combine_kernel<<<(uint32_t)((tot + 255) / 256), 256, 0, st>>>(a);
+    if (!pm_ok(cudaGetLastError(), "moe layer combine launch")) return 0;
+    pm_ev(ev, 5, st);
+    return 1;
 }
 
-#define PM_Q2(QR)                                                                      \
-    switch (qs) {                                                                      \
-    case PM_QUANT_Q4_K: return pm_layer_launch<QR, PM_QUANT_Q4_K>(a, L, st);           \
-    case PM_QUANT_Q2_K: return pm_layer_launch<QR, PM_QUANT_Q2_K>(a, L, st);           \
-    case PM_QUANT_IQ2_XXS: return pm_layer_launch<QR, PM_QUANT_IQ2_XXS>(a, L, st);     \
-    case PM_QUANT_MXFP4: return pm_layer_launch<QR, PM_QUANT_MXFP4>(a, L, st);         \
-    case PM_QUANT_Q8_0: return pm_layer_launch<QR, PM_QUANT_Q8_0>(a, L, st);           \
-    default: return 0;                                                                 \
+#define PM_Q2(QR)                                                                          \
+    switch (qs) {                                                                          \
+    case PM_QUANT_Q4_K: return pm_layer_launch<QR, PM_QUANT_Q4_K>(a, L, st, ev);           \
+    case PM_QUANT_Q2_K: return pm_layer_launch<QR, PM_QUANT_Q2_K>(a, L, st, ev);           \
+    case PM_QUANT_IQ2_XXS: return pm_layer_launch<QR, PM_QUANT_IQ2_XXS>(a, L, st, ev);     \
+    case PM_QUANT_MXFP4: return pm_layer_launch<QR, PM_QUANT_MXFP4>(a, L, st, ev);         \
+    case PM_QUANT_Q8_0: return pm_layer_launch<QR, PM_QUANT_Q8_0>(a, L, st, ev);           \
+    default: return 0;                                                                     \
     }
 
-static int pm_layer_dispatch(uint32_t qr, uint32_t qs, const pm_layer_args &a, const pm_layout &L, cudaStream_t st) {
+static int pm_layer_dispatch(uint32_t qr, uint32_t qs, const pm_layer_args &a, const pm_layout &L, cudaStream_t st,
+                             void *const *ev) {
     switch (qr) {
     case PM_QUANT_Q4_K: PM_Q2(PM_QUANT_Q4_K)
     case PM_QUANT_Q2_K: PM_Q2(PM_QUANT_Q2_K)
@@ -531,13 +539,12 @@ static int pm_layer_dispatch(uint32_t qr, uint32_t qs, const pm_layer_args &a, c
     }
 }
 
-extern "C" int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
-                                uint32_t n_tok, void *ws, size_t ws_bytes, void *stream) {
+static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
+                             uint32_t n_tok, void *ws, size_t ws_bytes, void *stream, void *const *ev) {
     if (!pm_desc_ok(d) || !out || !x || !ws || n_tok == 0) return 0;
     if (!pm_router_args_ok(d->n_expert, d->n_used, n_tok, d->router_mode, 0, d->n_group, d->topk_group)) return 0;
     const pm_layout L = pm_make_layout(d, n_tok);
     if (L.total > ws_bytes) return 0;
-    if ((uint64_t)n_tok * 64u * 4u > 160u * 1024u) return 0; /* down accumulator bound (decode path) */
     cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
     uint8_t *b = (uint8_t *)ws;
     pm_layer_args a;
@@ -566,25 +573,38 @@ extern "C" int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, cons
     a.pairs = (uint32_t *)(b + L.pairs);
     a.mid = (float *)(b + L.mid);
     a.midq = (pm_block_q8K *)(b + L.midq);
+    a.partial = (float *)(b + L.partial);
     a.cnt = (uint32_t *)(b + L.cnt);
     a.sel_done = (uint32_t *)(b + L.sel_done);
     a.err = (uint32_t *)(b + L.err);
     a.out = out;
     a.residual = residual;
-    const uint64_t items_est = L.max_items;
-    a.gu_rows = pm_pow2_rows(L.Fmax, items_est, 8, 64);
-    a.dn_rows = pm_pow2_rows(L.H, 1, 8, 64);
-    while (a.dn_rows > 8 && (uint64_t)a.T * a.dn_rows * 4u > 64u * 1024u) a.dn_rows >>= 1;
+    a.gu_rows = pm_pow2_rows(L.Fmax, L.max_items, 8, 128);
+    a.dn_rows = pm_pow2_rows(L.H, L.max_items, 16, 512);
 
     /* 1, 2: logits and q8_K(x) */
+    pm_ev(ev, 0, st);
     if (!pm_launch_router_logits(a.logits, d->router_w, x, d->router_logit_b, L.E, L.H, L.T, st)) return 0;
+    pm_ev(ev, 1, st);
     if (!pm_launch_q8k(a.xq, x, L.H, L.T, st)) return 0;
+    pm_ev(ev, 2, st);
     /* 3: select + CSR */
-    uint32_t smem_sel = 4u * 2u * L.E * 4u;
-    if (smem_sel < 2u * L.E * 4u) smem_sel = 2u * L.E * 4u;
+    const uint32_t smem_sel = 4u * 2u * L.E * 4u;
     static uint64_t done_sel = 0;
     if (!pm_smem_attr(pm_layer_select_kernel, smem_sel, &done_sel)) return 0;
     pm_layer_select_kernel<<<(L.T + 3u) / 4u, 128, smem_sel, st>>>(a);
     if (!pm_ok(cudaGetLastError(), "moe layer select launch")) return 0;
-    return pm_layer_dispatch(d->quant, d->n_shared ? d->shared_quant : d->quant, a, L, st);
+    pm_ev(ev, 3, st);
+    return pm_layer_dispatch(d->quant, d->n_shared ? d->shared_quant : d->quant, a, L, st, ev);
+}
+
+extern "C" int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
+                                uint32_t n_tok, void *ws, size_t ws_bytes, void *stream) {
+    return pm_moe_layer_impl(d, out, x, residual, n_tok, ws, ws_bytes, stream, nullptr);
+}
+
+extern "C" int pulsar_moe_layer_profiled(const pulsar_moe_layer_desc *d, float *out, const float *x,
+                                         const float *residual, uint32_t n_tok, void *ws, size_t ws_bytes,
+                                         void *stream, void *const *events) {
+    return pm_moe_layer_impl(d, out, x, residual, n_tok, ws, ws_bytes, stream, events);
 }

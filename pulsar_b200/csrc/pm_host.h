@@ -18,15 +18,28 @@ static inline int pm_cur_device() {
     return d;
 }
 
-/* raise a kernel's dynamic shared-memory cap once per device */
+/* raise a kernel's dynamic shared-memory cap to the most the device
+ * allows next to the kernel's static shared memory, once per (kernel,
+ * device); a request above it fails cleanly */
 template <class K>
 static inline int pm_smem_attr(K kernel, uint32_t bytes, uint64_t *done_mask) {
-    const int dev = pm_cur_device();
     if (bytes <= 48u * 1024u) return 1;
+    const int dev = pm_cur_device();
     if (dev < 64 && (*done_mask >> dev) & 1ull) return 1;
-    if (!pm_ok(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
-               "smem attribute"))
+    int optin = 0;
+    cudaFuncAttributes fa;
+    if (!pm_ok(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev), "smem optin query") ||
+        !pm_ok(cudaFuncGetAttributes(&fa, kernel), "kernel attributes"))
         return 0;
+    const int avail = optin - (int)fa.sharedSizeBytes;
+    if ((int)bytes > avail) {
+        fprintf(stderr, "pulsar-b200: %u bytes of shared memory requested, kernel allows %d\n", bytes, avail);
+        return 0;
+    }
+    if (!pm_ok(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, avail), "smem attribute")) {
+        (void)cudaGetLastError();
+        return 0;
+    }
     if (dev < 64) *done_mask |= 1ull << dev;
     return 1;
 }

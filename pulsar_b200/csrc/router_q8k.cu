@@ -52,35 +52,67 @@ extern "C" int pulsar_quantize_q8_K(void *out_dev, const void *x_dev, uint32_t i
  * order, xor butterfly, one rounding.  W rows may be any length; the
  * float4 path needs in_dim % 4 == 0 (16-byte aligned rows). */
 #define PM_RT_TOK 4
-__global__ void pm_router_logits_kernel(float *logits, const float *w, const float *x, const float *lbias,
-                                        uint32_t n_expert, uint32_t in_dim, uint32_t n_tok) {
+__global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, const float *__restrict__ w,
+                                                               const float *__restrict__ x,
+                                                               const float *__restrict__ lbias, uint32_t n_expert,
+                                                               uint32_t in_dim, uint32_t n_tok) {
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const uint32_t t0 = blockIdx.y * PM_RT_TOK;
     if (e >= n_expert) return;
+    const uint32_t nt = n_tok - t0 < PM_RT_TOK ? n_tok - t0 : PM_RT_TOK;
     const float *wr = w + (uint64_t)e * in_dim;
     double p[PM_RT_TOK];
 #pragma unroll
     for (int t = 0; t < PM_RT_TOK; t++) p[t] = 0.0;
     const uint32_t nj = (in_dim + 127u) / 128u;
-    const bool vec = (in_dim & 3u) == 0;
-    for (uint32_t j = 0; j < nj; j++) {
-        const uint32_t i0 = 128u * j + 4u * lane;
-        float wv[4];
-        if (vec && i0 + 3 < in_dim) {
-            const float4 q = __ldg((const float4 *)(wr + i0));
-            wv[0] = q.x, wv[1] = q.y, wv[2] = q.z, wv[3] = q.w;
-        } else {
+    if ((in_dim & 127u) == 0) {
+        /* whole 128-wide chunks: four chunks of W and x in flight per step */
+        uint32_t j = 0;
+        for (; j + 4 <= nj; j += 4) {
+            float4 wv[4], xv[4][PM_RT_TOK];
 #pragma unroll
-            for (int c = 0; c < 4; c++) wv[c] = i0 + c < in_dim ? wr[i0 + c] : 0.0f;
+            for (int q = 0; q < 4; q++) wv[q] = __ldg((const float4 *)(wr + 128u * (j + q) + 4u * lane));
+#pragma unroll
+            for (int t = 0; t < PM_RT_TOK; t++)
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    xv[q][t] = (uint32_t)t < nt ? __ldg((const float4 *)(x + (uint64_t)(t0 + t) * in_dim +
+                                                                          128u * (j + q) + 4u * lane))
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int t = 0; t < PM_RT_TOK; t++) {
+                    p[t] = fma((double)wv[q].x, (double)xv[q][t].x, p[t]);
+                    p[t] = fma((double)wv[q].y, (double)xv[q][t].y, p[t]);
+                    p[t] = fma((double)wv[q].z, (double)xv[q][t].z, p[t]);
+                    p[t] = fma((double)wv[q].w, (double)xv[q][t].w, p[t]);
+                }
         }
+        for (; j < nj; j++) {
+            const float4 wv = __ldg((const float4 *)(wr + 128u * j + 4u * lane));
 #pragma unroll
-        for (int t = 0; t < PM_RT_TOK; t++) {
-            if (t0 + t >= n_tok) break;
-            const float *xr = x + (uint64_t)(t0 + t) * in_dim;
+            for (int t = 0; t < PM_RT_TOK; t++) {
+                if ((uint32_t)t >= nt) break;
+                const float4 xv = __ldg((const float4 *)(x + (uint64_t)(t0 + t) * in_dim + 128u * j + 4u * lane));
+                p[t] = fma((double)wv.x, (double)xv.x, p[t]);
+                p[t] = fma((double)wv.y, (double)xv.y, p[t]);
+                p[t] = fma((double)wv.z, (double)xv.z, p[t]);
+                p[t] = fma((double)wv.w, (double)xv.w, p[t]);
+            }
+        }
+    } else {
+        for (uint32_t j = 0; j < nj; j++) {
+            const uint32_t i0 = 128u * j + 4u * lane;
 #pragma unroll
-            for (int c = 0; c < 4; c++)
-                if (i0 + c < in_dim) p[t] = fma((double)wv[c], (double)__ldg(xr + i0 + c), p[t]);
+            for (int t = 0; t < PM_RT_TOK; t++) {
+                if ((uint32_t)t >= nt) break;
+                const float *xr = x + (uint64_t)(t0 + t) * in_dim;
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+                    if (i0 + c < in_dim) p[t] = fma((double)wr[i0 + c], (double)xr[i0 + c], p[t]);
+            }
         }
     }
 #pragma unroll
@@ -91,7 +123,7 @@ __global__ void pm_router_logits_kernel(float *logits, const float *w, const flo
     if (lane == 0) {
 #pragma unroll
         for (int t = 0; t < PM_RT_TOK; t++) {
-            if (t0 + t >= n_tok) break;
+            if ((uint32_t)t >= nt) break;
             float l = __double2float_rn(p[t]);
             if (lbias) l = __fadd_rn(l, lbias[e]);
             logits[(uint64_t)(t0 + t) * n_expert + e] = l;

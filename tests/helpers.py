@@ -108,8 +108,11 @@ class HostLayer:
         dev = torch.device("cuda")
 
         def up_(a, slack=True):
-            t = torch.from_numpy(np.ascontiguousarray(a).reshape(-1).copy())
-            if slack and t.dtype == torch.uint8:
+            a = np.ascontiguousarray(a)
+            if a.dtype != np.uint8:  # f32 tensors keep their shape ([E][F] bias rows)
+                return torch.from_numpy(a.copy()).to(dev)
+            t = torch.from_numpy(a.reshape(-1).copy())
+            if slack:
                 t = torch.cat([t, torch.zeros(256, dtype=torch.uint8)])
             return t.to(dev)
 
