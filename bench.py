@@ -283,6 +283,8 @@ def cpu_baseline(stack, T: int, x0: np.ndarray, threads: int, budget_s: float = 
         rw = L.router_w.cpu().numpy()
         sb = L.router_select_b.cpu().numpy()
         rg, rd = L.rb_gu, L.rb_down
+        if not np.isfinite(x).all():
+            raise RuntimeError(f"cpu baseline: non-finite hidden rows entering layer {done}")
         t0 = time.perf_counter()
         lg = orc.router_logits(rw, x)
         sel, w = orc.router_select(lg, sb, k, 1.0, 0)

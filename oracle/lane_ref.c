@@ -150,10 +150,11 @@ int orc_router_select(int32_t *selected, float *weights, const float *logits, co
                     bp = prob[e];
                     best = e;
                 }
-            sel[k] = (int32_t)best;
+            /* only NaN scores left: the slot stays unrouted (-1, weight 0) */
+            sel[k] = best == UINT32_MAX ? -1 : (int32_t)best;
             w[k] = bp;
             sum += bp;
-            score[best] = -INFINITY;
+            if (best != UINT32_MAX) score[best] = -INFINITY;
         }
         if (softmax_mode == 2) {
             for (uint32_t s = 0; s < sink; s++) {

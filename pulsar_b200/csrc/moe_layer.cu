@@ -42,11 +42,15 @@ int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32
 
 __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 
+#define PM_TT 8 /* tokens per register tile = tokens per work unit */
+
 /* ------------------------------------------------------------ layout */
 
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
-    size_t logits, sel, w, xq, n_items, item_expert, item_start, pairs, mid, midq, partial, cnt, sel_done, err, total;
+    uint32_t max_work;
+    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, pairs, mid, midq, partial, cnt,
+        sel_done, err, total;
 };
 
 static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -74,6 +78,9 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.n_items = o, o = pm_al(o + 16);
     L.item_expert = o, o = pm_al(o + (size_t)L.max_items * 4);
     L.item_start = o, o = pm_al(o + (size_t)(L.max_items + 1) * 4);
+    L.max_work = L.max_items + (uint32_t)(((uint64_t)T * L.n_slot + PM_TT - 1) / PM_TT);
+    L.work_item = o, o = pm_al(o + (size_t)L.max_work * 4);
+    L.work_t0 = o, o = pm_al(o + (size_t)L.max_work * 4);
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
     L.midq = o, o = pm_al(o + (size_t)T * L.n_slot * L.fb * PM_Q8_K_BYTES);
@@ -99,8 +106,9 @@ struct pm_layer_args {
     int32_t *sel;
     float *w;
     pm_block_q8K *xq;
-    uint32_t *n_items; /* [0] all items, [1] routed items */
+    uint32_t *n_items; /* [0] all items, [1] routed items, [2] work units */
     uint32_t *item_expert, *item_start, *pairs;
+    uint32_t *work_item, *work_t0; /* work unit = (item, first token of its chunk of <= PM_TT) */
     float *mid;
     pm_block_q8K *midq;
     float *partial; /* [T * n_slot][H] down outputs before the combine */
@@ -115,126 +123,116 @@ struct pm_layer_args {
 
 __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_constant__ pm_layer_args a) {
     extern __shared__ __align__(16) uint8_t sm[];
-    __shared__ uint32_t is_last;
+    __shared__ uint32_t is_last, tot_pairs, tot_items, tot_work;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
     const uint32_t token = blockIdx.x * 4u + wid;
     if (token < a.T) {
         float *score = (float *)sm + (size_t)wid * 2 * a.E;
         pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0, a.n_group,
-                        a.topk_group, score, score + a.E);
+                        a.topk_group, score, score + a.E, a.n_slot);
+        if (lane < a.S) { /* shared experts: always-on slots k.., ids E + s, weight 1 */
+            a.sel[token * a.n_slot + a.k + lane] = (int32_t)(a.E + lane);
+            a.w[token * a.n_slot + a.k + lane] = 1.0f;
+        }
     }
-    /* sel/w rows are n_slot wide here; pm_select_token wrote them k wide */
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        const uint32_t prev = atomicAdd(a.sel_done, 1u);
-        is_last = prev == gridDim.x - 1u;
+        is_last = atomicAdd(a.sel_done, 1u) == gridDim.x - 1u;
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
     /* ---- the last CTA: CSR by expert over routed pairs in [lo, hi) ---- */
-    uint32_t *cnt = (uint32_t *)sm;       /* [E] counts, then cursors */
-    uint32_t *item_of = cnt + a.E;        /* [E] item index */
+    uint32_t *cnt = (uint32_t *)sm; /* [E] counts, then fill cursors */
     for (uint32_t e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     const uint32_t n_routed = a.T * a.k;
-    for (uint32_t p = threadIdx.x; p < n_routed; p += blockDim.x) {
-        const uint32_t e = (uint32_t)__ldcg(a.sel + p);
+    for (uint32_t q = threadIdx.x; q < n_routed; q += blockDim.x) {
+        const uint32_t e = (uint32_t)__ldcg(a.sel + (q / a.k) * a.n_slot + q % a.k);
         if (e >= a.lo && e < a.hi) atomicAdd(&cnt[e], 1u);
     }
     __syncthreads();
-    __shared__ uint32_t tot_pairs, tot_items;
     if (wid == 0) {
-        /* exclusive scans over experts: pair offsets and item indices */
-        uint32_t carry_p = 0, carry_i = 0;
+        /* exclusive scans over experts: pair offsets, item indices, work units */
+        uint32_t carry_p = 0, carry_i = 0, carry_w = 0;
         for (uint32_t c = 0; c < a.E; c += 32u) {
             const uint32_t e = c + lane;
             const uint32_t v = e < a.E ? cnt[e] : 0u;
-            uint32_t ip = v, ii = v ? 1u : 0u;
+            const uint32_t nw = (v + PM_TT - 1) / PM_TT;
+            uint32_t ip = v, ii = v ? 1u : 0u, iw = nw;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t up = __shfl_up_sync(0xffffffffu, ip, o);
                 const uint32_t ui = __shfl_up_sync(0xffffffffu, ii, o);
-                if (lane >= (uint32_t)o) ip += up, ii += ui;
+                const uint32_t uw = __shfl_up_sync(0xffffffffu, iw, o);
+                if (lane >= (uint32_t)o) ip += up, ii += ui, iw += uw;
             }
-            const uint32_t start = carry_p + ip - v, item = carry_i + ii - (v ? 1u : 0u);
+            const uint32_t start = carry_p + ip - v, item = carry_i + ii - (v ? 1u : 0u), w0 = carry_w + iw - nw;
             if (e < a.E) {
-                cnt[e] = start; /* becomes the cursor */
-                item_of[e] = v ? item : UINT32_MAX;
+                cnt[e] = start;
                 if (v) {
                     a.item_expert[item] = e;
                     a.item_start[item] = start;
+                    for (uint32_t j = 0; j < nw; j++) {
+                        a.work_item[w0 + j] = item;
+                        a.work_t0[w0 + j] = j * PM_TT;
+                    }
                 }
             }
             carry_p += __shfl_sync(0xffffffffu, ip, 31);
             carry_i += __shfl_sync(0xffffffffu, ii, 31);
+            carry_w += __shfl_sync(0xffffffffu, iw, 31);
         }
-        if (lane == 0) {
-            tot_pairs = carry_p;
-            tot_items = carry_i;
-        }
+        if (lane == 0) tot_pairs = carry_p, tot_items = carry_i, tot_work = carry_w;
     }
     __syncthreads();
     if (wid == 0) {
         /* stable fill: entries in (token, slot) order, ranks via match_any */
         for (uint32_t c = 0; c < n_routed; c += 32u) {
-            const uint32_t p = c + lane;
-            uint32_t e = UINT32_MAX;
-            if (p < n_routed) {
-                const uint32_t v = (uint32_t)__ldcg(a.sel + p);
+            const uint32_t q = c + lane;
+            uint32_t e = UINT32_MAX, pair = 0;
+            if (q < n_routed) {
+                pair = (q / a.k) * a.n_slot + q % a.k;
+                const uint32_t v = (uint32_t)__ldcg(a.sel + pair);
                 if (v >= a.lo && v < a.hi) e = v;
             }
             const uint32_t peers = __match_any_sync(0xffffffffu, e);
             const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
-            if (e != UINT32_MAX) {
-                const uint32_t t = p / a.k, s = p % a.k;
-                a.pairs[cnt[e] + rank] = t * a.n_slot + s;
-            }
+            if (e != UINT32_MAX) a.pairs[cnt[e] + rank] = pair;
             __syncwarp();
             if (e != UINT32_MAX && rank == 0) cnt[e] += __popc(peers);
             __syncwarp();
         }
     }
-    /* repack sel/w from k-wide to n_slot-wide rows (in place, backwards) */
     __syncthreads();
-    if (a.S) {
-        if (threadIdx.x == 0) {
-            for (int32_t t = (int32_t)a.T - 1; t >= 0; t--) {
-                for (int32_t s = (int32_t)a.k - 1; s >= 0; s--) {
-                    a.sel[(uint32_t)t * a.n_slot + s] = __ldcg(a.sel + (uint32_t)t * a.k + s);
-                    a.w[(uint32_t)t * a.n_slot + s] = __ldcg(a.w + (uint32_t)t * a.k + s);
-                }
-                for (uint32_t s = 0; s < a.S; s++) {
-                    a.sel[(uint32_t)t * a.n_slot + a.k + s] = (int32_t)(a.E + s);
-                    a.w[(uint32_t)t * a.n_slot + a.k + s] = 1.0f;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    /* shared experts: computed on the shard that owns expert 0 */
+    /* shared experts (computed on the shard that owns expert 0): one item
+     * each over all tokens, appended after the routed items */
     const uint32_t n_sh = a.lo == 0 ? a.S : 0u;
+    const uint32_t sh_chunks = (a.T + PM_TT - 1) / PM_TT;
     for (uint32_t s = 0; s < n_sh; s++) {
-        const uint32_t item = tot_items + s, base = tot_pairs + s * a.T;
+        const uint32_t item = tot_items + s, base = tot_pairs + s * a.T, w0 = tot_work + s * sh_chunks;
         if (threadIdx.x == 0) {
             a.item_expert[item] = a.E + s;
             a.item_start[item] = base;
         }
         for (uint32_t t = threadIdx.x; t < a.T; t += blockDim.x) a.pairs[base + t] = t * a.n_slot + a.k + s;
+        for (uint32_t j = threadIdx.x; j < sh_chunks; j += blockDim.x) {
+            a.work_item[w0 + j] = item;
+            a.work_t0[w0 + j] = j * PM_TT;
+        }
     }
     if (threadIdx.x == 0) {
         a.item_start[tot_items + n_sh] = tot_pairs + n_sh * a.T;
         a.n_items[0] = tot_items + n_sh;
         a.n_items[1] = tot_items;
+        a.n_items[2] = tot_work + n_sh * sh_chunks;
         *a.sel_done = 0;
     }
     for (uint32_t i = threadIdx.x; i < a.max_items * a.fb; i += blockDim.x) a.cnt[i] = 0;
 }
 
 /* ====================================================== 4: gate / up */
-
-#define PM_TT 8 /* tokens per register tile */
 
 struct pm_seg_gu2 {
     const uint8_t *g, *u;
@@ -262,8 +260,8 @@ struct pm_pass {
 };
 
 template <int Q>
-__device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t e, uint32_t row0,
-                                 uint32_t nrows, const pm_pass &ps) {
+__device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t t0, uint32_t e,
+                                 uint32_t row0, uint32_t nrows, const pm_pass &ps) {
     const bool routed = e < a.E;
     const uint64_t rb = routed ? a.rb_gu_r : a.rb_gu_s;
     uint64_t *grid;
@@ -272,8 +270,8 @@ __device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t
     seg.g = (routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate) + (uint64_t)row0 * rb;
     seg.u = (routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup) + (uint64_t)row0 * rb;
     const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
-    seg.pairs = a.pairs + s0;
-    seg.n = s1 - s0;
+    seg.pairs = a.pairs + s0 + t0;
+    seg.n = s1 - s0 - t0 < PM_TT ? s1 - s0 - t0 : PM_TT;
     seg.row0 = row0;
     seg.a = &a;
     seg.gb = routed && a.gate_b ? a.gate_b + (uint64_t)e * a.Fr : nullptr;
@@ -288,21 +286,24 @@ __global__ void __launch_bounds__(PM_THREADS)
     pm_layer_gu_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t last;
-    const uint32_t item = blockIdx.x;
-    if (item >= __ldcg(a.n_items)) return;
+    const uint32_t wk = blockIdx.x;
+    if (wk >= __ldcg(a.n_items + 2)) return;
+    const uint32_t item = __ldcg(a.work_item + wk), t0 = __ldcg(a.work_t0 + wk);
     const uint32_t e = __ldcg(a.item_expert + item);
     const bool routed = e < a.E;
     const uint32_t F = routed ? a.Fr : a.Fs;
     const uint32_t row0 = blockIdx.y * a.gu_rows;
     if (row0 >= F) return;
     const uint32_t nrows = F - row0 < a.gu_rows ? F - row0 : a.gu_rows;
-    const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, e, row0, nrows, pr)
-                           : pm_layer_gu_item<QS>(a, smem, item, e, row0, nrows, psh);
+    const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, t0, e, row0, nrows, pr)
+                           : pm_layer_gu_item<QS>(a, smem, item, t0, e, row0, nrows, psh);
     if (!ok) return;
-    /* the last tile of each 256-row block quantizes that block of mid */
+    /* the last (tile, token chunk) CTA of each 256-row block quantizes that
+     * block of every pair's mid row */
+    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
     const uint32_t fb = row0 / 256u;
     const uint32_t blk_rows = F - fb * 256u < 256u ? F - fb * 256u : 256u;
-    const uint32_t tiles = (blk_rows + a.gu_rows - 1) / a.gu_rows;
+    const uint32_t tiles = (blk_rows + a.gu_rows - 1) / a.gu_rows * ((s1 - s0 + PM_TT - 1) / PM_TT);
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -311,7 +312,6 @@ __global__ void __launch_bounds__(PM_THREADS)
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
     const uint32_t lane = threadIdx.x & 31u;
     float *stage_v = (float *)smem + (threadIdx.x >> 5) * 256u;
     for (uint32_t i = s0 + (threadIdx.x >> 5); i < s1; i += PM_WARPS) {
@@ -346,8 +346,8 @@ struct pm_seg_dn2 {
 };
 
 template <int Q>
-__device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t e, uint32_t row0,
-                                 uint32_t nrows, const pm_pass &ps) {
+__device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t t0, uint32_t e,
+                                 uint32_t row0, uint32_t nrows, const pm_pass &ps) {
     const bool routed = e < a.E;
     const uint64_t rb = routed ? a.rb_dn_r : a.rb_dn_s;
     uint64_t *grid;
@@ -355,8 +355,8 @@ __device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t
     pm_seg_dn2 seg;
     seg.d = (routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown) + (uint64_t)row0 * rb;
     const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
-    seg.pairs = a.pairs + s0;
-    seg.n = s1 - s0;
+    seg.pairs = a.pairs + s0 + t0;
+    seg.n = s1 - s0 - t0 < PM_TT ? s1 - s0 - t0 : PM_TT;
     seg.row0 = row0;
     seg.a = &a;
     const uint32_t F = routed ? a.Fr : a.Fs;
@@ -369,15 +369,16 @@ template <int QR, int QS>
 __global__ void __launch_bounds__(PM_THREADS)
     pm_layer_dn_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t item = blockIdx.x;
-    if (item >= __ldcg(a.n_items)) return;
+    const uint32_t wk = blockIdx.x;
+    if (wk >= __ldcg(a.n_items + 2)) return;
+    const uint32_t item = __ldcg(a.work_item + wk), t0 = __ldcg(a.work_t0 + wk);
     const uint32_t e = __ldcg(a.item_expert + item);
     const uint32_t row0 = blockIdx.y * a.dn_rows;
     const uint32_t nrows = a.H - row0 < a.dn_rows ? a.H - row0 : a.dn_rows;
     if (e < a.E)
-        pm_layer_dn_item<QR>(a, smem, item, e, row0, nrows, pr);
+        pm_layer_dn_item<QR>(a, smem, item, t0, e, row0, nrows, pr);
     else
-        pm_layer_dn_item<QS>(a, smem, item, e, row0, nrows, psh);
+        pm_layer_dn_item<QS>(a, smem, item, t0, e, row0, nrows, psh);
 }
 
 /* ================================================= 6: combine */
@@ -496,7 +497,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     uint32_t smem_gu = pm_pass_smem(gr, hu) > pm_pass_smem(gs, hu) ? pm_pass_smem(gr, hu) : pm_pass_smem(gs, hu);
     if (smem_gu < PM_WARPS * 1024u) smem_gu = PM_WARPS * 1024u;
     if (!pm_smem_attr(pm_layer_gu_kernel<QR, QS>, smem_gu, &done_gu)) return 0;
-    dim3 ggrid(L.max_items, (L.Fmax + a.gu_rows - 1) / a.gu_rows);
+    dim3 ggrid(L.max_work, (L.Fmax + a.gu_rows - 1) / a.gu_rows);
     pm_layer_gu_kernel<QR, QS><<<ggrid, PM_THREADS, smem_gu, st>>>(a, gr, gs);
     if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
     pm_ev(ev, 4, st);
@@ -506,7 +507,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     const pm_pass ds = a.S ? pm_pass_for(1, a.rb_dn_s, fs, a.dn_rows, QS == PM_QUANT_IQ2_XXS) : dr;
     const uint32_t smem_dn = pm_pass_smem(dr, fr) > pm_pass_smem(ds, fs) ? pm_pass_smem(dr, fr) : pm_pass_smem(ds, fs);
     if (!pm_smem_attr(pm_layer_dn_kernel<QR, QS>, smem_dn, &done_dn)) return 0;
-    dim3 dgrid(L.max_items, (a.H + a.dn_rows - 1) / a.dn_rows);
+    dim3 dgrid(L.max_work, (a.H + a.dn_rows - 1) / a.dn_rows);
     pm_layer_dn_kernel<QR, QS><<<dgrid, PM_THREADS, smem_dn, st>>>(a, dr, ds);
     if (!pm_ok(cudaGetLastError(), "moe layer down launch")) return 0;
     /* 6: combine */
@@ -571,6 +572,8 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.item_expert = (uint32_t *)(b + L.item_expert);
     a.item_start = (uint32_t *)(b + L.item_start);
     a.pairs = (uint32_t *)(b + L.pairs);
+    a.work_item = (uint32_t *)(b + L.work_item);
+    a.work_t0 = (uint32_t *)(b + L.work_t0);
     a.mid = (float *)(b + L.mid);
     a.midq = (pm_block_q8K *)(b + L.midq);
     a.partial = (float *)(b + L.partial);

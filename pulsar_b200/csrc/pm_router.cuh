@@ -42,13 +42,15 @@ __device__ __forceinline__ void pm_warp_argmax(const float *score, uint32_t lo, 
 __device__ __forceinline__ void pm_select_token(int32_t *selected, float *weights, const float *logits,
                                                 const float *bias, uint32_t n_expert, uint32_t k_used,
                                                 float weight_scale, uint32_t token, uint32_t mode, uint32_t n_shexp,
-                                                uint32_t n_group, uint32_t topk_group, float *score, float *prob) {
+                                                uint32_t n_group, uint32_t topk_group, float *score, float *prob,
+                                                uint32_t out_stride = 0) {
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t sink = mode == 2u ? n_shexp : 0u;
     const uint32_t n_logit = n_expert + sink, n_slot = k_used + sink;
+    const uint32_t stride = out_stride ? out_stride : n_slot; /* row stride of selected / weights */
     const float *lg = logits + (uint64_t)token * n_logit;
-    int32_t *sel = selected + (uint64_t)token * n_slot;
-    float *w = weights + (uint64_t)token * n_slot;
+    int32_t *sel = selected + (uint64_t)token * stride;
+    float *w = weights + (uint64_t)token * stride;
     for (uint32_t e = lane; e < n_expert; e += 32u) {
         const float raw = lg[e];
         const float p = mode == 1u ? raw : pm_sigmoid(raw);
@@ -91,12 +93,13 @@ __device__ __forceinline__ void pm_select_token(int32_t *selected, float *weight
         float bv;
         uint32_t bi;
         pm_warp_argmax(score, 0, n_expert, UINT32_MAX, bv, bi);
-        const float bp = prob[bi];
+        /* only NaN scores are left: the slot stays unrouted (-1, weight 0) */
+        const float bp = bi < n_expert ? prob[bi] : 0.0f;
         __syncwarp();
         if (lane == 0) {
-            sel[k] = (int32_t)bi;
+            sel[k] = bi < n_expert ? (int32_t)bi : -1;
             w[k] = bp;
-            score[bi] = -INFINITY;
+            if (bi < n_expert) score[bi] = -INFINITY;
         }
         sum = __fadd_rn(sum, bp);
         __syncwarp();
