@@ -138,20 +138,25 @@ class Runner:
         self.r = [torch.zeros((T, H), dtype=torch.float32, device=dev) for _ in range(2)]
         self.ws = torch.zeros(max(L.workspace_bytes(self.Tg) for L in stack), dtype=torch.uint8, device=dev)
         self.cur = torch.zeros((T, H), dtype=torch.float32, device=dev)
+        self.xn = torch.zeros((self.Tg, H), dtype=torch.float32, device=dev)
         self.graph = None
         self.stream = torch.cuda.Stream()
 
     def step_body(self):
+        """x -> per layer: x + moe(rms_norm(x)) -> cur (this rank's rows)"""
+        from pulsar_b200 import ops
         cur = self.x
         for L in self.stack:
             if self.world == 1:
                 nxt = self.h[0] if cur is not self.h[0] else self.h[1]
-                L.forward(cur, nxt, self.ws, residual=cur)
+                ops.rms_norm(self.xn, cur)
+                L.forward(self.xn, nxt, self.ws, residual=cur)
                 cur = nxt
             else:
                 import torch.distributed as dist
                 dist.all_gather_into_tensor(self.h[0], cur, group=self.group)
-                L.forward(self.h[0], self.part, self.ws)
+                ops.rms_norm(self.xn, self.h[0])
+                L.forward(self.xn, self.part, self.ws)
                 dist.reduce_scatter_tensor(self.rs, self.part, group=self.group)
                 nxt = self.r[0] if cur is not self.r[0] else self.r[1]
                 torch.add(self.rs, cur, out=nxt)
@@ -238,6 +243,7 @@ def profile_stages(runner: Runner, x_dev):
 
     from pulsar_b200 import lib
     from pulsar_b200._lib import check, ptr
+    from pulsar_b200 import ops
     st = runner.stream
     stage_ms = np.zeros(5)
     gu_bytes = layer_bytes = 0.0
@@ -247,12 +253,14 @@ def profile_stages(runner: Runner, x_dev):
     cur = runner.x
     for L in runner.stack:
         nxt = runner.h[0] if cur is not runner.h[0] else runner.h[1]
+        with torch.cuda.stream(st):
+            ops.rms_norm(runner.xn, cur)
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
         for e in evs:
             e.record(st)  # creates the event handle
         torch.cuda.synchronize()
         arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs])
-        check(lib().pulsar_moe_layer_profiled(ctypes.byref(L.desc()), ptr(nxt), ptr(cur), ptr(cur), runner.T,
+        check(lib().pulsar_moe_layer_profiled(ctypes.byref(L.desc()), ptr(nxt), ptr(runner.xn), ptr(cur), runner.T,
                                               ptr(runner.ws), runner.ws.numel(), st.cuda_stream, arr),
               "moe_layer_profiled")
         torch.cuda.synchronize()
@@ -286,7 +294,8 @@ def cpu_baseline(stack, T: int, x0: np.ndarray, threads: int, budget_s: float = 
         if not np.isfinite(x).all():
             raise RuntimeError(f"cpu baseline: non-finite hidden rows entering layer {done}")
         t0 = time.perf_counter()
-        lg = orc.router_logits(rw, x)
+        xn = (x / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6)).astype(np.float32)
+        lg = orc.router_logits(rw, xn)
         sel, w = orc.router_select(lg, sb, k, 1.0, 0)
         slots, ws = [], np.zeros((T, k + 1), np.float32)
         for t in range(T):
@@ -299,7 +308,7 @@ def cpu_baseline(stack, T: int, x0: np.ndarray, threads: int, budget_s: float = 
             ws[t, k] = 1.0
             row.append(dict(gate=sg, up=su, down=sd))
             slots.append(row)
-        out = orc.moe_ffn(x, slots, ws, H, k, (F, 2, rg, rd), (F, 2, rg, rd), n_threads=threads)
+        out = orc.moe_ffn(xn, slots, ws, H, k, (F, 2, rg, rd), (F, 2, rg, rd), n_threads=threads)
         x = (x + out).astype(np.float32)
         t_total += time.perf_counter() - t0
         done += 1
@@ -441,7 +450,7 @@ def main():
                 "config": config,
                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
-                "gpu_launches": 6 * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
+                "gpu_launches": 7 * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
                 "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
     if world > 1:
         import torch.distributed as dist

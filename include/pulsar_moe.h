@@ -109,6 +109,10 @@ int pulsar_add_bias_rows(void *x, const void *bias, uint32_t dim, uint32_t rows)
  * out[t][r] = W[r] . x[t] accumulated in binary64 in a fixed order */
 int pulsar_matmul_f32(void *out, const void *w, const void *x, uint32_t in_dim, uint32_t out_dim, uint32_t n_tok);
 
+/* replaces cu:6494 pulsar_rms_norm (klib:88): out = x / rms(x) * w per
+ * row (w may be NULL = ones); the normalisation ahead of an FFN layer */
+int pulsar_rms_norm(void *out, const void *x, const void *w, uint32_t n, uint32_t rows, float eps);
+
 /* replaces cu:6551 pulsar_swiglu (klib:111) */
 int pulsar_swiglu(void *out, const void *gate, const void *up, uint32_t n, float clamp, float weight,
                   uint32_t act_op);
@@ -166,6 +170,10 @@ typedef struct pulsar_moe_layer_desc {
     uint64_t shared_row_bytes_gu, shared_row_bytes_down;
     const void *shared_gate, *shared_up, *shared_down;
 } pulsar_moe_layer_desc;
+
+/* pulsar_rms_norm on an explicit stream (cudaStream_t, NULL = per-thread default) */
+int pulsar_rms_norm_stream(void *out, const void *x, const void *w, uint32_t n, uint32_t rows, float eps,
+                           void *stream);
 
 /* bytes of workspace pulsar_moe_layer needs for up to max_tok tokens */
 size_t pulsar_moe_layer_workspace(const pulsar_moe_layer_desc *d, uint32_t max_tok);

@@ -78,6 +78,8 @@ _SIGS = {
     "pulsar_matmul_f32": [_P, _P, _P, _U32, _U32, _U32],
     "pulsar_swiglu": [_P, _P, _P, _U32, _F, _F, _U32],
     "pulsar_add": [_P, _P, _P, _U32],
+    "pulsar_rms_norm": [_P, _P, _P, _U32, _U32, _F],
+    "pulsar_rms_norm_stream": [_P, _P, _P, _U32, _U32, _F, _P],
     "pulsar_router_logits_select": [_P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32, _U32, _U32, _P],
     "pulsar_moe_layer": [ctypes.POINTER(LayerDesc), _P, _P, _P, _U32, _P, ctypes.c_size_t, _P],
     "pulsar_moe_layer_profiled": [ctypes.POINTER(LayerDesc), _P, _P, _P, _U32, _P, ctypes.c_size_t, _P,

@@ -523,3 +523,44 @@ extern "C" uint32_t pulsar_b200_abi_error(void) {
     cudaMemcpyToSymbol(pm_err_word_abi, &z, 4);
     return v;
 }
+
+/* ============================================================ rms norm */
+
+/* out[r][i] = x[r][i] / sqrt(mean_i x[r][i]^2 + eps) * w[i] (w NULL = 1):
+ * the normalisation the engine applies to a layer's FFN input
+ * (cu:6469-6502 semantics).  One CTA per row, warp-shuffle reduction. */
+__global__ void pm_rms_norm_kernel(float *out, const float *x, const float *w, uint32_t n, float eps) {
+    __shared__ float part[32];
+    const float *xr = x + (uint64_t)blockIdx.x * n;
+    float *orow = out + (uint64_t)blockIdx.x * n;
+    float s = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) s += xr[i] * xr[i];
+    s = pm_warp_sum(s);
+    if ((threadIdx.x & 31u) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0f;
+        v = pm_warp_sum(v);
+        if (threadIdx.x == 0) part[0] = rsqrtf(v / (float)n + eps);
+    }
+    __syncthreads();
+    const float scale = part[0];
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) orow[i] = xr[i] * scale * (w ? w[i] : 1.0f);
+}
+
+/* replaces cu:6494 pulsar_rms_norm (klib:88) */
+extern "C" int pulsar_rms_norm(void *out_dev, const void *x_dev, const void *w_dev, uint32_t n, uint32_t rows,
+                               float eps) {
+    if (!out_dev || !x_dev || n == 0 || rows == 0) return 0;
+    pm_rms_norm_kernel<<<rows, 256>>>((float *)out_dev, (const float *)x_dev, (const float *)w_dev, n, eps);
+    return pm_ok(cudaGetLastError(), "rms norm launch");
+}
+
+/* the same on an explicit stream (cudaStream_t, NULL = per-thread default) */
+extern "C" int pulsar_rms_norm_stream(void *out_dev, const void *x_dev, const void *w_dev, uint32_t n, uint32_t rows,
+                                      float eps, void *stream) {
+    if (!out_dev || !x_dev || n == 0 || rows == 0) return 0;
+    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
+    pm_rms_norm_kernel<<<rows, 256, 0, st>>>((float *)out_dev, (const float *)x_dev, (const float *)w_dev, n, eps);
+    return pm_ok(cudaGetLastError(), "rms norm launch");
+}

@@ -17,7 +17,7 @@ from ._lib import ExpertPtrs, KernelError, Q8K_BLOCK_BYTES, check, lib, ptr
 __all__ = [
     "q8k_bytes", "expert_ptrs_tensor", "router_select", "quantize_q8_k", "moe_pair_swiglu", "moe_down",
     "moe_pair_swiglu_grouped", "moe_down_grouped", "moe_slot_sum", "moe_down_bias", "add_bias_rows",
-    "matmul_f32", "swiglu", "add", "router_logits_select", "quantize_rows", "KernelError",
+    "matmul_f32", "swiglu", "add", "rms_norm", "router_logits_select", "quantize_rows", "KernelError",
 ]
 
 
@@ -93,6 +93,12 @@ def swiglu(out, gate, up, n, clamp=0.0, weight=1.0, act_op=0):
 
 def add(out, a, b, n):
     check(lib().pulsar_add(ptr(out), ptr(a), ptr(b), n), "add")
+
+
+def rms_norm(out, x, w=None, eps=1e-6, stream=None):
+    rows, n = x.shape
+    s = torch.cuda.current_stream() if stream is None else stream
+    check(lib().pulsar_rms_norm_stream(ptr(out), ptr(x), ptr(w), n, rows, eps, s.cuda_stream), "rms_norm")
 
 
 def router_logits_select(selected, weights, logits, x, w, logit_bias, select_bias, in_dim, n_expert, k_used,
