@@ -58,8 +58,10 @@ class LayerDesc(ctypes.Structure):
 
 class WsView(ctypes.Structure):
     _fields_ = [("logits", ctypes.c_void_p), ("selected", ctypes.c_void_p), ("weights", ctypes.c_void_p),
-                ("xq", ctypes.c_void_p), ("mid", ctypes.c_void_p), ("midq", ctypes.c_void_p),
-                ("err", ctypes.c_void_p), ("n_items", ctypes.c_void_p), ("n_slot", ctypes.c_uint32),
+                ("xq", ctypes.c_void_p), ("mid", ctypes.c_void_p),
+                ("err", ctypes.c_void_p), ("n_items", ctypes.c_void_p), ("item_expert", ctypes.c_void_p),
+                ("item_start", ctypes.c_void_p), ("pairs", ctypes.c_void_p), ("work_item", ctypes.c_void_p),
+                ("work_t0", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("n_slot", ctypes.c_uint32),
                 ("f_max", ctypes.c_uint32)]
 
 

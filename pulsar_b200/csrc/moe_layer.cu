@@ -13,10 +13,10 @@
  *     id, pairs in (token, slot) order) and appends the shared experts
  *   4 gate/up: one CTA per (expert work item, row tile) streams the
  *     expert's rows once through a TMA ring and serves every token routed
- *     to it; glu * route weight -> mid.  The last tile CTA of each 256-row
- *     block quantizes that block of every pair's mid row to q8_K.
+ *     to it; glu * route weight -> mid (f32)
  *   5 down: one CTA per (expert work item, tile of output rows), the same
- *     engine, writing one partial row per (token, slot)
+ *     engine; it quantizes its tokens' mid rows to q8_K (CPU-lane math)
+ *     while staging them and writes one partial row per (token, slot)
  *   6 combine: per (token, row) the partials in slot order, + the down
  *     bias (sum_s w_s b_s, cu:3601) + the residual (deterministic)
  * Both expert kernels stage each token tile's q8_K rows in shared memory
@@ -49,7 +49,7 @@ __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
     uint32_t max_work;
-    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, pairs, mid, midq, partial, cnt,
+    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, pairs, mid, partial,
         sel_done, err, total;
 };
 
@@ -83,9 +83,7 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.work_t0 = o, o = pm_al(o + (size_t)L.max_work * 4);
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
-    L.midq = o, o = pm_al(o + (size_t)T * L.n_slot * L.fb * PM_Q8_K_BYTES);
     L.partial = o, o = pm_al(o + (size_t)T * L.n_slot * L.H * 4);
-    L.cnt = o, o = pm_al(o + (size_t)L.max_items * L.fb * 4);
     L.sel_done = o, o = pm_al(o + 4);
     L.err = o, o = pm_al(o + 4);
     L.total = o;
@@ -110,9 +108,8 @@ struct pm_layer_args {
     uint32_t *item_expert, *item_start, *pairs;
     uint32_t *work_item, *work_t0; /* work unit = (item, first token of its chunk of <= PM_TT) */
     float *mid;
-    pm_block_q8K *midq;
     float *partial; /* [T * n_slot][H] down outputs before the combine */
-    uint32_t *cnt, *sel_done, *err;
+    uint32_t *sel_done, *err;
     /* io */
     float *out;
     const float *residual;
@@ -135,11 +132,9 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
             a.w[token * a.n_slot + a.k + lane] = 1.0f;
         }
     }
+    __threadfence(); /* every thread publishes its own selection writes */
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        is_last = atomicAdd(a.sel_done, 1u) == gridDim.x - 1u;
-    }
+    if (threadIdx.x == 0) is_last = atomicAdd(a.sel_done, 1u) == gridDim.x - 1u;
     __syncthreads();
     if (!is_last) return;
     __threadfence();
@@ -229,12 +224,13 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
         a.n_items[2] = tot_work + n_sh * sh_chunks;
         *a.sel_done = 0;
     }
-    for (uint32_t i = threadIdx.x; i < a.max_items * a.fb; i += blockDim.x) a.cnt[i] = 0;
 }
 
 /* ====================================================== 4: gate / up */
 
 struct pm_seg_gu2 {
+    static constexpr bool F32 = false;
+    uint32_t n_f32;
     const uint8_t *g, *u;
     const uint32_t *pairs;
     uint32_t n, row0;
@@ -254,18 +250,29 @@ struct pm_seg_gu2 {
     }
 };
 
-/* geometry of one engine pass, computed on the host */
-struct pm_pass {
-    uint32_t S, stage, rc, lpr, ring_bytes, act_off;
-};
+/* the IQ2_XXS magnitude grid, expanded into shared memory (all threads) */
+__device__ __forceinline__ const uint64_t *pm_grid_fill(uint8_t *smem, bool need) {
+    uint64_t *g = (uint64_t *)smem;
+    if (need)
+        for (uint32_t i = threadIdx.x; i < 256; i += blockDim.x) {
+            const uint32_t k = pm_kgrid_layer[i];
+            uint64_t v = 0;
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const uint32_t d = (k >> (2 * q)) & 3u;
+                v |= (uint64_t)(d == 0 ? 8u : (d == 1 ? 25u : 43u)) << (8 * q);
+            }
+            g[i] = v;
+        }
+    return g; /* the first __syncthreads of the engine publishes it */
+}
 
 template <int Q>
 __device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t t0, uint32_t e,
                                  uint32_t row0, uint32_t nrows, const pm_pass &ps) {
     const bool routed = e < a.E;
     const uint64_t rb = routed ? a.rb_gu_r : a.rb_gu_s;
-    uint64_t *grid;
-    pm_ring ring = pm_ring_setup(smem, ps.S, ps.stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
+    const uint64_t *grid = pm_grid_fill(smem, Q == PM_QUANT_IQ2_XXS);
     pm_seg_gu2 seg;
     seg.g = (routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate) + (uint64_t)row0 * rb;
     seg.u = (routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup) + (uint64_t)row0 * rb;
@@ -276,16 +283,13 @@ __device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t
     seg.a = &a;
     seg.gb = routed && a.gate_b ? a.gate_b + (uint64_t)e * a.Fr : nullptr;
     seg.ub = routed && a.up_b ? a.up_b + (uint64_t)e * a.Fr : nullptr;
-    const pm_block_q8K **tokrows = (const pm_block_q8K **)(smem + ps.act_off - 128);
-    return pm_gemv_tile<Q, 2, PM_TT>(seg, ring, smem + ps.act_off, tokrows, nrows, ps.rc, rb, a.H / 32u, ps.lpr,
-                                     grid, a.err);
+    return pm_gemv_warps<Q, 2, PM_TT>(seg, smem, ps, nrows, rb, a.H / 32u, grid, a.err);
 }
 
 template <int QR, int QS>
-__global__ void __launch_bounds__(PM_THREADS)
+__global__ void __launch_bounds__(PM_THREADS, 2)
     pm_layer_gu_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint32_t last;
     const uint32_t wk = blockIdx.x;
     if (wk >= __ldcg(a.n_items + 2)) return;
     const uint32_t item = __ldcg(a.work_item + wk), t0 = __ldcg(a.work_t0 + wk);
@@ -297,49 +301,23 @@ __global__ void __launch_bounds__(PM_THREADS)
     const uint32_t nrows = F - row0 < a.gu_rows ? F - row0 : a.gu_rows;
     const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, t0, e, row0, nrows, pr)
                            : pm_layer_gu_item<QS>(a, smem, item, t0, e, row0, nrows, psh);
-    if (!ok) return;
-    /* the last (tile, token chunk) CTA of each 256-row block quantizes that
-     * block of every pair's mid row */
-    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
-    const uint32_t fb = row0 / 256u;
-    const uint32_t blk_rows = F - fb * 256u < 256u ? F - fb * 256u : 256u;
-    const uint32_t tiles = (blk_rows + a.gu_rows - 1) / a.gu_rows * ((s1 - s0 + PM_TT - 1) / PM_TT);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        last = atomicAdd(a.cnt + (uint64_t)item * a.fb + fb, 1u) == tiles - 1u;
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    const uint32_t lane = threadIdx.x & 31u;
-    float *stage_v = (float *)smem + (threadIdx.x >> 5) * 256u;
-    for (uint32_t i = s0 + (threadIdx.x >> 5); i < s1; i += PM_WARPS) {
-        const uint32_t p = __ldcg(a.pairs + i);
-        const float *src = a.mid + (uint64_t)p * a.Fmax + fb * 256u;
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-            const uint32_t el = lane * 8u + q;
-            stage_v[el] = el < blk_rows ? __ldcg(src + el) : 0.0f; /* written by other CTAs: read via L2 */
-        }
-        __syncwarp();
-        pm_q8k_warp(stage_v, blk_rows, a.midq + (uint64_t)p * a.fb + fb);
-        __syncwarp();
-    }
+    if (ok) return;
+    (void)ok; /* a timeout is recorded in the error word; the layer output is then undefined */
 }
 
 /* ======================================================= 5: down */
 
 struct pm_seg_dn2 {
+    static constexpr bool F32 = true; /* mid rows are quantized to q8_K while staging */
+    uint32_t n_f32;
     const uint8_t *d;
     const uint32_t *pairs;
     uint32_t n, row0;
     const pm_layer_args *a;
     __device__ const uint8_t *base(int) const { return d; }
     __device__ uint32_t ntok() const { return n; }
-    __device__ const pm_block_q8K *tok(uint32_t ti) const {
-        return a->midq + (uint64_t)__ldcg(pairs + ti) * a->fb;
-    }
+    __device__ const pm_block_q8K *tok(uint32_t) const { return nullptr; }
+    __device__ const float *tok_f32(uint32_t ti) const { return a->mid + (uint64_t)__ldcg(pairs + ti) * a->Fmax; }
     __device__ void epi(uint32_t row, uint32_t ti, const float *v) const {
         a->partial[(uint64_t)__ldcg(pairs + ti) * a->H + row0 + row] = v[0];
     }
@@ -350,8 +328,7 @@ __device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t
                                  uint32_t row0, uint32_t nrows, const pm_pass &ps) {
     const bool routed = e < a.E;
     const uint64_t rb = routed ? a.rb_dn_r : a.rb_dn_s;
-    uint64_t *grid;
-    pm_ring ring = pm_ring_setup(smem, ps.S, ps.stage, Q == PM_QUANT_IQ2_XXS, pm_kgrid_layer, &grid);
+    const uint64_t *grid = pm_grid_fill(smem, Q == PM_QUANT_IQ2_XXS);
     pm_seg_dn2 seg;
     seg.d = (routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown) + (uint64_t)row0 * rb;
     const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
@@ -360,13 +337,12 @@ __device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t
     seg.row0 = row0;
     seg.a = &a;
     const uint32_t F = routed ? a.Fr : a.Fs;
-    const pm_block_q8K **tokrows = (const pm_block_q8K **)(smem + ps.act_off - 128);
-    pm_gemv_tile<Q, 1, PM_TT>(seg, ring, smem + ps.act_off, tokrows, nrows, ps.rc, rb, (F + 31u) / 32u, ps.lpr,
-                              grid, a.err);
+    seg.n_f32 = F;
+    pm_gemv_warps<Q, 1, PM_TT>(seg, smem, ps, nrows, rb, (F + 31u) / 32u, grid, a.err);
 }
 
 template <int QR, int QS>
-__global__ void __launch_bounds__(PM_THREADS)
+__global__ void __launch_bounds__(PM_THREADS, 2)
     pm_layer_dn_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t wk = blockIdx.x;
@@ -442,9 +418,14 @@ extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t
     v->weights = (float *)(b + L.w);
     v->xq = b + L.xq;
     v->mid = (float *)(b + L.mid);
-    v->midq = b + L.midq;
     v->err = (uint32_t *)(b + L.err);
     v->n_items = (uint32_t *)(b + L.n_items);
+    v->item_expert = (uint32_t *)(b + L.item_expert);
+    v->item_start = (uint32_t *)(b + L.item_start);
+    v->pairs = (uint32_t *)(b + L.pairs);
+    v->work_item = (uint32_t *)(b + L.work_item);
+    v->work_t0 = (uint32_t *)(b + L.work_t0);
+    v->partial = (float *)(b + L.partial);
     v->n_slot = L.n_slot;
     v->f_max = L.Fmax;
     return 1;
@@ -457,31 +438,32 @@ static uint32_t pm_pow2_rows(uint64_t nrows_total, uint64_t ctas_other, uint32_t
     return r;
 }
 
-/* pass geometry: ring chunks of at least one row per warp slot and about
- * 16 KB, as many stages as the shared-memory budget left by the token tile
- * allows (two CTAs per SM) */
+/* pass geometry: lanes per row (one lane per pair of units), rows per
+ * stage (~6 KB, whole passes of the warp), per-warp ring depth within a
+ * ~100 KB budget (two CTAs per SM), and the shared-memory layout */
 static pm_pass pm_pass_for(uint32_t nmat, uint64_t rb, uint32_t n_units, uint32_t rows_cta, bool grid) {
     pm_pass p;
-    p.lpr = n_units >= 32 ? 32u : (n_units >= 16 ? 16u : 8u);
-    const uint32_t step = PM_WARPS * (32u / p.lpr);
-    uint64_t rc = 16384u / (nmat * rb);
-    if (rc < step) rc = step;
-    rc = (rc / step) * step;
-    if (rc > rows_cta) rc = rows_cta;
-    while (rows_cta % rc) rc--;
-    p.rc = (uint32_t)rc;
-    p.stage = pm_stage_bytes(nmat, rb, p.rc);
-    const uint32_t acts = pm_acts_bytes(PM_TT, n_units);
-    const uint32_t budget = 110u * 1024u;
-    const uint32_t fixed = pm_ring_offset(grid) + acts + 128u;
-    const uint32_t S = budget > fixed + 2 * p.stage ? (budget - fixed) / p.stage : 2u;
+    const uint32_t pairs = (n_units + 1) / 2;
+    p.lpr = pairs >= 32 ? 32u : (pairs >= 16 ? 16u : (pairs >= 8 ? 8u : (pairs >= 4 ? 4u : 2u)));
+    const uint32_t rpp = 32u / p.lpr;
+    uint64_t rw = 6144u / (nmat * rb);
+    rw = (rw / rpp) * rpp;
+    if (rw < rpp) rw = rpp;
+    const uint32_t per_warp = (rows_cta + PM_WARPS - 1) / PM_WARPS;
+    if (rw > per_warp) rw = ((per_warp + rpp - 1) / rpp) * rpp;
+    p.rw = (uint32_t)rw;
+    p.stage = pm_stage_bytes(nmat, rb, p.rw);
+    p.off_bar = grid ? 2048u : 0u;
+    p.off_tok = p.off_bar + 512u;
+    p.off_acts = p.off_tok + 128u;
+    const uint32_t ring0 = (p.off_acts + pm_acts_bytes(PM_TT, n_units) + 127u) & ~127u;
+    const uint32_t budget = 100u * 1024u;
+    uint32_t S = budget > ring0 ? (budget - ring0) / (PM_WARPS * p.stage) : 2u;
     p.S = S < 2 ? 2 : (S > 8 ? 8 : S);
-    p.ring_bytes = (pm_ring_offset(grid) + p.S * p.stage + 15u) & ~15u;
-    p.act_off = p.ring_bytes + 128u; /* 128 bytes of token-row pointers precede the planes */
+    p.off_ring = ring0;
+    p.smem = ring0 + PM_WARPS * p.S * p.stage;
     return p;
 }
-
-static uint32_t pm_pass_smem(const pm_pass &p, uint32_t n_units) { return p.act_off + pm_acts_bytes(PM_TT, n_units); }
 
 static inline void pm_ev(void *const *ev, int i, cudaStream_t st) {
     if (ev && ev[i]) cudaEventRecord((cudaEvent_t)ev[i], st);
@@ -494,8 +476,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     const uint32_t hu = a.H / 32u;
     const pm_pass gr = pm_pass_for(2, a.rb_gu_r, hu, a.gu_rows, QR == PM_QUANT_IQ2_XXS);
     const pm_pass gs = a.S ? pm_pass_for(2, a.rb_gu_s, hu, a.gu_rows, QS == PM_QUANT_IQ2_XXS) : gr;
-    uint32_t smem_gu = pm_pass_smem(gr, hu) > pm_pass_smem(gs, hu) ? pm_pass_smem(gr, hu) : pm_pass_smem(gs, hu);
-    if (smem_gu < PM_WARPS * 1024u) smem_gu = PM_WARPS * 1024u;
+    uint32_t smem_gu = gr.smem > gs.smem ? gr.smem : gs.smem;
     if (!pm_smem_attr(pm_layer_gu_kernel<QR, QS>, smem_gu, &done_gu)) return 0;
     dim3 ggrid(L.max_work, (L.Fmax + a.gu_rows - 1) / a.gu_rows);
     pm_layer_gu_kernel<QR, QS><<<ggrid, PM_THREADS, smem_gu, st>>>(a, gr, gs);
@@ -505,7 +486,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     const uint32_t fr = (a.Fr + 31u) / 32u, fs = a.S ? (a.Fs + 31u) / 32u : fr;
     const pm_pass dr = pm_pass_for(1, a.rb_dn_r, fr, a.dn_rows, QR == PM_QUANT_IQ2_XXS);
     const pm_pass ds = a.S ? pm_pass_for(1, a.rb_dn_s, fs, a.dn_rows, QS == PM_QUANT_IQ2_XXS) : dr;
-    const uint32_t smem_dn = pm_pass_smem(dr, fr) > pm_pass_smem(ds, fs) ? pm_pass_smem(dr, fr) : pm_pass_smem(ds, fs);
+    const uint32_t smem_dn = dr.smem > ds.smem ? dr.smem : ds.smem;
     if (!pm_smem_attr(pm_layer_dn_kernel<QR, QS>, smem_dn, &done_dn)) return 0;
     dim3 dgrid(L.max_work, (a.H + a.dn_rows - 1) / a.dn_rows);
     pm_layer_dn_kernel<QR, QS><<<dgrid, PM_THREADS, smem_dn, st>>>(a, dr, ds);
@@ -575,14 +556,12 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.work_item = (uint32_t *)(b + L.work_item);
     a.work_t0 = (uint32_t *)(b + L.work_t0);
     a.mid = (float *)(b + L.mid);
-    a.midq = (pm_block_q8K *)(b + L.midq);
     a.partial = (float *)(b + L.partial);
-    a.cnt = (uint32_t *)(b + L.cnt);
     a.sel_done = (uint32_t *)(b + L.sel_done);
     a.err = (uint32_t *)(b + L.err);
     a.out = out;
     a.residual = residual;
-    a.gu_rows = pm_pow2_rows(L.Fmax, L.max_items, 8, 128);
+    a.gu_rows = pm_pow2_rows(L.Fmax, L.max_items, 8, 256);
     a.dn_rows = pm_pow2_rows(L.H, L.max_items, 16, 512);
 
     /* 1, 2: logits and q8_K(x) */

@@ -82,6 +82,38 @@ __device__ __forceinline__ bool pm_mbar_wait(uint64_t *bar, uint32_t parity, uin
     return true;
 }
 
+/* try_wait that may suspend the thread up to ~1 us instead of spinning */
+__device__ __forceinline__ bool pm_mbar_try_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(pm_smem_addr(bar)), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+
+/* bounded wait with suspension; false (and err |= TIMEOUT) on timeout */
+__device__ __forceinline__ bool pm_mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t *err) {
+    if (pm_mbar_try_sleep(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!pm_mbar_try_sleep(bar, parity)) {
+        if (clock64() - t0 > PM_WAIT_CYCLES) {
+            if (err) atomicOr(err, PM_ERR_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+/* order this thread's generic-proxy shared accesses before later
+ * async-proxy (TMA) writes to the same shared memory */
+__device__ __forceinline__ void pm_fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 /* ------------------------------------------------------ byte access */
 
 /* 4-byte little-endian word at any byte alignment in shared memory */

@@ -138,137 +138,264 @@ __device__ __forceinline__ void pm_acts_stage(const pm_acts &a, uint32_t nt, con
     }
 }
 
-/* Segment interface for pm_gemv_tile:
- *   const uint8_t* base(m)                 first row of the CTA's tile in matrix m
- *   uint32_t ntok()                         tokens of the item
- *   const pm_block_q8K* tok(ti)             q8_K row of token ti
- *   void epi(row, ti, const float* v)       one lane per (row, token) */
-template <int Q, int NMAT, int TT, class Seg>
-__device__ bool pm_gemv_tile(Seg &seg, const pm_ring &ring, uint8_t *act_smem, const pm_block_q8K **tokrows,
-                             uint32_t nrows, uint32_t rc, uint64_t rb, uint32_t n_units, uint32_t lpr,
-                             const uint64_t *grid, uint32_t *err) {
-    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    const uint32_t n = seg.ntok();
-    const uint32_t cps = (nrows + rc - 1) / rc;
-    const pm_acts acts = pm_acts_carve(act_smem, TT, n_units);
-    const uint32_t rows_per_warp = 32u / lpr;
-    const uint32_t sub = lane / lpr, sl = lane % lpr; /* row slot in the warp, lane in the row */
-    uint32_t issued = 0; /* chunks issued across token tiles (ring position) */
-    for (uint32_t t0 = 0; t0 < n; t0 += TT) {
-        const uint32_t nt = n - t0 < TT ? n - t0 : TT;
-        if (tid < nt) tokrows[tid] = seg.tok(t0 + tid);
-        __syncthreads();
-        pm_acts_stage(acts, nt, tokrows);
-        const uint32_t base_c = issued;
-        if (tid == 0) {
-            const uint32_t pro = cps < ring.S - 1 ? cps : ring.S - 1;
-            for (uint32_t c = 0; c < pro; c++) {
-                const uint8_t *src[NMAT];
-                const uint32_t r0 = c * rc, rows = nrows - r0 < rc ? nrows - r0 : rc;
+/* shared-memory layout of one engine pass (computed on the host) */
+struct pm_pass {
+    uint32_t S;        /* ring stages per warp */
+    uint32_t rw;       /* rows per stage */
+    uint32_t stage;    /* bytes per stage */
+    uint32_t lpr;      /* lanes per row (one lane per pair of units) */
+    uint32_t off_bar;  /* PM_WARPS * S mbarriers */
+    uint32_t off_acts; /* token-tile planes */
+    uint32_t off_tok;  /* TT token-row pointers */
+    uint32_t off_ring; /* PM_WARPS rings of S stages */
+    uint32_t smem;     /* total dynamic shared memory */
+};
+
+/* copy one stage (rows of NMAT matrices) with 1-D bulk copies: each piece
+ * is rounded out to 16-byte boundaries, so the staged byte at global
+ * address g sits at dst + off(m) + (g & 15); returns expected bytes */
+template <int NMAT>
+__device__ __forceinline__ void pm_issue_stage(uint8_t *dst, uint64_t *bar, const uint8_t *const *src,
+                                               uint32_t bytes) {
+    uint32_t total = 0, len[NMAT];
+    const uint8_t *lo[NMAT];
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) src[m] = seg.base(m) + (size_t)r0 * rb;
-                pm_issue_chunk<NMAT>(ring, base_c + c, src, rows * (uint32_t)rb);
-            }
+    for (int m = 0; m < NMAT; m++) {
+        const uintptr_t s0 = (uintptr_t)src[m];
+        lo[m] = (const uint8_t *)(s0 & ~(uintptr_t)15);
+        len[m] = (uint32_t)(((s0 + bytes + 15u) & ~(uintptr_t)15) - (s0 & ~(uintptr_t)15));
+        total += len[m];
+    }
+    pm_mbar_expect_tx(bar, total);
+    uint32_t off = 0;
+#pragma unroll
+    for (int m = 0; m < NMAT; m++) {
+        pm_bulk_g2s(dst + off, lo[m], len[m], bar);
+        off += len[m] + 16u;
+    }
+}
+
+template <int NMAT>
+__device__ __forceinline__ const uint8_t *pm_stage_ptr(const uint8_t *dst, const uint8_t *const *src, uint32_t bytes,
+                                                      int m) {
+    uint32_t off = 0;
+#pragma unroll
+    for (int i = 0; i < NMAT; i++) {
+        if (i == m) break;
+        const uintptr_t s0 = (uintptr_t)src[i];
+        off += (uint32_t)(((s0 + bytes + 15u) & ~(uintptr_t)15) - (s0 & ~(uintptr_t)15)) + 16u;
+    }
+    return dst + off + ((uintptr_t)src[m] & 15u);
+}
+
+/* quantize nt f32 rows of `n` values to q8_K (CPU-lane math, as
+ * pm_q8k_warp) straight into the planes: one warp per (token, 256-block);
+ * a lane holds 8 consecutive values = a quarter of one 32-value unit */
+__device__ __forceinline__ void pm_acts_stage_f32(const pm_acts &a, uint32_t nt, const float *const *rows,
+                                                  uint32_t n) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (uint32_t job = warp; job < nt * a.nblk; job += nw) {
+        const uint32_t ti = job / a.nblk, b = job % a.nblk;
+        const float *src = rows[ti] + (size_t)b * 256u;
+        const uint32_t valid = n - b * 256u < 256u ? n - b * 256u : 256u;
+        float v[8], amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t e = lane * 8u + (uint32_t)i;
+            v[i] = e < valid ? __ldcg(src + e) : 0.0f;
+            amax = fmaxf(amax, fabsf(v[i]));
         }
-        __syncthreads();
-        for (uint32_t c = 0; c < cps; c++) {
-            const uint32_t gc = base_c + c;
-            if (tid == 0 && c + ring.S - 1 < cps) {
-                const uint8_t *src[NMAT];
-                const uint32_t cc = c + ring.S - 1;
-                const uint32_t r0 = cc * rc, rows = nrows - r0 < rc ? nrows - r0 : rc;
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) src[m] = seg.base(m) + (size_t)r0 * rb;
-                pm_issue_chunk<NMAT>(ring, base_c + cc, src, rows * (uint32_t)rb);
+        for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        uint32_t qv[8];
+        int s = 0;
+        const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float r = amax == 0.0f ? 0.0f : roundf(__fmul_rn(v[i], inv));
+            r = fminf(fmaxf(r, -127.0f), 127.0f);
+            const int qi = (int)r;
+            s += qi;
+            qv[i] = (uint32_t)(uint8_t)(int8_t)qi;
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 1);    /* 16-value group sum (lane pair) */
+        const int s_hi = __shfl_down_sync(0xffffffffu, s, 2); /* the unit's second group */
+        const uint32_t u = b * 8u + (lane >> 2);
+        if (u < a.n_units) {
+            const uint32_t q = lane & 3u; /* quarter of the unit */
+            uint32_t *dst = (uint32_t *)(q < 2 ? a.lo + ti * a.n_units + u : a.hi + ti * a.n_units + u);
+            dst[(q & 1u) * 2u] = qv[0] | (qv[1] << 8) | (qv[2] << 16) | (qv[3] << 24);
+            dst[(q & 1u) * 2u + 1u] = qv[4] | (qv[5] << 8) | (qv[6] << 16) | (qv[7] << 24);
+            if (q == 0)
+                a.bs[ti * a.n_units + u] = (int32_t)((uint32_t)(uint16_t)(int16_t)s | ((uint32_t)(uint16_t)(int16_t)s_hi << 16));
+        }
+        if (lane == 0) a.d[ti * a.nblk + b] = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
+    }
+}
+
+/* Segment interface for pm_gemv_warps:
+ *   const uint8_t* base(m)                 first row of the CTA's tile in matrix m
+ *   uint32_t ntok()                         tokens of the work unit (<= TT)
+ *   const pm_block_q8K* tok(ti)             q8_K row of token ti, or
+ *   const float* tok_f32(ti)                its f32 row (Seg::F32 true: quantized while staging)
+ *   void epi(row, ti, const float* v)       one lane per (row, token)
+ *
+ * Warp-private pipelines: after the token tile is staged (one CTA barrier),
+ * warp w owns stages c = w, w + 8, ... of rw rows each and streams them
+ * through its own S-deep ring and mbarriers; there is no CTA-wide
+ * synchronisation while rows stream, so a warp waiting on memory never
+ * holds the others back.  Returns false on a wait timeout (err set). */
+template <int Q, int NMAT, int TT, class Seg>
+__device__ bool pm_gemv_warps(Seg &seg, uint8_t *smem, const pm_pass &ps, uint32_t nrows, uint64_t rb,
+                              uint32_t n_units, const uint64_t *grid, uint32_t *err) {
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint32_t nt = seg.ntok() < (uint32_t)TT ? seg.ntok() : (uint32_t)TT;
+    const pm_block_q8K **tokrows = (const pm_block_q8K **)(smem + ps.off_tok);
+    uint64_t *bars = (uint64_t *)(smem + ps.off_bar) + warp * ps.S;
+    uint8_t *ring = smem + ps.off_ring + (size_t)warp * ps.S * ps.stage;
+    const pm_acts acts = pm_acts_carve(smem + ps.off_acts, TT, n_units);
+    if constexpr (Seg::F32) {
+        if (tid < nt) ((const float **)tokrows)[tid] = seg.tok_f32(tid);
+    } else {
+        if (tid < nt) tokrows[tid] = seg.tok(tid);
+    }
+    if (lane == 0) {
+        for (uint32_t i = 0; i < ps.S; i++) pm_mbar_init(bars + i, 1);
+        pm_fence_barrier_init();
+    }
+    __syncthreads();
+    if constexpr (Seg::F32)
+        pm_acts_stage_f32(acts, nt, (const float *const *)tokrows, seg.n_f32);
+    else
+        pm_acts_stage(acts, nt, tokrows);
+    __syncthreads();
+
+    const uint32_t rw = ps.rw, lpr = ps.lpr;
+    const uint32_t n_stage_all = (nrows + rw - 1) / rw;
+    const uint32_t mine = n_stage_all > warp ? (n_stage_all - warp + PM_WARPS - 1) / PM_WARPS : 0u;
+    const uint32_t rows_per_pass = 32u / lpr;
+    const uint32_t sub = lane / lpr, sl = lane % lpr;
+
+    auto geom = [&](uint32_t i, const uint8_t **src, uint32_t &r0, uint32_t &rows) {
+        r0 = (warp + PM_WARPS * i) * rw;
+        rows = nrows - r0 < rw ? nrows - r0 : rw;
+#pragma unroll
+        for (int m = 0; m < NMAT; m++) src[m] = seg.base(m) + (size_t)r0 * rb;
+    };
+    if (lane == 0) {
+        const uint32_t pro = mine < ps.S ? mine : ps.S;
+        for (uint32_t i = 0; i < pro; i++) {
+            const uint8_t *src[NMAT];
+            uint32_t r0, rows;
+            geom(i, src, r0, rows);
+            pm_issue_stage<NMAT>(ring + (size_t)i * ps.stage, bars + i, src, rows * (uint32_t)rb);
+        }
+    }
+    bool ok = true;
+    for (uint32_t i = 0; i < mine; i++) {
+        const uint32_t st = i % ps.S;
+        if (!pm_mbar_wait_sleep(bars + st, (i / ps.S) & 1u, err)) {
+            ok = false;
+            if (lane == 0) { /* drain this warp's copies still in flight */
+                const uint32_t last = i + ps.S - 1 < mine ? i + ps.S - 1 : mine - 1;
+                for (uint32_t d = i; d <= last; d++) pm_mbar_wait(bars + (d % ps.S), (d / ps.S) & 1u, nullptr);
             }
-            const bool ok = pm_mbar_wait(ring.full + (gc % ring.S), (gc / ring.S) & 1u, err);
-            if (__syncthreads_or(!ok)) {
-                if (tid == 0) {
-                    const uint32_t last = c + ring.S - 1 < cps ? c + ring.S - 1 : cps - 1;
-                    for (uint32_t d = c; d <= last; d++)
-                        pm_mbar_wait(ring.full + ((base_c + d) % ring.S), ((base_c + d) / ring.S) & 1u, nullptr);
-                }
-                __syncthreads();
-                return false;
-            }
-            const uint32_t r0 = c * rc, rows = nrows - r0 < rc ? nrows - r0 : rc;
-            const uint8_t *rowp[NMAT];
-            {
-                const uint8_t *src[NMAT];
+            break;
+        }
+        const uint8_t *src[NMAT];
+        uint32_t r0, rows;
+        geom(i, src, r0, rows);
+        const uint8_t *stg = ring + (size_t)st * ps.stage;
+        const uint8_t *rowp[NMAT];
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) src[m] = seg.base(m) + (size_t)r0 * rb;
+        for (int m = 0; m < NMAT; m++) rowp[m] = pm_stage_ptr<NMAT>(stg, src, rows * (uint32_t)rb, m);
+        for (uint32_t jb = 0; jb < rows; jb += rows_per_pass) {
+            const uint32_t j = jb + sub;
+            const bool rv = j < rows;
+            float acc[NMAT][TT];
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) rowp[m] = pm_chunk_ptr<NMAT>(ring, gc, src, rows * (uint32_t)rb, m);
-            }
-            for (uint32_t jb = warp * rows_per_warp; jb < rows; jb += PM_WARPS * rows_per_warp) {
-                const uint32_t j = jb + sub;
-                const bool rv = j < rows;
-                float acc[NMAT][TT];
+            for (int m = 0; m < NMAT; m++)
 #pragma unroll
-                for (int m = 0; m < NMAT; m++)
+                for (int t = 0; t < TT; t++) acc[m][t] = 0.0f;
+            if (rv) {
+                /* a lane takes a PAIR of adjacent units (same super-block:
+                 * header and packed bytes load once for both) */
+                for (uint32_t u0 = 2u * sl; u0 < n_units; u0 += 2u * lpr) {
+                    const bool two = u0 + 1 < n_units;
+                    pm_wunit wu[NMAT][2];
 #pragma unroll
-                    for (int t = 0; t < TT; t++) acc[m][t] = 0.0f;
-                if (rv) {
-                    for (uint32_t u = sl; u < n_units; u += lpr) {
+                    for (int m = 0; m < NMAT; m++) {
+                        pm_decode<Q>(rowp[m] + (size_t)j * rb, u0, grid, wu[m][0]);
+                        if (two) pm_decode<Q>(rowp[m] + (size_t)j * rb, u0 + 1, grid, wu[m][1]);
+                    }
 #pragma unroll
-                        for (int m = 0; m < NMAT; m++) {
-                            pm_wunit wu;
-                            pm_decode<Q>(rowp[m] + (size_t)j * rb, u, grid, wu);
+                    for (int t = 0; t < TT; t++) {
+                        if (t < (int)nt) {
+                            const float yd = acts.d[t * acts.nblk + (u0 >> 3)];
 #pragma unroll
-                            for (int t = 0; t < TT; t++) {
-                                if (t < (int)nt) {
-                                    const uint4 lo = acts.lo[t * n_units + u], hi = acts.hi[t * n_units + u];
-                                    int s = __dp4a(wu.w[0], (int)lo.x, 0);
-                                    s = __dp4a(wu.w[1], (int)lo.y, s);
-                                    s = __dp4a(wu.w[2], (int)lo.z, s);
-                                    s = __dp4a(wu.w[3], (int)lo.w, s);
-                                    s = __dp4a(wu.w[4], (int)hi.x, s);
-                                    s = __dp4a(wu.w[5], (int)hi.y, s);
-                                    s = __dp4a(wu.w[6], (int)hi.z, s);
-                                    s = __dp4a(wu.w[7], (int)hi.w, s);
-                                    const float yd = acts.d[t * acts.nblk + (u >> 3)];
-                                    float cv = wu.A * (float)s;
+                            for (int h = 0; h < 2; h++) {
+                                if (h == 1 && !two) break;
+                                const uint32_t u = u0 + h;
+                                const uint4 lo = acts.lo[t * n_units + u], hi = acts.hi[t * n_units + u];
+                                int32_t bp = 0;
+                                if (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bp = acts.bs[t * n_units + u];
+#pragma unroll
+                                for (int m = 0; m < NMAT; m++) {
+                                    const pm_wunit &wv = wu[m][h];
+                                    int s0 = __dp4a(wv.w[0], (int)lo.x, 0);
+                                    int s1 = __dp4a(wv.w[4], (int)hi.x, 0);
+                                    s0 = __dp4a(wv.w[1], (int)lo.y, s0);
+                                    s1 = __dp4a(wv.w[5], (int)hi.y, s1);
+                                    s0 = __dp4a(wv.w[2], (int)lo.z, s0);
+                                    s1 = __dp4a(wv.w[6], (int)hi.z, s1);
+                                    s0 = __dp4a(wv.w[3], (int)lo.w, s0);
+                                    s1 = __dp4a(wv.w[7], (int)hi.w, s1);
+                                    float cv = wv.A * (float)(s0 + s1);
                                     if (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) {
-                                        const int32_t bp = acts.bs[t * n_units + u];
-                                        const int32_t msum = wu.ma * (int32_t)(int16_t)(bp & 0xffff) +
-                                                             wu.mb * (int32_t)(int16_t)((uint32_t)bp >> 16);
-                                        cv -= wu.B * (float)msum;
+                                        const int32_t msum = wv.ma * (int32_t)(int16_t)(bp & 0xffff) +
+                                                             wv.mb * (int32_t)(int16_t)((uint32_t)bp >> 16);
+                                        cv -= wv.B * (float)msum;
                                     }
-                                    acc[m][t] += yd * cv;
+                                    acc[m][t] = fmaf(yd, cv, acc[m][t]);
                                 }
                             }
                         }
                     }
                 }
+            }
 #pragma unroll
-                for (int m = 0; m < NMAT; m++)
+            for (int m = 0; m < NMAT; m++)
 #pragma unroll
-                    for (int t = 0; t < TT; t++) {
-                        if (t < (int)nt) {
-                            float v = acc[m][t];
-                            for (uint32_t o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                            acc[m][t] = v;
-                        }
-                    }
-                if (rv) {
-                    /* lane sl of the row writes token sl (spreads the epilogue) */
-                    for (uint32_t t = sl; t < nt; t += lpr) {
-                        float v[NMAT];
-#pragma unroll
-                        for (int m = 0; m < NMAT; m++) {
-                            float pick = 0.0f;
-#pragma unroll
-                            for (int q = 0; q < TT; q++)
-                                if (q == (int)t) pick = acc[m][q];
-                            v[m] = pick;
-                        }
-                        seg.epi(r0 + j, t0 + t, v);
+                for (int t = 0; t < TT; t++) {
+                    if (t < (int)nt) {
+                        float v = acc[m][t];
+                        for (uint32_t o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                        acc[m][t] = v;
                     }
                 }
+            if (rv) {
+                for (uint32_t t = sl; t < nt; t += lpr) { /* lane sl writes token sl */
+                    float v[NMAT];
+#pragma unroll
+                    for (int m = 0; m < NMAT; m++) {
+                        float pick = 0.0f;
+#pragma unroll
+                        for (int q = 0; q < TT; q++)
+                            if (q == (int)t) pick = acc[m][q];
+                        v[m] = pick;
+                    }
+                    seg.epi(r0 + j, t, v);
+                }
             }
-            __syncthreads();
         }
-        issued += cps;
+        __syncwarp();
+        if (lane == 0 && i + ps.S < mine) { /* refill the stage just consumed */
+            pm_fence_proxy_async();
+            const uint8_t *s2[NMAT];
+            uint32_t r2, rows2;
+            geom(i + ps.S, s2, r2, rows2);
+            pm_issue_stage<NMAT>(ring + (size_t)st * ps.stage, bars + st, s2, rows2 * (uint32_t)rb);
+        }
     }
-    return true;
+    return __syncthreads_or(!ok) == 0;
 }

@@ -247,18 +247,24 @@ def test_fused_layer_vs_oracle(oracle, pb, name, kw, T):
 
 
 def test_fused_layer_expert_shards_sum(oracle, pb):
-    """expert-parallel shards [lo, hi) computed separately sum to the full layer"""
+    """expert-parallel shards [lo, hi) computed separately sum to the full
+    layer, and each shard equals the oracle restricted to its experts"""
     L = HostLayer(H=512, F=512, E=32, k=8, quant=2, seed=4, router_mode=0, zipf=(1.1, "select"), shared=(2, 512))
     T = 9
     x = np.random.default_rng(9).normal(0, 1, (T, L.H)).astype(np.float32)
+    _, sel, w = L.oracle_route(x)
     dl = L.to_device()
     ws = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
     full = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
     dl.forward(dev(x), full, ws)
+    assert rel_l2(host(full), L.oracle_ffn(x, sel, w)) < TOL
     acc = np.zeros((T, L.H), np.float64)
     for lo, hi in ((0, 8), (8, 16), (16, 32)):
         dl.expert_lo, dl.expert_hi, dl._desc = lo, hi, None
         part = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
         dl.forward(dev(x), part, ws)
-        acc += host(part)
+        got = host(part)
+        ref = L.oracle_ffn(x, sel, w, lo=lo, hi=hi, with_shared=(lo == 0))
+        assert rel_l2(got, ref) < TOL, (lo, hi, rel_l2(got, ref))
+        acc += got
     assert rel_l2(acc, host(full)) < 1e-5
