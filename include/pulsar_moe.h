@@ -186,6 +186,20 @@ size_t pulsar_moe_layer_workspace(const pulsar_moe_layer_desc *d, uint32_t max_t
 int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
                      uint32_t n_tok, void *ws, size_t ws_bytes, void *stream);
 
+/* pulsar_moe_layer for callers that cannot allocate device memory (a
+ * plugin inside a host that owns all device memory through its own pool,
+ * or code that must not call cudaMalloc while it runs).  No counterpart in
+ * the reference.  The workspace is a fixed 32 MiB array inside the library,
+ * held by every GPU that loads it until the process exits; a call whose
+ * workspace (pulsar_moe_layer_workspace) exceeds 32 MiB returns 0 with a
+ * message.  The first call on a device resolves the array's address on that
+ * device, so make that first call before any stream capture.  Every call
+ * shares the one array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller.  Allocates
+ * nothing. */
+int pulsar_moe_layer_noalloc(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
+                             uint32_t n_tok, void *stream);
+
 /* device pointers into a layer workspace after a call, for inspection */
 typedef struct pulsar_moe_ws_view {
     float *logits;        /* [n_tok][E] */

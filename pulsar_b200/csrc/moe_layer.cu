@@ -29,6 +29,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "../../include/pulsar_moe.h"
 #include "pm_host.h"
 #include "pm_router.cuh"
@@ -589,4 +591,52 @@ extern "C" int pulsar_moe_layer_profiled(const pulsar_moe_layer_desc *d, float *
                                          const float *residual, uint32_t n_tok, void *ws, size_t ws_bytes,
                                          void *stream, void *const *events) {
     return pm_moe_layer_impl(d, out, x, residual, n_tok, ws, ws_bytes, stream, events);
+}
+
+/* ============================================ allocation-free variant */
+
+/* Some callers cannot call cudaMalloc: a plugin loaded into a host process
+ * that owns every byte of device memory through its own pool, or code that
+ * must not allocate (or synchronize the device) while it runs.  For them,
+ * pulsar_moe_layer_noalloc keeps the layer's workspace in this fixed
+ * array, which every GPU that loads the library holds until the process
+ * exits.  In host code `pm_noalloc_scratch` only names the symbol; the
+ * device address is resolved per device with cudaGetSymbolAddress. */
+#define PM_NOALLOC_SCRATCH_BYTES (32u << 20) /* 32 MiB */
+static __device__ __align__(256) uint8_t pm_noalloc_scratch[PM_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex pm_noalloc_mu;
+static void *pm_noalloc_addr[64];
+
+extern "C" int pulsar_moe_layer_noalloc(const pulsar_moe_layer_desc *d, float *out, const float *x,
+                                        const float *residual, uint32_t n_tok, void *stream) {
+    if (!pm_desc_ok(d) || !out || !x || n_tok == 0) return 0;
+    const pm_layout L = pm_make_layout(d, n_tok);
+    if (L.total > PM_NOALLOC_SCRATCH_BYTES) {
+        fprintf(stderr,
+                "pulsar-b200: pulsar_moe_layer_noalloc: %u tokens need %zu bytes of scratch, more than the "
+                "built-in %u; use fewer tokens per call or pulsar_moe_layer with your own workspace\n",
+                n_tok, L.total, PM_NOALLOC_SCRATCH_BYTES);
+        return 0;
+    }
+    int dev = 0;
+    if (!pm_ok(cudaGetDevice(&dev), "noalloc: current device") || dev < 0 || dev >= 64) return 0;
+    void *ws = nullptr;
+    {
+        /* first call on a device: resolve the array's device address there */
+        std::lock_guard<std::mutex> lock(pm_noalloc_mu);
+        if (!pm_noalloc_addr[dev]) {
+            void *p = nullptr;
+            if (!pm_ok(cudaGetSymbolAddress(&p, pm_noalloc_scratch), "noalloc: scratch address")) return 0;
+            pm_noalloc_addr[dev] = p;
+        }
+        ws = pm_noalloc_addr[dev];
+    }
+    /* the array keeps the previous call's contents: clear the words that
+     * must start at zero (selection arrival counter, error word) */
+    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
+    if (!pm_ok(cudaMemsetAsync((uint8_t *)ws + L.sel_done, 0, 4, st), "noalloc: clear counter") ||
+        !pm_ok(cudaMemsetAsync((uint8_t *)ws + L.err, 0, 4, st), "noalloc: clear error word"))
+        return 0;
+    return pm_moe_layer_impl(d, out, x, residual, n_tok, ws, PM_NOALLOC_SCRATCH_BYTES, stream, nullptr);
 }
