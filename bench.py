@@ -28,6 +28,7 @@ the token owners (NCCL).  --impl reference times the CPU lane alone.
 from __future__ import annotations
 
 import argparse
+import datetime
 import faulthandler
 import json
 import os
@@ -378,7 +379,7 @@ def main():
     group = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
         group = dist.group.WORLD
     E = CFG["n_expert"]
     lo, hi = (rank * E // world, (rank + 1) * E // world) if world > 1 else (0, 0)
@@ -452,12 +453,22 @@ def main():
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": 7 * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
                 "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
     if line is not None:
-        print(json.dumps(line))
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        # Skip destroy_process_group: tearing down NCCL communicators that live
+        # CUDA graphs still reference can block indefinitely.  All device work is
+        # complete here; every rank leaves after one bounded barrier.
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        threading.Timer(60.0, os._exit, args=(0,)).start()  # bound the barrier below
+        try:
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            sys.stderr.flush()
+            os._exit(0)
 
 
 if __name__ == "__main__":
