@@ -44,14 +44,13 @@ int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32
 
 __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 
-#define PM_TT 8 /* tokens per register tile = tokens per work unit */
 
 /* ------------------------------------------------------------ layout */
 
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
     uint32_t max_work;
-    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, pairs, mid, partial,
+    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, pairs, mid, partial,
         sel_done, err, total;
 };
 
@@ -83,6 +82,8 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.max_work = L.max_items + (uint32_t)(((uint64_t)T * L.n_slot + PM_TT - 1) / PM_TT);
     L.work_item = o, o = pm_al(o + (size_t)L.max_work * 4);
     L.work_t0 = o, o = pm_al(o + (size_t)L.max_work * 4);
+    L.wd = o, o = pm_al(o + (size_t)L.max_work * 16);
+    L.sk_c = o, o = pm_al(o + (size_t)(L.max_work + 1) * 4);
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
     L.partial = o, o = pm_al(o + (size_t)T * L.n_slot * L.H * 4);
@@ -106,23 +107,24 @@ struct pm_layer_args {
     int32_t *sel;
     float *w;
     pm_block_q8K *xq;
-    uint32_t *n_items; /* [0] all items, [1] routed items, [2] work units */
+    uint32_t *n_items; /* [0] all items, [1] routed items, [2] work units, [3] routed work units */
     uint32_t *item_expert, *item_start, *pairs;
     uint32_t *work_item, *work_t0; /* work unit = (item, first token of its chunk of <= PM_TT) */
+    uint4 *wd;      /* per work unit: expert id (E + s for shared s), first pair, token count */
+    uint32_t *sk_c; /* [n_work + 1] prefix of per-row costs (PM_SK_CR + nt) over work units */
     float *mid;
     float *partial; /* [T * n_slot][H] down outputs before the combine */
     uint32_t *sel_done, *err;
     /* io */
     float *out;
     const float *residual;
-    uint32_t gu_rows, dn_rows; /* rows per CTA */
 };
 
 /* ============================================ 3: select + CSR build */
 
 __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_constant__ pm_layer_args a) {
     extern __shared__ __align__(16) uint8_t sm[];
-    __shared__ uint32_t is_last, tot_pairs, tot_items, tot_work;
+    __shared__ uint32_t is_last, tot_pairs, tot_items, tot_work, tot_cost;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
     const uint32_t token = blockIdx.x * 4u + wid;
     if (token < a.T) {
@@ -151,37 +153,45 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
     }
     __syncthreads();
     if (wid == 0) {
-        /* exclusive scans over experts: pair offsets, item indices, work units */
-        uint32_t carry_p = 0, carry_i = 0, carry_w = 0;
+        /* exclusive scans over experts: pair offsets, item indices, work
+         * units and the stream-K cost line (per-row cost PM_SK_CR + nt of
+         * each of the expert's chunks: all full but the last) */
+        uint32_t carry_p = 0, carry_i = 0, carry_w = 0, carry_c = 0;
         for (uint32_t c = 0; c < a.E; c += 32u) {
             const uint32_t e = c + lane;
             const uint32_t v = e < a.E ? cnt[e] : 0u;
-            const uint32_t nw = (v + PM_TT - 1) / PM_TT;
-            uint32_t ip = v, ii = v ? 1u : 0u, iw = nw;
+            const uint32_t nw = (v + PM_TT - 1) / PM_TT, cost = PM_SK_CR * nw + v;
+            uint32_t ip = v, ii = v ? 1u : 0u, iw = nw, ic = cost;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const uint32_t up = __shfl_up_sync(0xffffffffu, ip, o);
                 const uint32_t ui = __shfl_up_sync(0xffffffffu, ii, o);
                 const uint32_t uw = __shfl_up_sync(0xffffffffu, iw, o);
-                if (lane >= (uint32_t)o) ip += up, ii += ui, iw += uw;
+                const uint32_t uc = __shfl_up_sync(0xffffffffu, ic, o);
+                if (lane >= (uint32_t)o) ip += up, ii += ui, iw += uw, ic += uc;
             }
             const uint32_t start = carry_p + ip - v, item = carry_i + ii - (v ? 1u : 0u), w0 = carry_w + iw - nw;
+            const uint32_t c0 = carry_c + ic - cost;
             if (e < a.E) {
                 cnt[e] = start;
                 if (v) {
                     a.item_expert[item] = e;
                     a.item_start[item] = start;
                     for (uint32_t j = 0; j < nw; j++) {
+                        const uint32_t nt = v - j * PM_TT < PM_TT ? v - j * PM_TT : PM_TT;
                         a.work_item[w0 + j] = item;
                         a.work_t0[w0 + j] = j * PM_TT;
+                        a.wd[w0 + j] = make_uint4(e, start + j * PM_TT, nt, 0u);
+                        a.sk_c[w0 + j] = c0 + j * (PM_SK_CR + PM_TT);
                     }
                 }
             }
             carry_p += __shfl_sync(0xffffffffu, ip, 31);
             carry_i += __shfl_sync(0xffffffffu, ii, 31);
             carry_w += __shfl_sync(0xffffffffu, iw, 31);
+            carry_c += __shfl_sync(0xffffffffu, ic, 31);
         }
-        if (lane == 0) tot_pairs = carry_p, tot_items = carry_i, tot_work = carry_w;
+        if (lane == 0) tot_pairs = carry_p, tot_items = carry_i, tot_work = carry_w, tot_cost = carry_c;
     }
     __syncthreads();
     if (wid == 0) {
@@ -206,17 +216,21 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
     /* shared experts (computed on the shard that owns expert 0): one item
      * each over all tokens, appended after the routed items */
     const uint32_t n_sh = a.lo == 0 ? a.S : 0u;
-    const uint32_t sh_chunks = (a.T + PM_TT - 1) / PM_TT;
+    const uint32_t sh_chunks = (a.T + PM_TT - 1) / PM_TT, sh_cost = PM_SK_CR * sh_chunks + a.T;
     for (uint32_t s = 0; s < n_sh; s++) {
         const uint32_t item = tot_items + s, base = tot_pairs + s * a.T, w0 = tot_work + s * sh_chunks;
+        const uint32_t c0 = tot_cost + s * sh_cost;
         if (threadIdx.x == 0) {
             a.item_expert[item] = a.E + s;
             a.item_start[item] = base;
         }
         for (uint32_t t = threadIdx.x; t < a.T; t += blockDim.x) a.pairs[base + t] = t * a.n_slot + a.k + s;
         for (uint32_t j = threadIdx.x; j < sh_chunks; j += blockDim.x) {
+            const uint32_t nt = a.T - j * PM_TT < PM_TT ? a.T - j * PM_TT : PM_TT;
             a.work_item[w0 + j] = item;
             a.work_t0[w0 + j] = j * PM_TT;
+            a.wd[w0 + j] = make_uint4(a.E + s, base + j * PM_TT, nt, 0u);
+            a.sk_c[w0 + j] = c0 + j * (PM_SK_CR + PM_TT);
         }
     }
     if (threadIdx.x == 0) {
@@ -224,33 +238,13 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
         a.n_items[0] = tot_items + n_sh;
         a.n_items[1] = tot_items;
         a.n_items[2] = tot_work + n_sh * sh_chunks;
+        a.n_items[3] = tot_work;
+        a.sk_c[tot_work + n_sh * sh_chunks] = tot_cost + n_sh * sh_cost;
         *a.sel_done = 0;
     }
 }
 
-/* ====================================================== 4: gate / up */
-
-struct pm_seg_gu2 {
-    static constexpr bool F32 = false;
-    uint32_t n_f32;
-    const uint8_t *g, *u;
-    const uint32_t *pairs;
-    uint32_t n, row0;
-    const pm_layer_args *a;
-    const float *gb, *ub;
-    __device__ const uint8_t *base(int m) const { return m == 0 ? g : u; }
-    __device__ uint32_t ntok() const { return n; }
-    __device__ const pm_block_q8K *tok(uint32_t ti) const {
-        return a->xq + (uint64_t)(__ldcg(pairs + ti) / a->n_slot) * a->hb;
-    }
-    __device__ void epi(uint32_t row, uint32_t ti, const float *v) const {
-        const uint32_t p = __ldcg(pairs + ti);
-        float x0 = v[0], x1 = v[1];
-        if (gb) x0 += gb[row0 + row];
-        if (ub) x1 += ub[row0 + row];
-        a->mid[(uint64_t)p * a->Fmax + row0 + row] = pm_glu(x0, x1, a->act) * a->w[p];
-    }
-};
+/* ========================================= 4, 5: gate/up and down */
 
 /* the IQ2_XXS magnitude grid, expanded into shared memory (all threads) */
 __device__ __forceinline__ const uint64_t *pm_grid_fill(uint8_t *smem, bool need) {
@@ -266,97 +260,258 @@ __device__ __forceinline__ const uint64_t *pm_grid_fill(uint8_t *smem, bool need
             }
             g[i] = v;
         }
-    return g; /* the first __syncthreads of the engine publishes it */
+    return g; /* the first __syncthreads of the kernel publishes it */
 }
 
-template <int Q>
-__device__ bool pm_layer_gu_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t t0, uint32_t e,
-                                 uint32_t row0, uint32_t nrows, const pm_pass &ps) {
-    const bool routed = e < a.E;
-    const uint64_t rb = routed ? a.rb_gu_r : a.rb_gu_s;
-    const uint64_t *grid = pm_grid_fill(smem, Q == PM_QUANT_IQ2_XXS);
-    pm_seg_gu2 seg;
-    seg.g = (routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate) + (uint64_t)row0 * rb;
-    seg.u = (routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup) + (uint64_t)row0 * rb;
-    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
-    seg.pairs = a.pairs + s0 + t0;
-    seg.n = s1 - s0 - t0 < PM_TT ? s1 - s0 - t0 : PM_TT;
-    seg.row0 = row0;
-    seg.a = &a;
-    seg.gb = routed && a.gate_b ? a.gate_b + (uint64_t)e * a.Fr : nullptr;
-    seg.ub = routed && a.up_b ? a.up_b + (uint64_t)e * a.Fr : nullptr;
-    return pm_gemv_warps<Q, 2, PM_TT>(seg, smem, ps, nrows, rb, a.H / 32u, grid, a.err);
+/* matrix rows of a work unit: gate/up F (routed or shared), down H */
+template <int EPI>
+__device__ __forceinline__ uint32_t pm_unit_rows(const pm_layer_args &a, uint32_t e) {
+    if (EPI == 1) return a.H;
+    return e < a.E ? a.Fr : a.Fs;
 }
 
-template <int QR, int QS>
-__global__ void __launch_bounds__(PM_THREADS, 2)
-    pm_layer_gu_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t wk = blockIdx.x;
-    if (wk >= __ldcg(a.n_items + 2)) return;
-    const uint32_t item = __ldcg(a.work_item + wk), t0 = __ldcg(a.work_t0 + wk);
-    const uint32_t e = __ldcg(a.item_expert + item);
-    const bool routed = e < a.E;
-    const uint32_t F = routed ? a.Fr : a.Fs;
-    const uint32_t row0 = blockIdx.y * a.gu_rows;
-    if (row0 >= F) return;
-    const uint32_t nrows = F - row0 < a.gu_rows ? F - row0 : a.gu_rows;
-    const bool ok = routed ? pm_layer_gu_item<QR>(a, smem, item, t0, e, row0, nrows, pr)
-                           : pm_layer_gu_item<QS>(a, smem, item, t0, e, row0, nrows, psh);
-    if (ok) return;
-    (void)ok; /* a timeout is recorded in the error word; the layer output is then undefined */
+/* position of work unit w on the cost line (rows x per-row cost) */
+template <int EPI>
+__device__ __forceinline__ uint64_t pm_line(const pm_layer_args &a, uint32_t w, uint32_t n_rw, uint64_t c_rw) {
+    const uint64_t c = __ldcg(a.sk_c + w);
+    if (EPI == 1) return c * a.H;
+    return w <= n_rw ? c * a.Fr : c_rw * a.Fr + (c - c_rw) * a.Fs;
 }
 
-/* ======================================================= 5: down */
-
-struct pm_seg_dn2 {
-    static constexpr bool F32 = true; /* mid rows are quantized to q8_K while staging */
-    uint32_t n_f32;
-    const uint8_t *d;
-    const uint32_t *pairs;
-    uint32_t n, row0;
-    const pm_layer_args *a;
-    __device__ const uint8_t *base(int) const { return d; }
-    __device__ uint32_t ntok() const { return n; }
-    __device__ const pm_block_q8K *tok(uint32_t) const { return nullptr; }
-    __device__ const float *tok_f32(uint32_t ti) const { return a->mid + (uint64_t)__ldcg(pairs + ti) * a->Fmax; }
-    __device__ void epi(uint32_t row, uint32_t ti, const float *v) const {
-        a->partial[(uint64_t)__ldcg(pairs + ti) * a->H + row0 + row] = v[0];
+template <int EPI>
+__device__ __forceinline__ pm_segi pm_seg_load(const pm_layer_args &a, uint32_t w, uint32_t r0, uint32_t r1) {
+    const uint4 d = __ldcg(a.wd + w);
+    const uint32_t e = d.x;
+    pm_segi s;
+    s.kind = e < a.E ? 0u : 1u;
+    s.nt = d.z;
+    s.r0 = r0;
+    s.r1 = r1;
+    s.pairs = a.pairs + d.y;
+    s.b0 = s.b1 = nullptr;
+    if (EPI == 0) {
+        s.base[0] = s.kind == 0 ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate;
+        s.base[1] = s.kind == 0 ? a.up + (uint64_t)e * a.st_gu_r : a.sup;
+        if (s.kind == 0 && a.gate_b) s.b0 = a.gate_b + (uint64_t)e * a.Fr;
+        if (s.kind == 0 && a.up_b) s.b1 = a.up_b + (uint64_t)e * a.Fr;
+    } else {
+        s.base[0] = s.kind == 0 ? a.down + (uint64_t)e * a.st_dn_r : a.sdown;
+        s.base[1] = nullptr;
     }
+    return s;
+}
+
+/* the CTA's slice of the cost line as segments k = 0 .. n_seg-1 */
+struct pm_slice {
+    uint32_t w_lo, r_lo, w_hi, r_hi, n_seg;
 };
 
-template <int Q>
-__device__ void pm_layer_dn_item(const pm_layer_args &a, uint8_t *smem, uint32_t item, uint32_t t0, uint32_t e,
-                                 uint32_t row0, uint32_t nrows, const pm_pass &ps) {
-    const bool routed = e < a.E;
-    const uint64_t rb = routed ? a.rb_dn_r : a.rb_dn_s;
-    const uint64_t *grid = pm_grid_fill(smem, Q == PM_QUANT_IQ2_XXS);
-    pm_seg_dn2 seg;
-    seg.d = (routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown) + (uint64_t)row0 * rb;
-    const uint32_t s0 = __ldcg(a.item_start + item), s1 = __ldcg(a.item_start + item + 1);
-    seg.pairs = a.pairs + s0 + t0;
-    seg.n = s1 - s0 - t0 < PM_TT ? s1 - s0 - t0 : PM_TT;
-    seg.row0 = row0;
-    seg.a = &a;
-    const uint32_t F = routed ? a.Fr : a.Fs;
-    seg.n_f32 = F;
-    pm_gemv_warps<Q, 1, PM_TT>(seg, smem, ps, nrows, rb, (F + 31u) / 32u, grid, a.err);
+template <int EPI>
+__device__ __forceinline__ pm_segi pm_seg_get(const pm_layer_args &a, const pm_segi *tab, const pm_slice &sl,
+                                              uint32_t k) {
+    if (k < PM_SK_MAXSEG) return tab[k];
+    const uint32_t w = sl.w_lo + k;
+    const uint32_t r1 = w == sl.w_hi ? sl.r_hi : pm_unit_rows<EPI>(a, __ldcg(a.wd + w).x);
+    return pm_seg_load<EPI>(a, w, 0u, r1);
 }
 
-template <int QR, int QS>
+/* a warp's walk over its stages g = warp, warp + 8, ... of the CTA's
+ * concatenated segments (segment k holds stages [g0, g0 + nst)) */
+struct pm_it {
+    uint32_t k, g0, nst, g;
+};
+
+template <int EPI>
+__device__ __forceinline__ void pm_it_norm(pm_it &it, const pm_layer_args &a, const pm_segi *tab,
+                                           const pm_slice &sl, const pm_skp &P) {
+    while (it.k < sl.n_seg && it.g >= it.g0 + it.nst) {
+        it.g0 += it.nst;
+        it.k++;
+        if (it.k < sl.n_seg) {
+            const pm_segi s = pm_seg_get<EPI>(a, tab, sl, it.k);
+            const uint32_t rw = P.k[s.kind].rw;
+            it.nst = (s.r1 - s.r0 + rw - 1) / rw;
+        }
+    }
+}
+
+template <int NMAT>
+__device__ __forceinline__ void pm_stage_src(const pm_segi &s, const pm_skind &kd, const pm_it &it,
+                                             const uint8_t **src, uint32_t &r, uint32_t &rows) {
+    r = s.r0 + (it.g - it.g0) * kd.rw;
+    rows = s.r1 - r < kd.rw ? s.r1 - r : kd.rw;
+#pragma unroll
+    for (int m = 0; m < NMAT; m++) src[m] = s.base[m] + (uint64_t)r * kd.rb;
+}
+
+/* Persistent stream-K pass (pm_gemv.cuh).  EPI 0: gate+up of every work
+ * unit, glu * route weight -> mid.  EPI 1: down of every work unit (mid
+ * rows quantized to q8_K while staging) -> one partial row per pair. */
+template <int QR, int QS, int NMAT, int EPI>
 __global__ void __launch_bounds__(PM_THREADS, 2)
-    pm_layer_dn_kernel(const __grid_constant__ pm_layer_args a, pm_pass pr, pm_pass psh) {
+    pm_layer_sk_kernel(const __grid_constant__ pm_layer_args a, const __grid_constant__ pm_skp P) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t wk = blockIdx.x;
-    if (wk >= __ldcg(a.n_items + 2)) return;
-    const uint32_t item = __ldcg(a.work_item + wk), t0 = __ldcg(a.work_t0 + wk);
-    const uint32_t e = __ldcg(a.item_expert + item);
-    const uint32_t row0 = blockIdx.y * a.dn_rows;
-    const uint32_t nrows = a.H - row0 < a.dn_rows ? a.H - row0 : a.dn_rows;
-    if (e < a.E)
-        pm_layer_dn_item<QR>(a, smem, item, t0, e, row0, nrows, pr);
-    else
-        pm_layer_dn_item<QS>(a, smem, item, t0, e, row0, nrows, psh);
+    __shared__ uint32_t s_cnt[2], s_lim[4], s_tok[PM_TT];
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint64_t *grid = pm_grid_fill(smem, QR == PM_QUANT_IQ2_XXS || QS == PM_QUANT_IQ2_XXS);
+    uint64_t *bars = (uint64_t *)(smem + P.off_bar) + warp * P.S;
+    pm_segi *tab = (pm_segi *)(smem + P.off_seg);
+    uint8_t *ring = smem + P.off_ring + (size_t)warp * P.S * P.stage;
+    const pm_acts acts = pm_acts_carve(smem + P.off_acts, P.P, P.NB);
+    if (lane == 0) {
+        for (uint32_t i = 0; i < P.S; i++) pm_mbar_init(bars + i, 1);
+        pm_fence_barrier_init();
+    }
+    if (tid < 2) s_cnt[tid] = 0;
+    __syncthreads();
+
+    /* ---- this CTA's slice [lo, hi) of the cost line ---- */
+    const uint32_t n_work = __ldcg(a.n_items + 2), n_rw = __ldcg(a.n_items + 3);
+    const uint64_t c_rw = __ldcg(a.sk_c + n_rw);
+    const uint64_t C = pm_line<EPI>(a, n_work, n_rw, c_rw);
+    const uint64_t lo = C * blockIdx.x / gridDim.x, hi = C * (blockIdx.x + 1) / gridDim.x;
+    {
+        uint32_t c0 = 0, c1 = 0; /* units that start at or before lo / hi */
+        for (uint32_t i = tid + 1; i <= n_work; i += blockDim.x) {
+            const uint64_t v = pm_line<EPI>(a, i, n_rw, c_rw);
+            c0 += v <= lo;
+            c1 += v <= hi;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            c0 += __shfl_xor_sync(0xffffffffu, c0, o);
+            c1 += __shfl_xor_sync(0xffffffffu, c1, o);
+        }
+        if (lane == 0) {
+            atomicAdd(&s_cnt[0], c0);
+            atomicAdd(&s_cnt[1], c1);
+        }
+    }
+    __syncthreads();
+    if (tid < 2) { /* (unit, row) of a position, rows rounded up to PM_SK_RQ */
+        const uint64_t pos = tid ? hi : lo;
+        uint32_t w = s_cnt[tid], r = 0;
+        if (w < n_work) {
+            const uint4 d = __ldcg(a.wd + w);
+            const uint32_t rows = pm_unit_rows<EPI>(a, d.x);
+            const uint64_t off = (pos - pm_line<EPI>(a, w, n_rw, c_rw)) / (PM_SK_CR + d.z);
+            const uint64_t rq = (off + PM_SK_RQ - 1) / PM_SK_RQ * PM_SK_RQ;
+            if (rq >= rows)
+                w++;
+            else
+                r = (uint32_t)rq;
+        }
+        s_lim[2 * tid] = w;
+        s_lim[2 * tid + 1] = r;
+    }
+    __syncthreads();
+    pm_slice sl;
+    sl.w_lo = s_lim[0], sl.r_lo = s_lim[1], sl.w_hi = s_lim[2], sl.r_hi = s_lim[3];
+    sl.n_seg = sl.w_hi >= sl.w_lo ? sl.w_hi - sl.w_lo + (sl.r_hi ? 1u : 0u) : 0u;
+    for (uint32_t k = tid; k < sl.n_seg && k < PM_SK_MAXSEG; k += blockDim.x) {
+        const uint32_t w = sl.w_lo + k;
+        const uint32_t r1 = w == sl.w_hi ? sl.r_hi : pm_unit_rows<EPI>(a, __ldcg(a.wd + w).x);
+        tab[k] = pm_seg_load<EPI>(a, w, k == 0 ? sl.r_lo : 0u, r1);
+    }
+    __syncthreads();
+    if (sl.n_seg == 0) return;
+
+    /* ---- warp-private rings: the prologue fills S stages ---- */
+    auto it_init = [&]() {
+        pm_it it;
+        it.k = 0, it.g0 = 0, it.g = warp;
+        const pm_segi s = tab[0];
+        it.nst = (s.r1 - s.r0 + P.k[s.kind].rw - 1) / P.k[s.kind].rw;
+        pm_it_norm<EPI>(it, a, tab, sl, P);
+        return it;
+    };
+    pm_it iti = it_init(), itc = iti;
+    uint32_t ni = 0, ci = 0;
+    auto issue = [&](uint32_t slot) {
+        const pm_segi s = pm_seg_get<EPI>(a, tab, sl, iti.k);
+        const uint8_t *src[NMAT];
+        uint32_t r, rows;
+        pm_stage_src<NMAT>(s, P.k[s.kind], iti, src, r, rows);
+        pm_issue_stage<NMAT>(ring + (size_t)slot * P.stage, bars + slot, src, rows * (uint32_t)P.k[s.kind].rb);
+    };
+    while (ni < P.S && iti.k < sl.n_seg) {
+        if (lane == 0) issue(ni);
+        ni++;
+        iti.g += PM_WARPS;
+        pm_it_norm<EPI>(iti, a, tab, sl, P);
+    }
+
+    /* ---- segments: swap the token tile, then consume this warp's stages ---- */
+    bool fail = false;
+    for (uint32_t k = 0; k < sl.n_seg; k++) {
+        if (k > 0 && __syncthreads_or(fail)) break;
+        const pm_segi s = pm_seg_get<EPI>(a, tab, sl, k);
+        const pm_skind &kd = P.k[s.kind];
+        if (EPI == 0) {
+            const pm_block_q8K *rows[PM_TT];
+#pragma unroll
+            for (uint32_t t = 0; t < PM_TT; t++)
+                rows[t] = t < s.nt ? a.xq + (uint64_t)(__ldcg(s.pairs + t) / a.n_slot) * a.hb : nullptr;
+            pm_acts_stage_q8(acts, s.nt, rows, kd.n_units);
+        } else {
+            const float *rows[PM_TT];
+#pragma unroll
+            for (uint32_t t = 0; t < PM_TT; t++)
+                rows[t] = t < s.nt ? a.mid + (uint64_t)__ldcg(s.pairs + t) * a.Fmax : nullptr;
+            pm_acts_stage_f32(acts, s.nt, rows, s.kind == 0 ? a.Fr : a.Fs);
+        }
+        if (tid < s.nt) s_tok[tid] = __ldcg(s.pairs + tid);
+        __syncthreads();
+        while (itc.k == k) {
+            const uint32_t slot = ci % P.S;
+            if (!pm_mbar_wait_sleep(bars + slot, (ci / P.S) & 1u, a.err)) {
+                fail = true;
+                break;
+            }
+            const uint8_t *src[NMAT];
+            uint32_t r, rows;
+            pm_stage_src<NMAT>(s, kd, itc, src, r, rows);
+            const uint8_t *stg = ring + (size_t)slot * P.stage;
+            pm_rowjob jb;
+#pragma unroll
+            for (int m = 0; m < NMAT; m++) jb.w[m] = pm_stage_ptr<NMAT>(stg, src, rows * (uint32_t)kd.rb, m);
+            if (NMAT == 1) jb.w[1] = nullptr;
+            jb.rb = kd.rb;
+            jb.rows = rows;
+            jb.npair = kd.npair;
+            jb.n_units = kd.n_units;
+            jb.row_g = r;
+            jb.nt = s.nt;
+            jb.act = a.act;
+            jb.ostride = EPI == 0 ? a.Fmax : a.H;
+            jb.acts = acts;
+            jb.grid = grid;
+            jb.tokpair = s_tok;
+            jb.out = EPI == 0 ? a.mid : a.partial;
+            jb.b0 = s.b0;
+            jb.b1 = s.b1;
+            jb.wts = a.w;
+            if (s.kind == 0)
+                pm_rows_any<QR, NMAT, EPI>(jb, kd.lpr);
+            else
+                pm_rows_any<QS, NMAT, EPI>(jb, kd.lpr);
+            __syncwarp();
+            if (iti.k < sl.n_seg) { /* refill the slot just consumed */
+                if (lane == 0) {
+                    pm_fence_proxy_async();
+                    issue(slot);
+                }
+                ni++;
+                iti.g += PM_WARPS;
+                pm_it_norm<EPI>(iti, a, tab, sl, P);
+            }
+            ci++;
+            itc.g += PM_WARPS;
+            pm_it_norm<EPI>(itc, a, tab, sl, P);
+        }
+    }
+    if (__syncthreads_or(fail) && lane == 0) /* drain this warp's copies still in flight */
+        for (uint32_t d = ci; d < ni; d++) pm_mbar_wait(bars + (d % P.S), (d / P.S) & 1u, nullptr);
 }
 
 /* ================================================= 6: combine */
@@ -433,38 +588,63 @@ extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t
     return 1;
 }
 
-/* largest power-of-two row count in [lo, hi] that still gives ~2 waves */
-static uint32_t pm_pow2_rows(uint64_t nrows_total, uint64_t ctas_other, uint32_t lo, uint32_t hi) {
-    uint32_t r = hi;
-    while (r > lo && ((nrows_total + r - 1) / r) * ctas_other < 2ull * 148ull) r >>= 1;
-    return r;
+/* geometry of one matrix kind: 16 lanes per row when a row has at least
+ * 32 unit pairs (2+ pairs per lane), else 4; a stage holds whole passes
+ * of the warp (32 / lpr rows) and about 4.5 KB */
+static pm_skind pm_kind_for(uint32_t nmat, uint64_t rb, uint32_t n) {
+    pm_skind k;
+    k.rb = rb;
+    k.n_units = (n + 31u) / 32u;
+    k.npair = (k.n_units + 1u) / 2u;
+    k.lpr = k.npair >= 32u ? 16u : 4u;
+    const uint32_t rpp = 32u / k.lpr;
+    uint64_t passes = 4608u / (nmat * rb * rpp);
+    if (passes < 1) passes = 1;
+    k.rw = (uint32_t)(rpp * passes);
+    return k;
 }
 
-/* pass geometry: lanes per row (one lane per pair of units), rows per
- * stage (~6 KB, whole passes of the warp), per-warp ring depth within a
- * ~100 KB budget (two CTAs per SM), and the shared-memory layout */
-static pm_pass pm_pass_for(uint32_t nmat, uint64_t rb, uint32_t n_units, uint32_t rows_cta, bool grid) {
-    pm_pass p;
-    const uint32_t pairs = (n_units + 1) / 2;
-    p.lpr = pairs >= 32 ? 32u : (pairs >= 16 ? 16u : (pairs >= 8 ? 8u : (pairs >= 4 ? 4u : 2u)));
-    const uint32_t rpp = 32u / p.lpr;
-    uint64_t rw = 6144u / (nmat * rb);
-    rw = (rw / rpp) * rpp;
-    if (rw < rpp) rw = rpp;
-    const uint32_t per_warp = (rows_cta + PM_WARPS - 1) / PM_WARPS;
-    if (rw > per_warp) rw = ((per_warp + rpp - 1) / rpp) * rpp;
-    p.rw = (uint32_t)rw;
-    p.stage = pm_stage_bytes(nmat, rb, p.rw);
-    p.off_bar = grid ? 2048u : 0u;
-    p.off_tok = p.off_bar + 512u;
-    p.off_acts = p.off_tok + 128u;
-    const uint32_t ring0 = (p.off_acts + pm_acts_bytes(PM_TT, n_units) + 127u) & ~127u;
-    const uint32_t budget = 100u * 1024u;
-    uint32_t S = budget > ring0 ? (budget - ring0) / (PM_WARPS * p.stage) : 2u;
-    p.S = S < 2 ? 2 : (S > 8 ? 8 : S);
-    p.off_ring = ring0;
-    p.smem = ring0 + PM_WARPS * p.S * p.stage;
-    return p;
+/* shared-memory layout: IQ2 grid | segment table | token tile | mbarriers
+ * | per-warp rings; ring depth from a ~110 KB budget (two CTAs per SM) */
+static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bool grid) {
+    pm_skp P;
+    P.k[0] = r;
+    P.k[1] = s;
+    const uint32_t st0 = pm_stage_bytes(nmat, r.rb, r.rw), st1 = pm_stage_bytes(nmat, s.rb, s.rw);
+    P.stage = ((st0 > st1 ? st0 : st1) + 15u) & ~15u;
+    P.P = r.npair > s.npair ? r.npair : s.npair;
+    const uint32_t nb0 = (r.n_units + 7u) / 8u, nb1 = (s.n_units + 7u) / 8u;
+    P.NB = nb0 > nb1 ? nb0 : nb1;
+    uint32_t off = grid ? 2048u : 0u;
+    P.off_seg = off;
+    off += PM_SK_MAXSEG * (uint32_t)sizeof(pm_segi);
+    P.off_acts = (off + 15u) & ~15u;
+    off = P.off_acts + pm_acts_bytes(P.P, P.NB);
+    P.off_bar = (off + 15u) & ~15u;
+    P.off_ring = (P.off_bar + PM_WARPS * 8u * 8u + 127u) & ~127u;
+    const uint32_t budget = 110u * 1024u;
+    uint32_t S = budget > P.off_ring ? (budget - P.off_ring) / (PM_WARPS * P.stage) : 2u;
+    P.S = S < 2 ? 2 : (S > 8 ? 8 : S);
+    P.smem = P.off_ring + PM_WARPS * P.S * P.stage;
+    return P;
+}
+
+/* persistent grid: resident CTAs per SM x SMs, cached per device */
+template <class K>
+static uint32_t pm_sk_grid(K kernel, uint32_t smem, int *occ, uint32_t *occ_smem) {
+    static int sms[64];
+    const int dev = pm_cur_device();
+    if (dev < 0 || dev >= 64) return 0;
+    if (!sms[dev] && !pm_ok(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev), "SM count"))
+        return 0;
+    if (occ_smem[dev] != smem || occ[dev] <= 0) {
+        int n = 0;
+        if (!pm_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, PM_THREADS, smem), "occupancy"))
+            return 0;
+        occ[dev] = n;
+        occ_smem[dev] = smem;
+    }
+    return (uint32_t)(occ[dev] > 0 ? occ[dev] : 1) * (uint32_t)sms[dev];
 }
 
 static inline void pm_ev(void *const *ev, int i, cudaStream_t st) {
@@ -474,24 +654,27 @@ static inline void pm_ev(void *const *ev, int i, cudaStream_t st) {
 template <int QR, int QS>
 static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st, void *const *ev) {
     static uint64_t done_gu = 0, done_dn = 0;
-    /* 4: gate/up (+ q8_K of mid) */
-    const uint32_t hu = a.H / 32u;
-    const pm_pass gr = pm_pass_for(2, a.rb_gu_r, hu, a.gu_rows, QR == PM_QUANT_IQ2_XXS);
-    const pm_pass gs = a.S ? pm_pass_for(2, a.rb_gu_s, hu, a.gu_rows, QS == PM_QUANT_IQ2_XXS) : gr;
-    uint32_t smem_gu = gr.smem > gs.smem ? gr.smem : gs.smem;
-    if (!pm_smem_attr(pm_layer_gu_kernel<QR, QS>, smem_gu, &done_gu)) return 0;
-    dim3 ggrid(L.max_work, (L.Fmax + a.gu_rows - 1) / a.gu_rows);
-    pm_layer_gu_kernel<QR, QS><<<ggrid, PM_THREADS, smem_gu, st>>>(a, gr, gs);
+    static int occ_gu[64], occ_dn[64];
+    static uint32_t sm_gu[64], sm_dn[64];
+    const bool grid = QR == PM_QUANT_IQ2_XXS || QS == PM_QUANT_IQ2_XXS;
+    /* 4: gate/up -> mid */
+    const pm_skind gr = pm_kind_for(2, a.rb_gu_r, a.H);
+    const pm_skp pg = pm_skp_for(2, gr, a.S ? pm_kind_for(2, a.rb_gu_s, a.H) : gr, grid);
+    auto kgu = pm_layer_sk_kernel<QR, QS, 2, 0>;
+    if (!pm_smem_attr(kgu, pg.smem, &done_gu)) return 0;
+    const uint32_t g_gu = pm_sk_grid(kgu, pg.smem, occ_gu, sm_gu);
+    if (!g_gu) return 0;
+    kgu<<<g_gu, PM_THREADS, pg.smem, st>>>(a, pg);
     if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
     pm_ev(ev, 4, st);
     /* 5: down -> partial rows */
-    const uint32_t fr = (a.Fr + 31u) / 32u, fs = a.S ? (a.Fs + 31u) / 32u : fr;
-    const pm_pass dr = pm_pass_for(1, a.rb_dn_r, fr, a.dn_rows, QR == PM_QUANT_IQ2_XXS);
-    const pm_pass ds = a.S ? pm_pass_for(1, a.rb_dn_s, fs, a.dn_rows, QS == PM_QUANT_IQ2_XXS) : dr;
-    const uint32_t smem_dn = dr.smem > ds.smem ? dr.smem : ds.smem;
-    if (!pm_smem_attr(pm_layer_dn_kernel<QR, QS>, smem_dn, &done_dn)) return 0;
-    dim3 dgrid(L.max_work, (a.H + a.dn_rows - 1) / a.dn_rows);
-    pm_layer_dn_kernel<QR, QS><<<dgrid, PM_THREADS, smem_dn, st>>>(a, dr, ds);
+    const pm_skind dr = pm_kind_for(1, a.rb_dn_r, a.Fr);
+    const pm_skp pd = pm_skp_for(1, dr, a.S ? pm_kind_for(1, a.rb_dn_s, a.Fs) : dr, grid);
+    auto kdn = pm_layer_sk_kernel<QR, QS, 1, 1>;
+    if (!pm_smem_attr(kdn, pd.smem, &done_dn)) return 0;
+    const uint32_t g_dn = pm_sk_grid(kdn, pd.smem, occ_dn, sm_dn);
+    if (!g_dn) return 0;
+    kdn<<<g_dn, PM_THREADS, pd.smem, st>>>(a, pd);
     if (!pm_ok(cudaGetLastError(), "moe layer down launch")) return 0;
     /* 6: combine */
     const uint64_t tot = (uint64_t)a.T * a.H;
@@ -557,14 +740,14 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.pairs = (uint32_t *)(b + L.pairs);
     a.work_item = (uint32_t *)(b + L.work_item);
     a.work_t0 = (uint32_t *)(b + L.work_t0);
+    a.wd = (uint4 *)(b + L.wd);
+    a.sk_c = (uint32_t *)(b + L.sk_c);
     a.mid = (float *)(b + L.mid);
     a.partial = (float *)(b + L.partial);
     a.sel_done = (uint32_t *)(b + L.sel_done);
     a.err = (uint32_t *)(b + L.err);
     a.out = out;
     a.residual = residual;
-    a.gu_rows = pm_pow2_rows(L.Fmax, L.max_items, 8, 256);
-    a.dn_rows = pm_pow2_rows(L.H, L.max_items, 16, 512);
 
     /* 1, 2: logits and q8_K(x) */
     pm_ev(ev, 0, st);

@@ -1,159 +1,472 @@
-/* pm_gemv.cuh - expert-major decode GEMV engine (token-tile register
- * blocking), used by the fused layer.
+/* pm_gemv.cuh - stream-K decode engine of the fused layer (gate/up and down).
  *
- * One CTA owns (expert work item, tile of R weight rows) of NMAT matrices
- * that share geometry (gate + up, or down).  The rows stream through an
- * S-stage shared-memory ring with 1-D TMA bulk copies (pm_stream.cuh
- * primitives).  The item's tokens are processed in tiles of TT: each
- * tile's q8_K activations are staged in shared memory once, split into two
- * 16-byte planes per 32-value unit so a warp's vector loads are
- * conflict-free.  Every 32-value weight unit is decoded ONCE into eight
- * int8x4 words plus a float scale pair, then dotted (dp4a) against all TT
- * tokens held in registers - the unpack cost is amortised over the tile.
- * Units of a row are spread over LPR lanes (32, or 16/8 for short rows so
- * no lane idles), partial sums reduce with shuffles, and the epilogue gets
- * one value per (row, token, matrix).
+ * Work.  The layer's selection kernel lists WORK UNITS: (expert, chunk of
+ * <= PM_TT tokens routed to it).  A work unit multiplies every row of the
+ * expert's matrices (gate+up: F rows of each; down: H rows) with its
+ * tokens.  Rows of a unit cost roughly (PM_SK_CR + nt) token-dots each
+ * (decode + nt dots), so the whole launch is a line of
+ *     C = sum over units of rows(unit) * (PM_SK_CR + nt(unit))
+ * cost units.  The kernel is persistent: CTA b of G takes the slice
+ * [b*C/G, (b+1)*C/G) of that line, cut at row boundaries (multiples of
+ * PM_SK_RQ), so every CTA gets the same amount of work whatever the
+ * routing skew - there is no tail of half-empty waves.  A CTA's slice is a
+ * short list of SEGMENTS (unit, row range).
  *
- * Per-unit contribution (format math of cu:1582-2190 / cpu_dot.rs, with the
- * 16-value Q2_K scales folded into the int8 weights, q*sc <= 45):
- *   yd * (A * sumi - B * (ma * bsum_lo + mb * bsum_hi))
+ * Streaming.  Each warp owns every 8th stage (rw rows of all NMAT
+ * matrices) of the CTA's concatenated segments and streams them through
+ * its own S-deep ring of 1-D TMA bulk copies on its own mbarriers, across
+ * segment boundaries, so HBM stays busy while the CTA swaps token tiles.
+ * The only CTA barriers are two per segment (token tile swap).
+ *
+ * Math.  A lane takes PAIRS of adjacent 32-value units of a row (same
+ * 256-value super-block / q8_K block): the pair's weights are decoded once
+ * into int8x4 words and dotted (dp4a) against each of the nt tokens; the
+ * integer sums of the pair are combined in integer arithmetic with the
+ * sub-block scales and mins before one float combination per (pair,
+ * token).  NT (the token count, compile time) unrolls the token loop.  The
+ * per-lane partial sums of a row are reduced with a shuffle
+ * reduce-scatter, which leaves each (matrix, token) total in one lane.
+ * Activation tiles are stored as four 16-byte planes per unit pair
+ * ([plane][token][pair]) so a quarter-warp's vector loads never collide.
+ *
+ * Format math (crates/kernels/cuda/pulsar_kernels.cu dot functors q4_K
+ * cu:1699, q2_K cu:1625, iq2_xxs cu:1582, mxfp4 cu:2053, q8_0 cu:2174;
+ * crates/quant/src/cpu_dot.rs :92 :250 :732), regrouped per unit pair:
+ *   Q4_K   yd * ((d/16) * (16 sc0 S0 + sc1 S1') - dmin * (m0 B0 + m1 B1))
+ *          (S1' is the high-nibble dot taken on the nibbles in place, = 16 S1)
+ *   Q2_K   yd * (d * (S0 + S1) - dmin * sum m16 * B16)   (16-value scales folded)
+ *   IQ2    yd * (d/8) * ((2s0+1) S0 + (2s1+1) S1)
+ *   MXFP4, Q8_0  yd * (d0 S0 + d1 S1)
  */
 #pragma once
 #include "pm_stream.cuh"
 
-struct pm_wunit {
-    int32_t w[8];
-    float A, B;
-    int32_t ma, mb;
+#define PM_TT 8       /* tokens per work unit (register tile) */
+#define PM_SK_CR 2u   /* per-row decode cost, in token-dot units */
+#define PM_SK_RQ 8u   /* slice boundaries fall on multiples of this many rows */
+#define PM_SK_MAXSEG 64u
+
+/* ------------------------------------------------------- activations */
+
+/* staged activations of one token tile:
+ *   x  [4][PM_TT][P] uint4 : plane 0/1 = bytes 0-15/16-31 of the pair's
+ *                            first unit, plane 2/3 = of its second unit
+ *   bs [PM_TT][P] int4     : 16-value bsums (u0 lo, u0 hi, u1 lo, u1 hi)
+ *   d  [PM_TT][NB] float   : q8_K block scale */
+struct pm_acts {
+    uint4 *x;
+    int4 *bs;
+    float *d;
+    uint32_t P, NB;
 };
 
-template <int Q>
-__device__ __forceinline__ void pm_decode(const uint8_t *row, uint32_t u, const uint64_t *grid, pm_wunit &o) {
-    const uint32_t sb = u >> 3, s = u & 7u;
-    if constexpr (Q == PM_QUANT_Q4_K) {
-        const uint8_t *b = row + sb * PM_Q4_K_BYTES;
-        const uint4 hdr = *(const uint4 *)b;
-        int scv, mnv;
-        pm_k4_scale_min((int)s, b + 4, &scv, &mnv);
-        const uint4 *qp = (const uint4 *)(b + 16 + 32 * (s >> 1));
-        const uint4 q0 = qp[0], q1 = qp[1];
-        const uint32_t raw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const int sh = (s & 1) * 4;
-#pragma unroll
-        for (int i = 0; i < 8; i++) o.w[i] = (int32_t)((raw[i] >> sh) & 0x0f0f0f0fu);
-        o.A = pm_h2f(hdr.x & 0xffffu) * (float)scv;
-        o.B = pm_h2f(hdr.x >> 16);
-        o.ma = o.mb = mnv;
-    } else if constexpr (Q == PM_QUANT_Q2_K) {
-        const uint8_t *b = row + sb * PM_Q2_K_BYTES;
-        const uint32_t *q = (const uint32_t *)(b + 16 + 32 * (s >> 2));
-        const int sh = 2 * (s & 3);
-        const uint32_t scw = *(const uint16_t *)(b + 2 * s);
-        const uint32_t sc0 = scw & 15u, sc1 = (scw >> 8) & 15u;
+__host__ __device__ __forceinline__ uint32_t pm_acts_bytes(uint32_t P, uint32_t NB) {
+    return PM_TT * (P * 80u + NB * 4u) + 64u;
+}
+
+__device__ __forceinline__ pm_acts pm_acts_carve(uint8_t *p, uint32_t P, uint32_t NB) {
+    pm_acts a;
+    a.P = P;
+    a.NB = NB;
+    a.x = (uint4 *)p;
+    a.bs = (int4 *)(a.x + 4u * PM_TT * P);
+    a.d = (float *)(a.bs + PM_TT * P);
+    return a;
+}
+
+/* nt tokens' q8_K rows (n_units 32-value units each) into the planes;
+ * block scales of tokens nt..PM_TT-1 are zeroed.  All threads. */
+__device__ __forceinline__ void pm_acts_stage_q8(const pm_acts &a, uint32_t nt, const pm_block_q8K *const *rows,
+                                                 uint32_t n_units) {
+    const uint32_t words = n_units * 8u;
+    for (uint32_t i = threadIdx.x; i < nt * words; i += blockDim.x) {
+        const uint32_t t = i / words, wd = i % words;
+        const uint32_t u = wd >> 3, k = wd & 7u;
+        const int32_t v = __ldcg((const int32_t *)((const uint8_t *)(rows[t] + (u >> 3)) + 4 + 32 * (u & 7u)) + k);
+        const uint32_t plane = 2u * (u & 1u) + (k >> 2);
+        ((int32_t *)(a.x + (plane * PM_TT + t) * a.P + (u >> 1)))[k & 3u] = v;
+    }
+    for (uint32_t i = threadIdx.x; i < nt * n_units; i += blockDim.x) {
+        const uint32_t t = i / n_units, u = i % n_units;
+        const pm_block_q8K *blk = rows[t] + (u >> 3);
+        const uint32_t w = (uint32_t)__ldcg((const int32_t *)((const uint8_t *)blk + 260 + 4 * (u & 7u)));
+        int32_t *dst = (int32_t *)(a.bs + t * a.P + (u >> 1)) + 2u * (u & 1u);
+        dst[0] = (int32_t)(int16_t)(w & 0xffffu);
+        dst[1] = (int32_t)(int16_t)(w >> 16);
+        if ((u & 7u) == 0) a.d[t * a.NB + (u >> 3)] = __ldcg(&blk->d);
+    }
+    for (uint32_t i = threadIdx.x; i < (PM_TT - nt) * a.NB; i += blockDim.x) a.d[nt * a.NB + i] = 0.0f;
+}
+
+/* nt f32 rows of n values quantized to q8_K exactly like the CPU lane
+ * (cpu_dot.rs:26-50: d = amax/127, round half away from zero, clamp
+ * +-127) straight into the planes: one warp per (token, 256-block), a lane
+ * holds 8 consecutive values = a quarter of one unit.  All threads. */
+__device__ __forceinline__ void pm_acts_stage_f32(const pm_acts &a, uint32_t nt, const float *const *rows,
+                                                  uint32_t n) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const uint32_t n_units = (n + 31u) / 32u, nblk = (n + 255u) / 256u;
+    for (uint32_t job = warp; job < nt * nblk; job += nw) {
+        const uint32_t t = job / nblk, b = job % nblk;
+        const float *src = rows[t] + (size_t)b * 256u;
+        const uint32_t valid = n - b * 256u < 256u ? n - b * 256u : 256u;
+        float v[8], amax = 0.0f;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const uint32_t v = (q[i] >> sh) & 0x03030303u; /* 0..3 per byte */
-            o.w[i] = (int32_t)(v * (i < 4 ? sc0 : sc1));   /* <= 45 per byte, no carry */
+            const uint32_t e = lane * 8u + (uint32_t)i;
+            v[i] = e < valid ? __ldcg(src + e) : 0.0f;
+            amax = fmaxf(amax, fabsf(v[i]));
         }
-        const uint32_t dd = *(const uint32_t *)(b + 80);
-        o.A = pm_h2f(dd & 0xffffu);
-        o.B = pm_h2f(dd >> 16);
-        o.ma = (int32_t)((scw >> 4) & 15u);
-        o.mb = (int32_t)(scw >> 12);
-    } else if constexpr (Q == PM_QUANT_IQ2_XXS) {
-        const uint16_t *h = (const uint16_t *)(row + sb * PM_IQ2_XXS_BYTES);
-        const uint32_t aux0 = (uint32_t)h[1 + 4 * s] | ((uint32_t)h[2 + 4 * s] << 16);
-        const uint32_t aux1 = (uint32_t)h[3 + 4 * s] | ((uint32_t)h[4 + 4 * s] << 16);
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-            pm_iq2_signed(grid[(aux0 >> (8 * k)) & 0xffu], pm_ksigns_dev((aux1 >> (7 * k)) & 127u), o.w[2 * k],
-                          o.w[2 * k + 1]);
-        o.A = 0.125f * pm_h2f(h[0]) * (float)(2u * (aux1 >> 28) + 1u);
-        o.B = 0.0f;
-        o.ma = o.mb = 0;
+        for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        uint32_t qv[8];
+        int s = 0;
+        const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float r = amax == 0.0f ? 0.0f : roundf(__fmul_rn(v[i], inv));
+            r = fminf(fmaxf(r, -127.0f), 127.0f);
+            const int qi = (int)r;
+            s += qi;
+            qv[i] = (uint32_t)(uint8_t)(int8_t)qi;
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 1);              /* 16-value sum (lane pair) */
+        const int s_hi = __shfl_down_sync(0xffffffffu, s, 2); /* the unit's second 16 */
+        const uint32_t u = b * 8u + (lane >> 2);
+        if (u < n_units) {
+            const uint32_t q = lane & 3u; /* quarter of the unit */
+            const uint32_t plane = 2u * (u & 1u) + (q >> 1);
+            uint32_t *dst = (uint32_t *)(a.x + (plane * PM_TT + t) * a.P + (u >> 1)) + 2u * (q & 1u);
+            dst[0] = qv[0] | (qv[1] << 8) | (qv[2] << 16) | (qv[3] << 24);
+            dst[1] = qv[4] | (qv[5] << 8) | (qv[6] << 16) | (qv[7] << 24);
+            if (q == 0) {
+                int32_t *bd = (int32_t *)(a.bs + t * a.P + (u >> 1)) + 2u * (u & 1u);
+                bd[0] = s;
+                bd[1] = s_hi;
+            }
+        }
+        if (lane == 0) a.d[t * a.NB + b] = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
+    }
+    for (uint32_t i = threadIdx.x; i < (PM_TT - nt) * a.NB; i += blockDim.x) a.d[nt * a.NB + i] = 0.0f;
+}
+
+/* ------------------------------------------------------ pair decode */
+
+/* one row's unit pair (units 2p, 2p+1) of one matrix, decoded */
+struct pm_wp {
+    uint32_t w0[8], w1[8]; /* int8x4 weights (Q4_K: nibbles in place) */
+    int32_t i0, i1;        /* integer sub-block multipliers */
+    int32_t m0, m1, m2, m3;
+    float d, dm;
+};
+
+__device__ __forceinline__ int pm_dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+template <int Q>
+__device__ __forceinline__ void pm_decode_pair(const uint8_t *row, uint32_t p, bool two, const uint64_t *grid,
+                                               pm_wp &o) {
+    if constexpr (Q == PM_QUANT_Q4_K) {
+        const uint8_t *b = row + (p >> 2) * PM_Q4_K_BYTES;
+        const uint32_t sp = p & 3u;
+        const uint4 h = *(const uint4 *)b;
+        const uint32_t hdr = h.x, sa = h.y, sb = h.z, sc = h.w;
+        /* 6-bit scale/min of sub-blocks 2sp and 2sp+1 (k4 packing, cu:1699) */
+        const uint32_t sh = 16u * (sp & 1u);
+        const uint32_t ea = (sa >> sh) & 0xffffu, eb = (sb >> sh) & 0xffffu, ec = (sc >> sh) & 0xffffu;
+        int32_t s0, s1, n0, n1;
+        if (sp < 2) {
+            s0 = (int32_t)(ea & 63u), s1 = (int32_t)((ea >> 8) & 63u);
+            n0 = (int32_t)(eb & 63u), n1 = (int32_t)((eb >> 8) & 63u);
+        } else {
+            s0 = (int32_t)((ec & 15u) | ((ea >> 6) & 3u) << 4);
+            s1 = (int32_t)(((ec >> 8) & 15u) | ((ea >> 14) & 3u) << 4);
+            n0 = (int32_t)(((ec >> 4) & 15u) | ((eb >> 6) & 3u) << 4);
+            n1 = (int32_t)(((ec >> 12) & 15u) | ((eb >> 14) & 3u) << 4);
+        }
+        const uint4 *qp = (const uint4 *)(b + 16 + 32 * sp);
+        const uint4 q0 = qp[0], q1 = qp[1];
+        const uint32_t raw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            o.w0[i] = raw[i] & 0x0f0f0f0fu;
+            o.w1[i] = raw[i] & 0xf0f0f0f0u;
+        }
+        o.i0 = 16 * s0, o.i1 = s1, o.m0 = n0, o.m1 = n1;
+        o.d = pm_h2f(hdr & 0xffffu) * 0.0625f;
+        o.dm = pm_h2f(hdr >> 16);
+    } else if constexpr (Q == PM_QUANT_Q2_K) {
+        const uint8_t *b = row + (p >> 2) * PM_Q2_K_BYTES;
+        const uint32_t sp = p & 3u;
+        const uint32_t *q = (const uint32_t *)(b + 16 + 32 * (sp >> 1));
+        const uint32_t sh0 = 4u * (sp & 1u);
+        const uint32_t scw = *(const uint32_t *)(b + 4 * sp);
+        const uint32_t c0 = scw & 15u, c1 = (scw >> 8) & 15u, c2 = (scw >> 16) & 15u, c3 = (scw >> 24) & 15u;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t v = q[i];
+            o.w0[i] = ((v >> sh0) & 0x03030303u) * (i < 4 ? c0 : c1);
+            o.w1[i] = ((v >> (sh0 + 2u)) & 0x03030303u) * (i < 4 ? c2 : c3);
+        }
+        o.i0 = o.i1 = 1;
+        o.m0 = (int32_t)((scw >> 4) & 15u), o.m1 = (int32_t)((scw >> 12) & 15u);
+        o.m2 = (int32_t)((scw >> 20) & 15u), o.m3 = (int32_t)(scw >> 28);
+        const uint32_t dd = *(const uint32_t *)(b + 80);
+        o.d = pm_h2f(dd & 0xffffu);
+        o.dm = pm_h2f(dd >> 16);
+    } else if constexpr (Q == PM_QUANT_IQ2_XXS) {
+        const uint8_t *b = row + (p >> 2) * PM_IQ2_XXS_BYTES;
+        const uint32_t sp = p & 3u;
+        uint32_t aux[4];
+        pm_lds_words<4>(b + 2 + 16 * sp, aux);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            int32_t a0, a1, b0, b1;
+            pm_iq2_signed(grid[(aux[0] >> (8 * k)) & 0xffu], pm_ksigns_dev((aux[1] >> (7 * k)) & 127u), a0, a1);
+            pm_iq2_signed(grid[(aux[2] >> (8 * k)) & 0xffu], pm_ksigns_dev((aux[3] >> (7 * k)) & 127u), b0, b1);
+            o.w0[2 * k] = (uint32_t)a0, o.w0[2 * k + 1] = (uint32_t)a1;
+            o.w1[2 * k] = (uint32_t)b0, o.w1[2 * k + 1] = (uint32_t)b1;
+        }
+        o.i0 = (int32_t)(2u * (aux[1] >> 28) + 1u);
+        o.i1 = (int32_t)(2u * (aux[3] >> 28) + 1u);
+        o.d = 0.125f * pm_h2f(*(const uint16_t *)b);
+        o.dm = 0.0f;
     } else if constexpr (Q == PM_QUANT_MXFP4) {
-        const uint8_t *b = row + u * PM_MXFP4_BLOCK;
+        const uint8_t *b = row + (size_t)(2u * p) * PM_MXFP4_BLOCK;
         uint32_t q[4];
         pm_lds_words<4>(b + 1, q);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            o.w[i] = pm_e2m1x4(q[i] & 0x0f0f0f0fu);
-            o.w[4 + i] = pm_e2m1x4((q[i] >> 4) & 0x0f0f0f0fu);
+            o.w0[i] = (uint32_t)pm_e2m1x4(q[i] & 0x0f0f0f0fu);
+            o.w0[4 + i] = (uint32_t)pm_e2m1x4((q[i] >> 4) & 0x0f0f0f0fu);
         }
-        o.A = pm_mxfp4_scale_half(b[0]);
-        o.B = 0.0f;
-        o.ma = o.mb = 0;
-    } else if constexpr (Q == PM_QUANT_Q8_0) {
-        const uint8_t *b = row + u * PM_Q8_0_BLOCK;
-        uint32_t q[8];
-        pm_lds_words<8>(b + 2, q);
+        o.d = pm_mxfp4_scale_half(b[0]);
+        if (two) {
+            pm_lds_words<4>(b + PM_MXFP4_BLOCK + 1, q);
 #pragma unroll
-        for (int i = 0; i < 8; i++) o.w[i] = (int32_t)q[i];
-        o.A = pm_h2f(*(const uint16_t *)b);
-        o.B = 0.0f;
-        o.ma = o.mb = 0;
+            for (int i = 0; i < 4; i++) {
+                o.w1[i] = (uint32_t)pm_e2m1x4(q[i] & 0x0f0f0f0fu);
+                o.w1[4 + i] = (uint32_t)pm_e2m1x4((q[i] >> 4) & 0x0f0f0f0fu);
+            }
+            o.dm = pm_mxfp4_scale_half(b[PM_MXFP4_BLOCK]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) o.w1[i] = 0u;
+            o.dm = 0.0f;
+        }
+    } else if constexpr (Q == PM_QUANT_Q8_0) {
+        const uint8_t *b = row + (size_t)(2u * p) * PM_Q8_0_BLOCK;
+        pm_lds_words<8>(b + 2, o.w0);
+        o.d = pm_h2f(*(const uint16_t *)b);
+        if (two) {
+            pm_lds_words<8>(b + PM_Q8_0_BLOCK + 2, o.w1);
+            o.dm = pm_h2f(*(const uint16_t *)(b + PM_Q8_0_BLOCK));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) o.w1[i] = 0u;
+            o.dm = 0.0f;
+        }
     }
 }
 
-/* staged activations of one token tile in shared memory:
- *   lo/hi planes: [TT][n_units] x 16 bytes; bs: [TT][n_units] (int16 pair); d: [TT][nblk] */
-struct pm_acts {
-    uint4 *lo, *hi;
-    float *d;
-    int32_t *bs;
-    uint32_t n_units, nblk;
+/* the pair's contribution for one token (before the q8_K block scale) */
+template <int Q>
+__device__ __forceinline__ float pm_pair_dot(const pm_wp &w, const uint4 &A, const uint4 &B, const uint4 &C,
+                                             const uint4 &D, const int4 &bs) {
+    int c0, c1;
+    if constexpr (Q == PM_QUANT_Q4_K) {
+        c0 = pm_dp4a_us(w.w0[0], (int)A.x, 0);
+        c1 = pm_dp4a_us(w.w1[0], (int)C.x, 0);
+        c0 = pm_dp4a_us(w.w0[1], (int)A.y, c0);
+        c1 = pm_dp4a_us(w.w1[1], (int)C.y, c1);
+        c0 = pm_dp4a_us(w.w0[2], (int)A.z, c0);
+        c1 = pm_dp4a_us(w.w1[2], (int)C.z, c1);
+        c0 = pm_dp4a_us(w.w0[3], (int)A.w, c0);
+        c1 = pm_dp4a_us(w.w1[3], (int)C.w, c1);
+        c0 = pm_dp4a_us(w.w0[4], (int)B.x, c0);
+        c1 = pm_dp4a_us(w.w1[4], (int)D.x, c1);
+        c0 = pm_dp4a_us(w.w0[5], (int)B.y, c0);
+        c1 = pm_dp4a_us(w.w1[5], (int)D.y, c1);
+        c0 = pm_dp4a_us(w.w0[6], (int)B.z, c0);
+        c1 = pm_dp4a_us(w.w1[6], (int)D.z, c1);
+        c0 = pm_dp4a_us(w.w0[7], (int)B.w, c0);
+        c1 = pm_dp4a_us(w.w1[7], (int)D.w, c1);
+    } else {
+        c0 = __dp4a((int)w.w0[0], (int)A.x, 0);
+        c1 = __dp4a((int)w.w1[0], (int)C.x, 0);
+        c0 = __dp4a((int)w.w0[1], (int)A.y, c0);
+        c1 = __dp4a((int)w.w1[1], (int)C.y, c1);
+        c0 = __dp4a((int)w.w0[2], (int)A.z, c0);
+        c1 = __dp4a((int)w.w1[2], (int)C.z, c1);
+        c0 = __dp4a((int)w.w0[3], (int)A.w, c0);
+        c1 = __dp4a((int)w.w1[3], (int)C.w, c1);
+        c0 = __dp4a((int)w.w0[4], (int)B.x, c0);
+        c1 = __dp4a((int)w.w1[4], (int)D.x, c1);
+        c0 = __dp4a((int)w.w0[5], (int)B.y, c0);
+        c1 = __dp4a((int)w.w1[5], (int)D.y, c1);
+        c0 = __dp4a((int)w.w0[6], (int)B.z, c0);
+        c1 = __dp4a((int)w.w1[6], (int)D.z, c1);
+        c0 = __dp4a((int)w.w0[7], (int)B.w, c0);
+        c1 = __dp4a((int)w.w1[7], (int)D.w, c1);
+    }
+    if constexpr (Q == PM_QUANT_Q4_K) {
+        const int32_t ms = w.m0 * (bs.x + bs.y) + w.m1 * (bs.z + bs.w);
+        return w.d * (float)(w.i0 * c0 + w.i1 * c1) - w.dm * (float)ms;
+    } else if constexpr (Q == PM_QUANT_Q2_K) {
+        const int32_t ms = w.m0 * bs.x + w.m1 * bs.y + w.m2 * bs.z + w.m3 * bs.w;
+        return w.d * (float)(c0 + c1) - w.dm * (float)ms;
+    } else if constexpr (Q == PM_QUANT_IQ2_XXS) {
+        return w.d * (float)(w.i0 * c0 + w.i1 * c1);
+    } else {
+        return w.d * (float)c0 + w.dm * (float)c1;
+    }
+}
+
+/* ------------------------------------------------------ reduce-scatter */
+
+/* Halving exchange across the LPR lanes of a row: at each step a lane
+ * keeps one half of its values (chosen by one lane-index bit) and adds
+ * the partner's copy of that half.  idx returns the original index of
+ * v[0]; afterwards a lane holds max(V / LPR, 1) consecutive totals. */
+template <int V, int LPR, int S = 0>
+struct pm_rs {
+    static __device__ __forceinline__ void run(float *v, uint32_t lane, int &idx) {
+        constexpr int Vc = V >> S, H = Vc / 2, O = LPR >> (S + 1);
+        if constexpr (Vc > 1 && O >= 1) {
+            const bool bit = (lane & (uint32_t)O) != 0;
+#pragma unroll
+            for (int i = 0; i < H; i++) {
+                const float send = bit ? v[i] : v[i + H];
+                const float keep = bit ? v[i + H] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+            }
+            if (bit) idx += H;
+            pm_rs<V, LPR, S + 1>::run(v, lane, idx);
+        } else if constexpr (Vc == 1) {
+            /* one value left: finish the sum over the remaining lane bits */
+#pragma unroll
+            for (int o = O; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
 };
 
-__host__ __device__ __forceinline__ uint32_t pm_acts_bytes(uint32_t TT, uint32_t n_units) {
-    const uint32_t nblk = (n_units + 7) / 8;
-    return TT * (n_units * 36u + nblk * 4u) + 64u;
-}
+/* ------------------------------------------------------ one stage */
 
-__device__ __forceinline__ pm_acts pm_acts_carve(uint8_t *p, uint32_t TT, uint32_t n_units) {
-    pm_acts a;
-    a.n_units = n_units;
-    a.nblk = (n_units + 7) / 8;
-    a.lo = (uint4 *)p;
-    a.hi = a.lo + TT * n_units;
-    a.bs = (int32_t *)(a.hi + TT * n_units);
-    a.d = (float *)(a.bs + TT * n_units);
-    return a;
-}
-
-/* copy nt tokens' q8_K rows (292-byte blocks) into the planes; all threads */
-__device__ __forceinline__ void pm_acts_stage(const pm_acts &a, uint32_t nt, const pm_block_q8K *const *rows) {
-    const uint32_t words = a.n_units * 8u; /* int32 words of qs per token */
-    for (uint32_t i = threadIdx.x; i < nt * words; i += blockDim.x) {
-        const uint32_t ti = i / words, wdx = i % words;
-        const uint32_t u = wdx >> 3, k = wdx & 7u;
-        const int32_t v = __ldcg((const int32_t *)((const uint8_t *)(rows[ti] + (u >> 3)) + 4 + 32 * (u & 7u)) + k);
-        int32_t *dst = (int32_t *)(k < 4 ? a.lo + ti * a.n_units + u : a.hi + ti * a.n_units + u);
-        dst[k & 3u] = v;
-    }
-    for (uint32_t i = threadIdx.x; i < nt * a.n_units; i += blockDim.x) {
-        const uint32_t ti = i / a.n_units, u = i % a.n_units;
-        const pm_block_q8K *blk = rows[ti] + (u >> 3);
-        a.bs[ti * a.n_units + u] = __ldcg((const int32_t *)((const uint8_t *)blk + 260 + 4 * (u & 7u)));
-        if ((u & 7u) == 0) a.d[ti * a.nblk + (u >> 3)] = __ldcg(&blk->d);
-    }
-}
-
-/* shared-memory layout of one engine pass (computed on the host) */
-struct pm_pass {
-    uint32_t S;        /* ring stages per warp */
-    uint32_t rw;       /* rows per stage */
-    uint32_t stage;    /* bytes per stage */
-    uint32_t lpr;      /* lanes per row (one lane per pair of units) */
-    uint32_t off_bar;  /* PM_WARPS * S mbarriers */
-    uint32_t off_acts; /* token-tile planes */
-    uint32_t off_tok;  /* TT token-row pointers */
-    uint32_t off_ring; /* PM_WARPS rings of S stages */
-    uint32_t smem;     /* total dynamic shared memory */
+struct pm_rowjob {
+    const uint8_t *w[2]; /* the stage's row 0 of each matrix (shared memory) */
+    uint64_t rb;
+    uint32_t rows, npair, n_units, row_g, nt, act, ostride;
+    pm_acts acts;
+    const uint64_t *grid;
+    const uint32_t *tokpair; /* (token, slot) pair id of each token of the unit */
+    float *out;
+    const float *b0, *b1; /* gate / up bias rows of the expert (or null) */
+    const float *wts;     /* route weight per pair */
 };
+
+/* EPI 0: gate/up -> mid = glu(g + bg, u + bu) * w;  EPI 1: down -> partial */
+template <int Q, int NMAT, int NT, int LPR, int EPI>
+__device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
+    constexpr int RPP = 32 / LPR;
+    constexpr int NTP = NT <= 1 ? 1 : (NT <= 2 ? 2 : (NT <= 4 ? 4 : 8));
+    constexpr int V = NMAT * NTP;
+    constexpr int K = V >= LPR ? V / LPR : 1;
+    const uint32_t lane = threadIdx.x & 31u, sub = lane / LPR, sl = lane % LPR;
+    const pm_acts &ac = jb.acts;
+    const uint32_t P = ac.P;
+    for (uint32_t j0 = 0; j0 < jb.rows; j0 += RPP) {
+        const uint32_t j = j0 + sub;
+        const bool rv = j < jb.rows;
+        float v[V];
+#pragma unroll
+        for (int i = 0; i < V; i++) v[i] = 0.0f;
+        if (rv) {
+            for (uint32_t p = sl; p < jb.npair; p += LPR) {
+                const bool two = 2u * p + 1u < jb.n_units;
+                pm_wp W[NMAT];
+#pragma unroll
+                for (int m = 0; m < NMAT; m++) pm_decode_pair<Q>(jb.w[m] + (size_t)j * jb.rb, p, two, jb.grid, W[m]);
+                const uint32_t blk = p >> 2;
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    const uint4 A = ac.x[(0 * PM_TT + t) * P + p];
+                    const uint4 B = ac.x[(1 * PM_TT + t) * P + p];
+                    const uint4 C = ac.x[(2 * PM_TT + t) * P + p];
+                    const uint4 D = ac.x[(3 * PM_TT + t) * P + p];
+                    int4 bs = make_int4(0, 0, 0, 0);
+                    if constexpr (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bs = ac.bs[t * P + p];
+                    const float yd = ac.d[t * ac.NB + blk];
+#pragma unroll
+                    for (int m = 0; m < NMAT; m++)
+                        v[m * NTP + t] = fmaf(yd, pm_pair_dot<Q>(W[m], A, B, C, D, bs), v[m * NTP + t]);
+                    /* keep at most two tokens' activations live (no spills at NT = 8) */
+                    if ((t & 1) == 1) asm volatile("" ::: "memory");
+                }
+            }
+        }
+        int idx = 0;
+        pm_rs<V, LPR>::run(v, lane, idx);
+        /* lanes that hold a distinct total (the rest hold copies) */
+        const bool owner = V >= LPR || (sl & (uint32_t)(LPR / V - 1)) == 0;
+        if constexpr (NMAT == 2) {
+            /* the first exchange split gate | up: the partner lane holds up */
+            float u[K];
+#pragma unroll
+            for (int i = 0; i < K; i++) u[i] = __shfl_xor_sync(0xffffffffu, v[i], LPR / 2);
+            if (rv && owner && idx < NTP) {
+#pragma unroll
+                for (int i = 0; i < K; i++) {
+                    const uint32_t t = (uint32_t)(idx + i);
+                    if (t < jb.nt) {
+                        const uint32_t row = jb.row_g + j, pr = jb.tokpair[t];
+                        float g = v[i], up = u[i];
+                        if (jb.b0) g += jb.b0[row];
+                        if (jb.b1) up += jb.b1[row];
+                        jb.out[(size_t)pr * jb.ostride + row] = pm_glu(g, up, jb.act) * jb.wts[pr];
+                    }
+                }
+            }
+        } else {
+            if (rv && owner) {
+#pragma unroll
+                for (int i = 0; i < K; i++) {
+                    const uint32_t t = (uint32_t)(idx + i);
+                    if (t < jb.nt) jb.out[(size_t)jb.tokpair[t] * jb.ostride + jb.row_g + j] = v[i];
+                }
+            }
+        }
+    }
+}
+
+template <int Q, int NMAT, int LPR, int EPI>
+__device__ __forceinline__ void pm_rows_nt(const pm_rowjob &jb) {
+    switch (jb.nt) {
+    case 1: pm_rows<Q, NMAT, 1, LPR, EPI>(jb); break;
+    case 2: pm_rows<Q, NMAT, 2, LPR, EPI>(jb); break;
+    case 3: pm_rows<Q, NMAT, 3, LPR, EPI>(jb); break;
+    case 4: pm_rows<Q, NMAT, 4, LPR, EPI>(jb); break;
+    case 5:
+    case 6: pm_rows<Q, NMAT, 6, LPR, EPI>(jb); break;
+    default: pm_rows<Q, NMAT, 8, LPR, EPI>(jb); break;
+    }
+}
+
+template <int Q, int NMAT, int EPI>
+__device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, uint32_t lpr) {
+    if (lpr == 16u)
+        pm_rows_nt<Q, NMAT, 16, EPI>(jb);
+    else
+        pm_rows_nt<Q, NMAT, 4, EPI>(jb);
+}
+
+/* ------------------------------------------------------ stage copies */
 
 /* copy one stage (rows of NMAT matrices) with 1-D bulk copies: each piece
  * is rounded out to 16-byte boundaries, so the staged byte at global
- * address g sits at dst + off(m) + (g & 15); returns expected bytes */
+ * address g sits at dst + off(m) + (g & 15) */
 template <int NMAT>
 __device__ __forceinline__ void pm_issue_stage(uint8_t *dst, uint64_t *bar, const uint8_t *const *src,
                                                uint32_t bytes) {
@@ -188,214 +501,30 @@ __device__ __forceinline__ const uint8_t *pm_stage_ptr(const uint8_t *dst, const
     return dst + off + ((uintptr_t)src[m] & 15u);
 }
 
-/* quantize nt f32 rows of `n` values to q8_K (CPU-lane math, as
- * pm_q8k_warp) straight into the planes: one warp per (token, 256-block);
- * a lane holds 8 consecutive values = a quarter of one 32-value unit */
-__device__ __forceinline__ void pm_acts_stage_f32(const pm_acts &a, uint32_t nt, const float *const *rows,
-                                                  uint32_t n) {
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (uint32_t job = warp; job < nt * a.nblk; job += nw) {
-        const uint32_t ti = job / a.nblk, b = job % a.nblk;
-        const float *src = rows[ti] + (size_t)b * 256u;
-        const uint32_t valid = n - b * 256u < 256u ? n - b * 256u : 256u;
-        float v[8], amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const uint32_t e = lane * 8u + (uint32_t)i;
-            v[i] = e < valid ? __ldcg(src + e) : 0.0f;
-            amax = fmaxf(amax, fabsf(v[i]));
-        }
-#pragma unroll
-        for (int m = 16; m > 0; m >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-        uint32_t qv[8];
-        int s = 0;
-        const float inv = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            float r = amax == 0.0f ? 0.0f : roundf(__fmul_rn(v[i], inv));
-            r = fminf(fmaxf(r, -127.0f), 127.0f);
-            const int qi = (int)r;
-            s += qi;
-            qv[i] = (uint32_t)(uint8_t)(int8_t)qi;
-        }
-        s += __shfl_xor_sync(0xffffffffu, s, 1);    /* 16-value group sum (lane pair) */
-        const int s_hi = __shfl_down_sync(0xffffffffu, s, 2); /* the unit's second group */
-        const uint32_t u = b * 8u + (lane >> 2);
-        if (u < a.n_units) {
-            const uint32_t q = lane & 3u; /* quarter of the unit */
-            uint32_t *dst = (uint32_t *)(q < 2 ? a.lo + ti * a.n_units + u : a.hi + ti * a.n_units + u);
-            dst[(q & 1u) * 2u] = qv[0] | (qv[1] << 8) | (qv[2] << 16) | (qv[3] << 24);
-            dst[(q & 1u) * 2u + 1u] = qv[4] | (qv[5] << 8) | (qv[6] << 16) | (qv[7] << 24);
-            if (q == 0)
-                a.bs[ti * a.n_units + u] = (int32_t)((uint32_t)(uint16_t)(int16_t)s | ((uint32_t)(uint16_t)(int16_t)s_hi << 16));
-        }
-        if (lane == 0) a.d[ti * a.nblk + b] = amax == 0.0f ? 0.0f : __fdiv_rn(amax, 127.0f);
-    }
-}
+/* ------------------------------------------------------ launch geometry */
 
-/* Segment interface for pm_gemv_warps:
- *   const uint8_t* base(m)                 first row of the CTA's tile in matrix m
- *   uint32_t ntok()                         tokens of the work unit (<= TT)
- *   const pm_block_q8K* tok(ti)             q8_K row of token ti, or
- *   const float* tok_f32(ti)                its f32 row (Seg::F32 true: quantized while staging)
- *   void epi(row, ti, const float* v)       one lane per (row, token)
- *
- * Warp-private pipelines: after the token tile is staged (one CTA barrier),
- * warp w owns stages c = w, w + 8, ... of rw rows each and streams them
- * through its own S-deep ring and mbarriers; there is no CTA-wide
- * synchronisation while rows stream, so a warp waiting on memory never
- * holds the others back.  Returns false on a wait timeout (err set). */
-template <int Q, int NMAT, int TT, class Seg>
-__device__ bool pm_gemv_warps(Seg &seg, uint8_t *smem, const pm_pass &ps, uint32_t nrows, uint64_t rb,
-                              uint32_t n_units, const uint64_t *grid, uint32_t *err) {
-    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    const uint32_t nt = seg.ntok() < (uint32_t)TT ? seg.ntok() : (uint32_t)TT;
-    const pm_block_q8K **tokrows = (const pm_block_q8K **)(smem + ps.off_tok);
-    uint64_t *bars = (uint64_t *)(smem + ps.off_bar) + warp * ps.S;
-    uint8_t *ring = smem + ps.off_ring + (size_t)warp * ps.S * ps.stage;
-    const pm_acts acts = pm_acts_carve(smem + ps.off_acts, TT, n_units);
-    if constexpr (Seg::F32) {
-        if (tid < nt) ((const float **)tokrows)[tid] = seg.tok_f32(tid);
-    } else {
-        if (tid < nt) tokrows[tid] = seg.tok(tid);
-    }
-    if (lane == 0) {
-        for (uint32_t i = 0; i < ps.S; i++) pm_mbar_init(bars + i, 1);
-        pm_fence_barrier_init();
-    }
-    __syncthreads();
-    if constexpr (Seg::F32)
-        pm_acts_stage_f32(acts, nt, (const float *const *)tokrows, seg.n_f32);
-    else
-        pm_acts_stage(acts, nt, tokrows);
-    __syncthreads();
+/* per matrix kind (0 routed experts, 1 shared expert) */
+struct pm_skind {
+    uint64_t rb;      /* row bytes */
+    uint32_t n_units; /* 32-value units per row */
+    uint32_t npair;
+    uint32_t lpr;     /* lanes per row: 16 or 4 */
+    uint32_t rw;      /* rows per stage */
+};
 
-    const uint32_t rw = ps.rw, lpr = ps.lpr;
-    const uint32_t n_stage_all = (nrows + rw - 1) / rw;
-    const uint32_t mine = n_stage_all > warp ? (n_stage_all - warp + PM_WARPS - 1) / PM_WARPS : 0u;
-    const uint32_t rows_per_pass = 32u / lpr;
-    const uint32_t sub = lane / lpr, sl = lane % lpr;
+/* shared-memory layout of one stream-K launch (computed on the host) */
+struct pm_skp {
+    pm_skind k[2];
+    uint32_t S;      /* ring stages per warp */
+    uint32_t stage;  /* bytes per stage */
+    uint32_t P, NB;  /* activation tile geometry (max over kinds) */
+    uint32_t off_bar, off_seg, off_acts, off_ring, smem;
+};
 
-    auto geom = [&](uint32_t i, const uint8_t **src, uint32_t &r0, uint32_t &rows) {
-        r0 = (warp + PM_WARPS * i) * rw;
-        rows = nrows - r0 < rw ? nrows - r0 : rw;
-#pragma unroll
-        for (int m = 0; m < NMAT; m++) src[m] = seg.base(m) + (size_t)r0 * rb;
-    };
-    if (lane == 0) {
-        const uint32_t pro = mine < ps.S ? mine : ps.S;
-        for (uint32_t i = 0; i < pro; i++) {
-            const uint8_t *src[NMAT];
-            uint32_t r0, rows;
-            geom(i, src, r0, rows);
-            pm_issue_stage<NMAT>(ring + (size_t)i * ps.stage, bars + i, src, rows * (uint32_t)rb);
-        }
-    }
-    bool ok = true;
-    for (uint32_t i = 0; i < mine; i++) {
-        const uint32_t st = i % ps.S;
-        if (!pm_mbar_wait_sleep(bars + st, (i / ps.S) & 1u, err)) {
-            ok = false;
-            if (lane == 0) { /* drain this warp's copies still in flight */
-                const uint32_t last = i + ps.S - 1 < mine ? i + ps.S - 1 : mine - 1;
-                for (uint32_t d = i; d <= last; d++) pm_mbar_wait(bars + (d % ps.S), (d / ps.S) & 1u, nullptr);
-            }
-            break;
-        }
-        const uint8_t *src[NMAT];
-        uint32_t r0, rows;
-        geom(i, src, r0, rows);
-        const uint8_t *stg = ring + (size_t)st * ps.stage;
-        const uint8_t *rowp[NMAT];
-#pragma unroll
-        for (int m = 0; m < NMAT; m++) rowp[m] = pm_stage_ptr<NMAT>(stg, src, rows * (uint32_t)rb, m);
-        for (uint32_t jb = 0; jb < rows; jb += rows_per_pass) {
-            const uint32_t j = jb + sub;
-            const bool rv = j < rows;
-            float acc[NMAT][TT];
-#pragma unroll
-            for (int m = 0; m < NMAT; m++)
-#pragma unroll
-                for (int t = 0; t < TT; t++) acc[m][t] = 0.0f;
-            if (rv) {
-                /* a lane takes a PAIR of adjacent units (same super-block:
-                 * header and packed bytes load once for both) */
-                for (uint32_t u0 = 2u * sl; u0 < n_units; u0 += 2u * lpr) {
-                    const bool two = u0 + 1 < n_units;
-                    pm_wunit wu[NMAT][2];
-#pragma unroll
-                    for (int m = 0; m < NMAT; m++) {
-                        pm_decode<Q>(rowp[m] + (size_t)j * rb, u0, grid, wu[m][0]);
-                        if (two) pm_decode<Q>(rowp[m] + (size_t)j * rb, u0 + 1, grid, wu[m][1]);
-                    }
-#pragma unroll
-                    for (int t = 0; t < TT; t++) {
-                        if (t < (int)nt) {
-                            const float yd = acts.d[t * acts.nblk + (u0 >> 3)];
-#pragma unroll
-                            for (int h = 0; h < 2; h++) {
-                                if (h == 1 && !two) break;
-                                const uint32_t u = u0 + h;
-                                const uint4 lo = acts.lo[t * n_units + u], hi = acts.hi[t * n_units + u];
-                                int32_t bp = 0;
-                                if (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bp = acts.bs[t * n_units + u];
-#pragma unroll
-                                for (int m = 0; m < NMAT; m++) {
-                                    const pm_wunit &wv = wu[m][h];
-                                    int s0 = __dp4a(wv.w[0], (int)lo.x, 0);
-                                    int s1 = __dp4a(wv.w[4], (int)hi.x, 0);
-                                    s0 = __dp4a(wv.w[1], (int)lo.y, s0);
-                                    s1 = __dp4a(wv.w[5], (int)hi.y, s1);
-                                    s0 = __dp4a(wv.w[2], (int)lo.z, s0);
-                                    s1 = __dp4a(wv.w[6], (int)hi.z, s1);
-                                    s0 = __dp4a(wv.w[3], (int)lo.w, s0);
-                                    s1 = __dp4a(wv.w[7], (int)hi.w, s1);
-                                    float cv = wv.A * (float)(s0 + s1);
-                                    if (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) {
-                                        const int32_t msum = wv.ma * (int32_t)(int16_t)(bp & 0xffff) +
-                                                             wv.mb * (int32_t)(int16_t)((uint32_t)bp >> 16);
-                                        cv -= wv.B * (float)msum;
-                                    }
-                                    acc[m][t] = fmaf(yd, cv, acc[m][t]);
-                                }
-                            }
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int m = 0; m < NMAT; m++)
-#pragma unroll
-                for (int t = 0; t < TT; t++) {
-                    if (t < (int)nt) {
-                        float v = acc[m][t];
-                        for (uint32_t o = lpr >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                        acc[m][t] = v;
-                    }
-                }
-            if (rv) {
-                for (uint32_t t = sl; t < nt; t += lpr) { /* lane sl writes token sl */
-                    float v[NMAT];
-#pragma unroll
-                    for (int m = 0; m < NMAT; m++) {
-                        float pick = 0.0f;
-#pragma unroll
-                        for (int q = 0; q < TT; q++)
-                            if (q == (int)t) pick = acc[m][q];
-                        v[m] = pick;
-                    }
-                    seg.epi(r0 + j, t, v);
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0 && i + ps.S < mine) { /* refill the stage just consumed */
-            pm_fence_proxy_async();
-            const uint8_t *s2[NMAT];
-            uint32_t r2, rows2;
-            geom(i + ps.S, s2, r2, rows2);
-            pm_issue_stage<NMAT>(ring + (size_t)st * ps.stage, bars + st, s2, rows2 * (uint32_t)rb);
-        }
-    }
-    return __syncthreads_or(!ok) == 0;
-}
+/* one segment of a CTA's slice: rows [r0, r1) of one work unit */
+struct pm_segi {
+    const uint8_t *base[2]; /* row 0 of each matrix */
+    const uint32_t *pairs;  /* the unit's (token, slot) pair ids */
+    const float *b0, *b1;   /* bias rows (gate/up) */
+    uint32_t nt, r0, r1, kind;
+};
