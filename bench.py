@@ -68,6 +68,9 @@ class ClockSampler:
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
+            t0 = time.time()  # nvidia-smi takes a moment to start: wait for its first sample
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except FileNotFoundError:
             self.proc = None
         return self
@@ -427,7 +430,7 @@ def main():
             roof = {"bound": "hbm", "kernel": "pm_layer_gu_kernel (gate/up + glu + q8_K of mid)",
                     "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
                     "traffic": None, "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms,
-                    "stage_ms": dict(zip(["router_logits", "q8k_x", "select_csr", "gate_up", "down_combine"],
+                    "stage_ms": dict(zip(["router_logits+q8k_x", "(fused)", "select_csr", "gate_up", "down_combine"],
                                          map(float, st_ms))),
                     "layer": {"algorithmic_bytes": layer_bytes, "eager_ms": layer_ms,
                               "eager_gbs": layer_bytes / (layer_ms / 1e3) / 1e9,

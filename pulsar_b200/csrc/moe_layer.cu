@@ -37,8 +37,8 @@
 #include "pm_gemv.cuh"
 
 int pm_launch_q8k(void *out, const float *x, uint32_t in_dim, uint32_t n_rows, cudaStream_t st);
-int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
-                            uint32_t in_dim, uint32_t n_tok, cudaStream_t st);
+int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
+                               uint32_t in_dim, uint32_t n_tok, void *xq, cudaStream_t st);
 int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32_t mode, uint32_t n_shexp,
                       uint32_t n_group, uint32_t topk_group);
 
@@ -122,11 +122,29 @@ struct pm_layer_args {
 
 /* ============================================ 3: select + CSR build */
 
-__global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_constant__ pm_layer_args a) {
+#define PM_SEL_STAGE 16384u /* routed pairs staged in shared memory (u16 each) */
+#define PM_SEL_WARPS 8u      /* tokens per CTA (one warp each) */
+#define PM_SEL_MASK_T 448u   /* batches up to this size fill pairs from token masks */
+
+/* uint4 component-wise sum */
+__device__ __forceinline__ uint4 pm_add4(uint4 x, uint4 y) {
+    return make_uint4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
+}
+
+/* Phase 1: one warp per token picks its top-k (pm_select_token).  Phase 2
+ * (the last CTA to arrive): group the routed (token, slot) pairs of this
+ * shard by expert.  Per expert e with v pairs: one item, ceil(v / PM_TT)
+ * work units, and the stream-K cost (PM_SK_CR * units + v); a block-wide
+ * exclusive scan over experts places everything.  Pairs are filled in
+ * (token, slot) order: a token selects an expert at most once, so the
+ * rank of pair (t, s) in its expert's list is the number of earlier tokens
+ * that chose the same expert - a popcount over a per-expert token mask. */
+__global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_constant__ pm_layer_args a) {
     extern __shared__ __align__(16) uint8_t sm[];
-    __shared__ uint32_t is_last, tot_pairs, tot_items, tot_work, tot_cost;
+    __shared__ uint32_t is_last;
+    __shared__ uint4 wsum[PM_SEL_WARPS], carry;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
-    const uint32_t token = blockIdx.x * 4u + wid;
+    const uint32_t token = blockIdx.x * PM_SEL_WARPS + wid;
     if (token < a.T) {
         float *score = (float *)sm + (size_t)wid * 2 * a.E;
         pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0, a.n_group,
@@ -142,67 +160,107 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+
     /* ---- the last CTA: CSR by expert over routed pairs in [lo, hi) ---- */
-    uint32_t *cnt = (uint32_t *)sm; /* [E] counts, then fill cursors */
-    for (uint32_t e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
-    __syncthreads();
     const uint32_t n_routed = a.T * a.k;
+    uint32_t *cnt = (uint32_t *)sm; /* [E] counts, then start offsets */
+    const uint32_t mw = (a.T + 31u) / 32u;
+    uint32_t *mask = cnt + a.E; /* [E][mw] token masks (small batches) */
+    const bool masks = a.T <= PM_SEL_MASK_T;
+    /* the selections, read once with independent loads (u16; 0xffff = not in this shard) */
+    uint16_t *ss = (uint16_t *)(sm + (size_t)PM_SEL_WARPS * 2 * a.E * 4);
+    const bool staged = n_routed <= PM_SEL_STAGE && a.E < 65535u;
+    auto sel_at = [&](uint32_t q) -> uint32_t {
+        uint32_t e;
+        if (staged) {
+            e = ss[q];
+            return e == 0xffffu ? UINT32_MAX : e;
+        }
+        e = (uint32_t)__ldcg(a.sel + (q / a.k) * a.n_slot + q % a.k);
+        return e >= a.lo && e < a.hi ? e : UINT32_MAX;
+    };
+    for (uint32_t e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
+    if (masks)
+        for (uint32_t i = threadIdx.x; i < a.E * mw; i += blockDim.x) mask[i] = 0;
+    if (staged) {
+#pragma unroll 4
+        for (uint32_t q = threadIdx.x; q < n_routed; q += blockDim.x) {
+            const uint32_t e = (uint32_t)__ldcg(a.sel + (q / a.k) * a.n_slot + q % a.k);
+            ss[q] = (uint16_t)(e >= a.lo && e < a.hi ? e : 0xffffu);
+        }
+    }
+    if (threadIdx.x == 0) carry = make_uint4(0, 0, 0, 0);
+    __syncthreads();
     for (uint32_t q = threadIdx.x; q < n_routed; q += blockDim.x) {
-        const uint32_t e = (uint32_t)__ldcg(a.sel + (q / a.k) * a.n_slot + q % a.k);
-        if (e >= a.lo && e < a.hi) atomicAdd(&cnt[e], 1u);
+        const uint32_t e = sel_at(q);
+        if (e == UINT32_MAX) continue;
+        atomicAdd(&cnt[e], 1u);
+        if (masks) {
+            const uint32_t t = q / a.k;
+            atomicOr(&mask[e * mw + t / 32u], 1u << (t % 32u));
+        }
     }
     __syncthreads();
-    if (wid == 0) {
-        /* exclusive scans over experts: pair offsets, item indices, work
-         * units and the stream-K cost line (per-row cost PM_SK_CR + nt of
-         * each of the expert's chunks: all full but the last) */
-        uint32_t carry_p = 0, carry_i = 0, carry_w = 0, carry_c = 0;
-        for (uint32_t c = 0; c < a.E; c += 32u) {
-            const uint32_t e = c + lane;
-            const uint32_t v = e < a.E ? cnt[e] : 0u;
-            const uint32_t nw = (v + PM_TT - 1) / PM_TT, cost = PM_SK_CR * nw + v;
-            uint32_t ip = v, ii = v ? 1u : 0u, iw = nw, ic = cost;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t up = __shfl_up_sync(0xffffffffu, ip, o);
-                const uint32_t ui = __shfl_up_sync(0xffffffffu, ii, o);
-                const uint32_t uw = __shfl_up_sync(0xffffffffu, iw, o);
-                const uint32_t uc = __shfl_up_sync(0xffffffffu, ic, o);
-                if (lane >= (uint32_t)o) ip += up, ii += ui, iw += uw, ic += uc;
-            }
-            const uint32_t start = carry_p + ip - v, item = carry_i + ii - (v ? 1u : 0u), w0 = carry_w + iw - nw;
-            const uint32_t c0 = carry_c + ic - cost;
-            if (e < a.E) {
-                cnt[e] = start;
-                if (v) {
-                    a.item_expert[item] = e;
-                    a.item_start[item] = start;
-                    for (uint32_t j = 0; j < nw; j++) {
-                        const uint32_t nt = v - j * PM_TT < PM_TT ? v - j * PM_TT : PM_TT;
-                        a.work_item[w0 + j] = item;
-                        a.work_t0[w0 + j] = j * PM_TT;
-                        a.wd[w0 + j] = make_uint4(e, start + j * PM_TT, nt, 0u);
-                        a.sk_c[w0 + j] = c0 + j * (PM_SK_CR + PM_TT);
-                    }
+    /* exclusive scan over experts of (pairs, items, work units, cost) */
+#pragma unroll 1
+    for (uint32_t c0 = 0; c0 < a.E; c0 += blockDim.x) {
+        const uint32_t e = c0 + threadIdx.x;
+        const uint32_t v = e < a.E ? cnt[e] : 0u;
+        const uint32_t nw = (v + PM_TT - 1) / PM_TT;
+        const uint4 own = make_uint4(v, v ? 1u : 0u, nw, PM_SK_CR * nw + v);
+        uint4 x = own;
+#pragma unroll 1
+        for (uint32_t o = 1; o < 32u; o <<= 1) {
+            const uint4 y = make_uint4(__shfl_up_sync(0xffffffffu, x.x, o), __shfl_up_sync(0xffffffffu, x.y, o),
+                                       __shfl_up_sync(0xffffffffu, x.z, o), __shfl_up_sync(0xffffffffu, x.w, o));
+            if (lane >= o) x = pm_add4(x, y);
+        }
+        if (lane == 31u) wsum[wid] = x;
+        __syncthreads();
+        uint4 pre = carry;
+#pragma unroll 1
+        for (uint32_t w2 = 0; w2 < wid; w2++) pre = pm_add4(pre, wsum[w2]);
+        const uint4 incl = pm_add4(pre, x);
+        const uint32_t start = incl.x - own.x, item = incl.y - own.y, w0 = incl.z - own.z, cst = incl.w - own.w;
+        if (e < a.E) {
+            cnt[e] = start;
+            if (v) {
+                a.item_expert[item] = e;
+                a.item_start[item] = start;
+#pragma unroll 1
+                for (uint32_t j = 0; j < nw; j++) {
+                    const uint32_t nt = v - j * PM_TT < PM_TT ? v - j * PM_TT : PM_TT;
+                    a.work_item[w0 + j] = item;
+                    a.work_t0[w0 + j] = j * PM_TT;
+                    a.wd[w0 + j] = make_uint4(e, start + j * PM_TT, nt, 0u);
+                    a.sk_c[w0 + j] = cst + j * (PM_SK_CR + PM_TT);
                 }
             }
-            carry_p += __shfl_sync(0xffffffffu, ip, 31);
-            carry_i += __shfl_sync(0xffffffffu, ii, 31);
-            carry_w += __shfl_sync(0xffffffffu, iw, 31);
-            carry_c += __shfl_sync(0xffffffffu, ic, 31);
         }
-        if (lane == 0) tot_pairs = carry_p, tot_items = carry_i, tot_work = carry_w, tot_cost = carry_c;
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1u) carry = incl;
+        __syncthreads();
     }
-    __syncthreads();
-    if (wid == 0) {
-        /* stable fill: entries in (token, slot) order, ranks via match_any */
+    const uint32_t tot_pairs = carry.x, tot_items = carry.y, tot_work = carry.z, tot_cost = carry.w;
+    /* fill the pair lists in (token, slot) order */
+    if (masks) {
+        for (uint32_t q = threadIdx.x; q < n_routed; q += blockDim.x) {
+            const uint32_t e = sel_at(q);
+            if (e == UINT32_MAX) continue;
+            const uint32_t t = q / a.k;
+            const uint32_t *m = mask + e * mw;
+            uint32_t rank = __popc(m[t / 32u] & ((1u << (t % 32u)) - 1u));
+            for (uint32_t i = 0; i < t / 32u; i++) rank += __popc(m[i]);
+            a.pairs[cnt[e] + rank] = t * a.n_slot + q % a.k;
+        }
+    } else if (wid == 0) {
+        /* large batches: one warp in order, ranks via match_any */
         for (uint32_t c = 0; c < n_routed; c += 32u) {
             const uint32_t q = c + lane;
             uint32_t e = UINT32_MAX, pair = 0;
             if (q < n_routed) {
                 pair = (q / a.k) * a.n_slot + q % a.k;
-                const uint32_t v = (uint32_t)__ldcg(a.sel + pair);
-                if (v >= a.lo && v < a.hi) e = v;
+                e = sel_at(q);
             }
             const uint32_t peers = __match_any_sync(0xffffffffu, e);
             const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
@@ -212,7 +270,6 @@ __global__ void __launch_bounds__(128) pm_layer_select_kernel(const __grid_const
             __syncwarp();
         }
     }
-    __syncthreads();
     /* shared experts (computed on the shard that owns expert 0): one item
      * each over all tokens, appended after the routed items */
     const uint32_t n_sh = a.lo == 0 ? a.S : 0u;
@@ -751,15 +808,15 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
 
     /* 1, 2: logits and q8_K(x) */
     pm_ev(ev, 0, st);
-    if (!pm_launch_router_logits(a.logits, d->router_w, x, d->router_logit_b, L.E, L.H, L.T, st)) return 0;
+    if (!pm_launch_router_logits_q8(a.logits, d->router_w, x, d->router_logit_b, L.E, L.H, L.T, a.xq, st)) return 0;
     pm_ev(ev, 1, st);
-    if (!pm_launch_q8k(a.xq, x, L.H, L.T, st)) return 0;
-    pm_ev(ev, 2, st);
+    pm_ev(ev, 2, st); /* q8_K of x is written by the router kernel */
     /* 3: select + CSR */
-    const uint32_t smem_sel = 4u * 2u * L.E * 4u;
+    const uint32_t n_routed = L.T * L.k;
+    const uint32_t smem_sel = PM_SEL_WARPS * 2u * L.E * 4u + (n_routed <= PM_SEL_STAGE ? 2u * n_routed : 0u);
     static uint64_t done_sel = 0;
     if (!pm_smem_attr(pm_layer_select_kernel, smem_sel, &done_sel)) return 0;
-    pm_layer_select_kernel<<<(L.T + 3u) / 4u, 128, smem_sel, st>>>(a);
+    pm_layer_select_kernel<<<(L.T + PM_SEL_WARPS - 1) / PM_SEL_WARPS, PM_SEL_WARPS * 32u, smem_sel, st>>>(a);
     if (!pm_ok(cudaGetLastError(), "moe layer select launch")) return 0;
     pm_ev(ev, 3, st);
     return pm_layer_dispatch(d->quant, d->n_shared ? d->shared_quant : d->quant, a, L, st, ev);

@@ -37,7 +37,7 @@ __device__ __forceinline__ void pm_warp_argmax(const float *score, uint32_t lo, 
 }
 
 /* one warp per token; scores and probabilities staged in shared memory
- * (4 warps x 2 x n_expert floats).  Semantics of cu:939-1050 plus the
+ * (2 x n_expert floats per warp).  Semantics of cu:939-1050 plus the
  * group-limited pre-selection (n_group > 1). */
 __device__ __forceinline__ void pm_select_token(int32_t *selected, float *weights, const float *logits,
                                                 const float *bias, uint32_t n_expert, uint32_t k_used,

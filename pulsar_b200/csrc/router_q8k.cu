@@ -131,11 +131,131 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
     }
 }
 
-int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
-                            uint32_t in_dim, uint32_t n_tok, cudaStream_t st) {
+/* Token-tiled variant (in_dim % 128 == 0): a CTA stages TPB tokens' rows
+ * of x in shared memory once, already widened to binary64, and its 8
+ * warps each take one expert, so x is read from L2 and converted once
+ * per 8 experts instead of once per expert.  Every (expert, token) dot
+ * keeps the fixed order above (lane partials over i = 128 j + 4 lane + c,
+ * j and c ascending, xor butterfly), so the bits equal the per-warp
+ * kernel's.  With xq set, the CTAs of expert column 0 also write the
+ * tile's q8_K rows (CPU-lane quantizer, pm_q8k_warp). */
+#define PM_RT_G 8 /* 128-wide chunks of a W row in flight per warp */
+template <int TPB>
+__global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, const float *__restrict__ w,
+                                                             const float *__restrict__ x,
+                                                             const float *__restrict__ lbias, uint32_t n_expert,
+                                                             uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq) {
+    extern __shared__ double2 xs[]; /* [TPB][in_dim / 2] */
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t t0 = blockIdx.y * TPB;
+    const uint32_t nt = n_tok - t0 < (uint32_t)TPB ? n_tok - t0 : (uint32_t)TPB;
+    const uint32_t e = blockIdx.x * (blockDim.x >> 5) + warp;
+    const uint32_t nj = in_dim / 128u;
+    const float *wr = w + (uint64_t)(e < n_expert ? e : 0u) * in_dim;
+    /* the first group of W chunks is in flight while x is staged */
+    float4 wv[PM_RT_G];
+#pragma unroll
+    for (int q = 0; q < PM_RT_G; q++)
+        wv[q] = (uint32_t)q < nj ? __ldg((const float4 *)(wr + 128u * q + 4u * lane)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t h4 = in_dim / 4u;
+    for (uint32_t i = threadIdx.x; i < nt * h4; i += blockDim.x) {
+        /* chunk j of token t: lane l's four values at [64 j + l] and [64 j + 32 + l] */
+        const uint32_t t = i / h4, r = i % h4;
+        const float4 v = __ldg((const float4 *)(x + (uint64_t)(t0 + t) * in_dim) + r);
+        const uint32_t o = t * (in_dim / 2u) + 64u * (r >> 5) + (r & 31u);
+        xs[o] = make_double2((double)v.x, (double)v.y);
+        xs[o + 32u] = make_double2((double)v.z, (double)v.w);
+    }
+    if (xq && blockIdx.x == 0) {
+        const uint32_t nb = (in_dim + 255u) / 256u;
+        for (uint32_t job = warp; job < nt * nb; job += blockDim.x >> 5) {
+            const uint32_t t = job / nb, b = job % nb;
+            const uint32_t bn = in_dim - b * 256u < 256u ? in_dim - b * 256u : 256u;
+            const float *src = x + (uint64_t)(t0 + t) * in_dim + b * 256u;
+            pm_q8k_warp(src, bn, xq + (uint64_t)(t0 + t) * nb + b);
+        }
+    }
+    __syncthreads();
+    if (e >= n_expert) return;
+    double p[TPB];
+#pragma unroll
+    for (int t = 0; t < TPB; t++) p[t] = 0.0; /* rows t >= nt hold stale data and are never written */
+    const uint32_t h2 = in_dim / 2u;
+    for (uint32_t g = 0; g < nj; g += PM_RT_G) {
+        float4 nx[PM_RT_G]; /* the next group, loaded while this one is used */
+#pragma unroll
+        for (int q = 0; q < PM_RT_G; q++) {
+            const uint32_t jn = g + PM_RT_G + q;
+            nx[q] = jn < nj ? __ldg((const float4 *)(wr + 128u * jn + 4u * lane)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < PM_RT_G; q++) {
+            const uint32_t j = g + q;
+            if (j < nj) {
+                const double w0 = wv[q].x, w1 = wv[q].y, w2 = wv[q].z, w3 = wv[q].w;
+#pragma unroll
+                for (int t = 0; t < TPB; t++) {
+                    const double2 a = xs[t * h2 + 64u * j + lane], b = xs[t * h2 + 64u * j + 32u + lane];
+                    p[t] = fma(w0, a.x, p[t]);
+                    p[t] = fma(w1, a.y, p[t]);
+                    p[t] = fma(w2, b.x, p[t]);
+                    p[t] = fma(w3, b.y, p[t]);
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < PM_RT_G; q++) wv[q] = nx[q];
+    }
+#pragma unroll
+    for (int t = 0; t < TPB; t++) {
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) p[t] = p[t] + __shfl_xor_sync(0xffffffffu, p[t], m);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < TPB; t++) {
+            if ((uint32_t)t >= nt) break;
+            float l = __double2float_rn(p[t]);
+            if (lbias) l = __fadd_rn(l, lbias[e]);
+            logits[(uint64_t)(t0 + t) * n_expert + e] = l;
+        }
+    }
+}
+
+template <int TPB>
+static int pm_launch_router_tile(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
+                                 uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq, cudaStream_t st) {
+    static uint64_t done = 0;
+    const uint32_t smem = TPB * in_dim * 8u;
+    if (!pm_smem_attr(pm_router_tile_kernel<TPB>, smem, &done)) return 0;
+    dim3 grid((n_expert + 7u) / 8u, (n_tok + TPB - 1) / TPB);
+    pm_router_tile_kernel<TPB><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq);
+    return pm_ok(cudaGetLastError(), "router logits launch");
+}
+
+/* logits (and, with xq, the q8_K rows of x) on stream st */
+int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
+                               uint32_t in_dim, uint32_t n_tok, void *xq, cudaStream_t st) {
+    if (in_dim % 128u == 0 && in_dim <= 25600u) {
+        /* tokens per tile: no more than the batch, x tile within 200 KB */
+        uint32_t tpb = n_tok >= 4 ? 4u : (n_tok >= 2 ? 2u : 1u);
+        while (tpb > 1 && tpb * in_dim * 8u > 200u * 1024u) tpb >>= 1;
+        pm_block_q8K *q = (pm_block_q8K *)xq;
+        switch (tpb) {
+        case 4: return pm_launch_router_tile<4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        case 2: return pm_launch_router_tile<2>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        default: return pm_launch_router_tile<1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        }
+    }
     dim3 grid((n_expert + 3u) / 4u, (n_tok + PM_RT_TOK - 1) / PM_RT_TOK);
     pm_router_logits_kernel<<<grid, 128, 0, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok);
-    return pm_ok(cudaGetLastError(), "router logits launch");
+    if (!pm_ok(cudaGetLastError(), "router logits launch")) return 0;
+    return xq ? pm_launch_q8k(xq, x, in_dim, n_tok, st) : 1;
+}
+
+int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
+                            uint32_t in_dim, uint32_t n_tok, cudaStream_t st) {
+    return pm_launch_router_logits_q8(logits, w, x, lbias, n_expert, in_dim, n_tok, nullptr, st);
 }
 
 /* cu:6526 pulsar_matmul_f32: out[t][r] = W[r] . x[t], here in the fixed
