@@ -208,10 +208,12 @@ typedef struct pulsar_moe_ws_view {
     void *xq;             /* q8_K [n_tok][ceil(H/256)] */
     float *mid;           /* [n_tok * n_slot][F_max] */
     uint32_t *err;        /* error word: bit 0 wait timeout */
-    uint32_t *n_items;    /* [0] expert work items, [1] routed ones (distinct experts), [2] work units */
+    uint32_t *n_items;    /* [0] expert work items, [1] routed ones (distinct experts), [2] work units,
+                           * [3] routed work units, [4] tensor-core tiles, [5] their gate/up K splits */
     uint32_t *item_expert, *item_start, *pairs; /* CSR of (token, slot) pairs by expert */
     uint32_t *work_item, *work_t0;              /* work units: (item, first token of its chunk) */
     float *partial;                             /* [n_tok * n_slot][H] down rows before the combine */
+    uint32_t *tc_tile;                          /* tensor-core tiles: (item, first token) pairs of u32 */
     uint32_t n_slot, f_max;
 } pulsar_moe_ws_view;
 /* pulsar_moe_layer that also records events[0..5] (cudaEvent_t, NULL

@@ -61,7 +61,8 @@ class WsView(ctypes.Structure):
                 ("xq", ctypes.c_void_p), ("mid", ctypes.c_void_p),
                 ("err", ctypes.c_void_p), ("n_items", ctypes.c_void_p), ("item_expert", ctypes.c_void_p),
                 ("item_start", ctypes.c_void_p), ("pairs", ctypes.c_void_p), ("work_item", ctypes.c_void_p),
-                ("work_t0", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("n_slot", ctypes.c_uint32),
+                ("work_t0", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("tc_tile", ctypes.c_void_p),
+                ("n_slot", ctypes.c_uint32),
                 ("f_max", ctypes.c_uint32)]
 
 

@@ -35,6 +35,7 @@
 #include "pm_host.h"
 #include "pm_router.cuh"
 #include "pm_gemv.cuh"
+#include "pm_tc.cuh"
 
 int pm_launch_q8k(void *out, const float *x, uint32_t in_dim, uint32_t n_rows, cudaStream_t st);
 int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
@@ -44,14 +45,32 @@ int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32
 
 __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 
+#define PM_TC_N 64u  /* tokens per tensor-core tile (MMA N) */
+#define PM_TC_MIN 128u /* experts with at least this many tokens take the tensor-core path */
+
+/* formats with a tensor-core (fp16 dequant) path */
+static bool pm_tc_fmt(uint32_t q) { return q == PM_QUANT_Q4_K; }
+
+static int pm_sm_count() {
+    static int sms[64];
+    const int dev = pm_cur_device();
+    if (dev < 0 || dev >= 64) return 148;
+    if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 148;
+    }
+    return sms[dev];
+}
+
 
 /* ------------------------------------------------------------ layout */
 
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
     uint32_t max_work;
-    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, pairs, mid, partial,
-        sel_done, err, total;
+    uint32_t max_tc, ks_max;
+    size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, tc_tile, pairs, mid,
+        midq, tcp, partial, sel_done, err, total;
 };
 
 static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -76,7 +95,7 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.sel = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.w = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.xq = o, o = pm_al(o + (size_t)T * L.hb * PM_Q8_K_BYTES);
-    L.n_items = o, o = pm_al(o + 16);
+    L.n_items = o, o = pm_al(o + 32);
     L.item_expert = o, o = pm_al(o + (size_t)L.max_items * 4);
     L.item_start = o, o = pm_al(o + (size_t)(L.max_items + 1) * 4);
     L.max_work = L.max_items + (uint32_t)(((uint64_t)T * L.n_slot + PM_TT - 1) / PM_TT);
@@ -84,8 +103,20 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.work_t0 = o, o = pm_al(o + (size_t)L.max_work * 4);
     L.wd = o, o = pm_al(o + (size_t)L.max_work * 16);
     L.sk_c = o, o = pm_al(o + (size_t)(L.max_work + 1) * 4);
+    /* tensor-core tiles: experts with >= PM_TC_MIN tokens, in tiles of PM_TC_N */
+    L.max_tc = (uint32_t)(routed / PM_TC_MIN + (routed + PM_TC_N - 1) / PM_TC_N + 1 +
+                          (uint64_t)L.S * ((T + PM_TC_N - 1) / PM_TC_N));
+    L.tc_tile = o, o = pm_al(o + (size_t)L.max_tc * 8);
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
+    L.midq = o, o = pm_al(o + (size_t)T * L.n_slot * L.fb * PM_Q8_K_BYTES);
+    /* split-K partial sums of the tensor-core gate/up tiles: [ks][pair][gate|up][Fmax] */
+    {
+        const uint64_t per = (uint64_t)T * L.n_slot * 2 * L.Fmax * 4;
+        uint64_t ks = per ? (64ull << 20) / per : 1;
+        L.ks_max = (uint32_t)(ks < 1 ? 1 : (ks > 8 ? 8 : ks));
+        L.tcp = o, o = pm_al(o + (size_t)L.ks_max * per);
+    }
     L.partial = o, o = pm_al(o + (size_t)T * L.n_slot * L.H * 4);
     L.sel_done = o, o = pm_al(o + 4);
     L.err = o, o = pm_al(o + 4);
@@ -107,10 +138,15 @@ struct pm_layer_args {
     int32_t *sel;
     float *w;
     pm_block_q8K *xq;
-    uint32_t *n_items; /* [0] all items, [1] routed items, [2] work units, [3] routed work units */
+    uint32_t *n_items; /* [0] all items, [1] routed items, [2] work units, [3] routed work units,
+                        * [4] tensor-core tiles, [5] their gate/up K splits */
     uint32_t *item_expert, *item_start, *pairs;
     uint32_t *work_item, *work_t0; /* work unit = (item, first token of its chunk of <= PM_TT) */
     uint4 *wd;      /* per work unit: expert id (E + s for shared s), first pair, token count */
+    uint2 *tc_tile; /* tensor-core tiles: (item, first token) */
+    pm_block_q8K *midq; /* q8_K of the mid rows of tensor-core pairs */
+    float *tcp;     /* [ks][pair][2][Fmax] split-K gate/up sums of tensor-core tiles */
+    uint32_t ks_max, tc_r, tc_s, n_sm; /* split bound; tensor-core path on for routed / shared */
     uint32_t *sk_c; /* [n_work + 1] prefix of per-row costs (PM_SK_CR + nt) over work units */
     float *mid;
     float *partial; /* [T * n_slot][H] down outputs before the combine */
@@ -206,8 +242,11 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
     for (uint32_t c0 = 0; c0 < a.E; c0 += blockDim.x) {
         const uint32_t e = c0 + threadIdx.x;
         const uint32_t v = e < a.E ? cnt[e] : 0u;
-        const uint32_t nw = (v + PM_TT - 1) / PM_TT;
-        const uint4 own = make_uint4(v, v ? 1u : 0u, nw, PM_SK_CR * nw + v);
+        const bool tcq = a.tc_r && v >= PM_TC_MIN; /* this expert's tokens go to tensor-core tiles */
+        const uint32_t nw = tcq ? 0u : (v + PM_TT - 1) / PM_TT;
+        const uint32_t nti = tcq ? (v + PM_TC_N - 1) / PM_TC_N : 0u;
+        /* .y packs items (high 16 bits) and tensor-core tiles (low 16 bits) */
+        const uint4 own = make_uint4(v, ((v ? 1u : 0u) << 16) | nti, nw, PM_SK_CR * nw + (tcq ? 0u : v));
         uint4 x = own;
 #pragma unroll 1
         for (uint32_t o = 1; o < 32u; o <<= 1) {
@@ -221,7 +260,8 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
 #pragma unroll 1
         for (uint32_t w2 = 0; w2 < wid; w2++) pre = pm_add4(pre, wsum[w2]);
         const uint4 incl = pm_add4(pre, x);
-        const uint32_t start = incl.x - own.x, item = incl.y - own.y, w0 = incl.z - own.z, cst = incl.w - own.w;
+        const uint32_t start = incl.x - own.x, item = (incl.y >> 16) - (own.y >> 16);
+        const uint32_t tt0 = (incl.y & 0xffffu) - nti, w0 = incl.z - own.z, cst = incl.w - own.w;
         if (e < a.E) {
             cnt[e] = start;
             if (v) {
@@ -235,13 +275,16 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
                     a.wd[w0 + j] = make_uint4(e, start + j * PM_TT, nt, 0u);
                     a.sk_c[w0 + j] = cst + j * (PM_SK_CR + PM_TT);
                 }
+#pragma unroll 1
+                for (uint32_t j = 0; j < nti; j++) a.tc_tile[tt0 + j] = make_uint2(item, j * PM_TC_N);
             }
         }
         __syncthreads();
         if (threadIdx.x == blockDim.x - 1u) carry = incl;
         __syncthreads();
     }
-    const uint32_t tot_pairs = carry.x, tot_items = carry.y, tot_work = carry.z, tot_cost = carry.w;
+    const uint32_t tot_pairs = carry.x, tot_items = carry.y >> 16, tot_tc = carry.y & 0xffffu;
+    const uint32_t tot_work = carry.z, tot_cost = carry.w;
     /* fill the pair lists in (token, slot) order */
     if (masks) {
         for (uint32_t q = threadIdx.x; q < n_routed; q += blockDim.x) {
@@ -273,7 +316,9 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
     /* shared experts (computed on the shard that owns expert 0): one item
      * each over all tokens, appended after the routed items */
     const uint32_t n_sh = a.lo == 0 ? a.S : 0u;
-    const uint32_t sh_chunks = (a.T + PM_TT - 1) / PM_TT, sh_cost = PM_SK_CR * sh_chunks + a.T;
+    const bool sh_tc = a.tc_s && a.T >= PM_TC_MIN; /* shared experts on the tensor-core path */
+    const uint32_t sh_chunks = sh_tc ? 0u : (a.T + PM_TT - 1) / PM_TT, sh_cost = PM_SK_CR * sh_chunks + a.T;
+    const uint32_t sh_tiles = sh_tc ? (a.T + PM_TC_N - 1) / PM_TC_N : 0u;
     for (uint32_t s = 0; s < n_sh; s++) {
         const uint32_t item = tot_items + s, base = tot_pairs + s * a.T, w0 = tot_work + s * sh_chunks;
         const uint32_t c0 = tot_cost + s * sh_cost;
@@ -289,13 +334,23 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
             a.wd[w0 + j] = make_uint4(a.E + s, base + j * PM_TT, nt, 0u);
             a.sk_c[w0 + j] = c0 + j * (PM_SK_CR + PM_TT);
         }
+        for (uint32_t j = threadIdx.x; j < sh_tiles; j += blockDim.x)
+            a.tc_tile[tot_tc + s * sh_tiles + j] = make_uint2(item, j * PM_TC_N);
     }
     if (threadIdx.x == 0) {
+        const uint32_t n_tc = tot_tc + n_sh * sh_tiles;
+        /* K splits of the tensor-core gate/up pass: about one unit per SM */
+        const uint32_t units = n_tc * ((a.Fmax + 127u) / 128u);
+        uint32_t ks = units ? (a.n_sm + units - 1) / units : 1u;
+        const uint32_t ks_cap = a.ks_max < a.H / 64u ? a.ks_max : a.H / 64u;
+        ks = ks < 1u ? 1u : (ks > ks_cap ? ks_cap : ks);
         a.item_start[tot_items + n_sh] = tot_pairs + n_sh * a.T;
         a.n_items[0] = tot_items + n_sh;
         a.n_items[1] = tot_items;
         a.n_items[2] = tot_work + n_sh * sh_chunks;
         a.n_items[3] = tot_work;
+        a.n_items[4] = n_tc;
+        a.n_items[5] = ks;
         a.sk_c[tot_work + n_sh * sh_chunks] = tot_cost + n_sh * sh_cost;
         *a.sel_done = 0;
     }
@@ -571,6 +626,277 @@ __global__ void __launch_bounds__(PM_THREADS, 2)
         for (uint32_t d = ci; d < ni; d++) pm_mbar_wait(bars + (d % P.S), (d / P.S) & 1u, nullptr);
 }
 
+/* ============================== 4b, 5b: tensor-core expert tiles */
+
+/* A tensor-core UNIT is (tile of <= PM_TC_N tokens of one expert, block of
+ * 128 matrix rows, K split).  NMAT 2: gate and up rows (K = H) into two
+ * accumulators, split-K sums to tcp.  NMAT 1: down rows (K = F) against the
+ * q8_K mid rows, one partial row per pair.  Per 64-wide K chunk every
+ * thread dequantizes operand rows to fp16 straight into a 128-byte-swizzled
+ * stage (Q4_K weights: one (matrix, row) or one half row per thread; q8_K
+ * tokens: 16 values per thread), then one thread issues the tcgen05 MMAs
+ * (M 128, N PM_TC_N, K 16) and commits them to the stage's mbarrier, which
+ * frees the stage pm_tcg::S chunks later.  Tensor memory holds NMAT x N fp32
+ * columns for the CTA's lifetime. */
+template <int Q, int HALF>
+__device__ __forceinline__ void pm_tc_weights(const uint8_t *row, uint32_t c, uint4 *oh, uint4 *ol) {
+    if constexpr (Q == PM_QUANT_Q4_K) {
+        pm_tc_q4k_row<HALF>(row, c, oh, ol);
+    } else { /* no tensor-core tiles are listed for other formats */
+#pragma unroll
+        for (int j = 0; j < 8; j++) oh[j] = ol[j] = make_uint4(0, 0, 0, 0);
+    }
+}
+
+/* operand stages of the tensor-core kernels (fp16 hi + lo tiles) */
+template <int NMAT>
+struct pm_tcg {
+    static constexpr uint32_t N = PM_TC_N;
+    static constexpr uint32_t A = 128u * 128u;  /* one 128 x 64 fp16 tile */
+    static constexpr uint32_t B = N * 128u;     /* one N x 64 fp16 tile */
+    static constexpr uint32_t STAGE = NMAT * 2u * A + 2u * B;
+    static constexpr uint32_t S = NMAT == 2 ? 2u : 3u;
+    static constexpr uint32_t SMEM = 1024u + S * STAGE;
+};
+
+template <int QR, int QS, int NMAT>
+__global__ void __launch_bounds__(PM_THREADS, 1) pm_tc_kernel(const __grid_constant__ pm_layer_args a) {
+    extern __shared__ uint8_t smem_raw[];
+    using G = pm_tcg<NMAT>;
+    constexpr uint32_t N = G::N, S = G::S, A_BYTES = G::A, B_BYTES = G::B, STAGE = G::STAGE;
+    __shared__ uint64_t empty[S], done;
+    __shared__ uint32_t tslot;
+    __shared__ uint32_t s_pair[N];
+    __shared__ const pm_block_q8K *s_src[N];
+    uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023u) & ~(uintptr_t)1023u);
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint32_t n_tiles = __ldcg(a.n_items + 4);
+    const uint32_t KS = NMAT == 2 ? __ldcg(a.n_items + 5) : 1u;
+    const uint32_t rt_n = ((NMAT == 2 ? a.Fmax : a.H) + 127u) / 128u;
+    const uint32_t units = n_tiles * rt_n * KS;
+    if (blockIdx.x >= units) return;
+    if (warp == 0) pm_tmem_alloc(&tslot, NMAT * N);
+    if (tid == 0) {
+        for (uint32_t i = 0; i < S; i++) pm_mbar_init(&empty[i], 1);
+        pm_mbar_init(&done, 1);
+        pm_fence_barrier_init();
+    }
+    pm_tc_fence_before();
+    __syncthreads();
+    pm_tc_fence_after();
+    const uint32_t tmem = tslot;
+    const uint32_t idesc = pm_idesc_f16(128, N);
+    uint32_t it = 0, nu = 0;
+    bool ok = true;
+    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const uint32_t tile = u / (rt_n * KS), rem = u % (rt_n * KS), rt = rem / KS, ks = rem % KS;
+        const uint2 tt = __ldcg(a.tc_tile + tile);
+        const uint32_t item = tt.x, t0 = tt.y, e = __ldcg(a.item_expert + item);
+        const uint32_t s0 = __ldcg(a.item_start + item), cnt = __ldcg(a.item_start + item + 1) - s0;
+        const uint32_t nt = cnt - t0 < N ? cnt - t0 : N;
+        const bool routed = e < a.E;
+        const uint32_t rows = NMAT == 2 ? (routed ? a.Fr : a.Fs) : a.H;
+        const uint32_t K = NMAT == 2 ? a.H : (routed ? a.Fr : a.Fs);
+        const uint32_t nch = K / 64u, cps = (nch + KS - 1) / KS;
+        const uint32_t c0 = ks * cps, c1 = c0 + cps < nch ? c0 + cps : nch;
+        if (rt * 128u >= rows || c0 >= c1) continue; /* uniform over the CTA */
+        const uint64_t rb = NMAT == 2 ? (routed ? a.rb_gu_r : a.rb_gu_s) : (routed ? a.rb_dn_r : a.rb_dn_s);
+        const uint8_t *mat[2];
+        if (NMAT == 2) {
+            mat[0] = routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate;
+            mat[1] = routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup;
+        } else {
+            mat[0] = routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown;
+            mat[1] = nullptr;
+        }
+        if (tid < N) {
+            const uint32_t p = tid < nt ? __ldcg(a.pairs + s0 + t0 + tid) : 0u;
+            s_pair[tid] = p;
+            s_src[tid] = tid >= nt ? nullptr
+                         : NMAT == 2 ? a.xq + (uint64_t)(p / a.n_slot) * a.hb
+                                     : a.midq + (uint64_t)p * a.fb;
+        }
+        __syncthreads();
+        /* this thread's operand rows: (matrix, row) for gate/up, (row, half) for down */
+        const uint32_t r = tid & 127u, hsel = tid >> 7;
+        const uint32_t grow = rt * 128u + r;
+        const uint8_t *wrow = grow < rows ? mat[NMAT == 2 ? hsel : 0] + (uint64_t)grow * rb : nullptr;
+        const uint32_t btok = tid >> 2, bq = tid & 3u;
+        for (uint32_t c = c0; c < c1; c++, it++) {
+            const uint32_t st = it % S;
+            /* the stage's previous MMAs are done (bounded wait; its outcome is
+             * made uniform by the barrier below) */
+            const bool got = it < S || pm_mbar_wait(&empty[st], ((it / S) + 1u) & 1u, a.err);
+            uint8_t *stage = sm + st * STAGE;
+            /* A: weights, hi tiles then lo tiles */
+            {
+                uint4 vh[8], vl[8];
+                if (wrow) {
+                    if (NMAT == 2) {
+                        if (routed) pm_tc_weights<QR, 0>(wrow, c, vh, vl); else pm_tc_weights<QS, 0>(wrow, c, vh, vl);
+                    } else if (hsel == 0) {
+                        if (routed) pm_tc_weights<QR, 1>(wrow, c, vh, vl); else pm_tc_weights<QS, 1>(wrow, c, vh, vl);
+                    } else {
+                        if (routed) pm_tc_weights<QR, 2>(wrow, c, vh, vl); else pm_tc_weights<QS, 2>(wrow, c, vh, vl);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) vh[j] = vl[j] = make_uint4(0, 0, 0, 0);
+                }
+                const uint32_t m = NMAT == 2 ? hsel : 0u;
+                uint8_t *ah = stage + m * A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u;
+                uint8_t *al = ah + NMAT * A_BYTES;
+#pragma unroll
+                for (uint32_t j = 0; j < 8; j++) {
+                    if (NMAT == 1 && (j >> 2) != hsel) continue; /* down: this thread's half row */
+                    const uint32_t off = (j ^ (r & 7u)) << 4;
+                    *(uint4 *)(ah + off) = vh[j];
+                    *(uint4 *)(al + off) = vl[j];
+                }
+            }
+            /* B: token activations (q8_K -> f32 -> fp16 hi + lo), 16 values per thread */
+            {
+                uint4 vh[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, vl[2] = {vh[0], vh[1]};
+                const pm_block_q8K *src = s_src[btok];
+                if (src) pm_tc_q8_16(src, 64u * c + 16u * bq, vh, vl);
+                uint8_t *bh = stage + 2u * NMAT * A_BYTES + (btok >> 3) * 1024u + (btok & 7u) * 128u;
+#pragma unroll
+                for (uint32_t j = 0; j < 2; j++) {
+                    const uint32_t off = ((2u * bq + j) ^ (btok & 7u)) << 4;
+                    *(uint4 *)(bh + off) = vh[j];
+                    *(uint4 *)(bh + B_BYTES + off) = vl[j];
+                }
+            }
+            pm_fence_proxy_async();
+            if (!__syncthreads_and(got)) {
+                ok = false;
+                break;
+            }
+            if (tid == 0) {
+                pm_tc_fence_after();
+                const uint64_t bh = pm_desc_sw128(stage + 2u * NMAT * A_BYTES);
+                const uint64_t bl = pm_desc_sw128(stage + 2u * NMAT * A_BYTES + B_BYTES);
+#pragma unroll
+                for (uint32_t m = 0; m < NMAT; m++) {
+                    const uint64_t ah = pm_desc_sw128(stage + m * A_BYTES);
+                    const uint64_t al = pm_desc_sw128(stage + (NMAT + m) * A_BYTES);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < 4; kk++) {
+                        /* w x = wh xh + wh xl + wl xh (+ wl xl, below fp32 rounding) */
+                        pm_mma_f16(tmem + m * N, ah + 2 * kk, bh + 2 * kk, idesc, (c > c0 || kk > 0) ? 1u : 0u);
+                        pm_mma_f16(tmem + m * N, ah + 2 * kk, bl + 2 * kk, idesc, 1u);
+                        pm_mma_f16(tmem + m * N, al + 2 * kk, bh + 2 * kk, idesc, 1u);
+                    }
+                }
+                pm_mma_commit(&empty[st]);
+            }
+        }
+        if (!ok) break;
+        /* ---- epilogue: accumulators -> global ---- */
+        if (tid == 0) pm_mma_commit(&done);
+        if (!__syncthreads_and(pm_mbar_wait(&done, nu & 1u, a.err))) {
+            ok = false;
+            break;
+        }
+        nu++;
+        pm_tc_fence_after();
+        {
+            const uint32_t lq = warp & 3u, ch = warp >> 2; /* lanes 32 lq.., tokens 32 ch.. */
+            const uint32_t row = rt * 128u + lq * 32u + lane;
+#pragma unroll
+            for (uint32_t m = 0; m < NMAT; m++) {
+#pragma unroll
+                for (uint32_t h = 0; h < 2; h++) {
+                    float v[16];
+                    const uint32_t col = m * N + ch * 32u + h * 16u;
+                    pm_tmem_ld16(tmem + ((lq * 32u) << 16) + col, v);
+                    if (row < rows) {
+#pragma unroll
+                        for (uint32_t i = 0; i < 16; i++) {
+                            const uint32_t t = ch * 32u + h * 16u + i;
+                            if (t < nt) {
+                                const uint32_t p = s_pair[t];
+                                if (NMAT == 2)
+                                    a.tcp[(((uint64_t)ks * a.T * a.n_slot + p) * 2u + m) * a.Fmax + row] = v[i];
+                                else
+                                    a.partial[(uint64_t)p * a.H + row] = v[i];
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        pm_tc_fence_before();
+        __syncthreads();
+    }
+    /* every issued MMA completed (each unit waits for `done`), except after a
+     * wait that timed out; release tensor memory in all cases */
+    pm_tc_fence_before();
+    __syncthreads();
+    pm_tc_fence_after();
+    if (warp == 0) pm_tmem_free(tmem, NMAT * N);
+}
+
+/* mid rows of tensor-core pairs: the K-split gate/up sums (fixed order),
+ * biases, glu, route weight -> mid (f32), then q8_K of each 256-block with
+ * the CPU-lane quantizer -> midq (the tensor-core down pass's input).
+ * Block (tile, 256-row block, group of 8 tokens), a thread per row: the
+ * split sums of all 8 tokens are loaded together. */
+#define PM_TC_MID_TG 8u
+__global__ void __launch_bounds__(256) pm_tc_mid_kernel(const __grid_constant__ pm_layer_args a) {
+    __shared__ float s_v[PM_TC_MID_TG][256];
+    const uint32_t n_tiles = __ldcg(a.n_items + 4);
+    const uint32_t ngrp = PM_TC_N / PM_TC_MID_TG;
+    const uint32_t tile = blockIdx.x / ngrp, grp = blockIdx.x % ngrp;
+    if (tile >= n_tiles) return;
+    const uint32_t KS = __ldcg(a.n_items + 5);
+    const uint2 tt = __ldcg(a.tc_tile + tile);
+    const uint32_t item = tt.x, e = __ldcg(a.item_expert + item);
+    const uint32_t s0 = __ldcg(a.item_start + item), cnt = __ldcg(a.item_start + item + 1) - s0;
+    const uint32_t t0 = tt.y + grp * PM_TC_MID_TG;
+    if (t0 >= cnt) return;
+    const uint32_t nt = cnt - t0 < PM_TC_MID_TG ? cnt - t0 : PM_TC_MID_TG;
+    const bool routed = e < a.E;
+    const uint32_t F = routed ? a.Fr : a.Fs;
+    const uint32_t b = blockIdx.y, row = b * 256u + threadIdx.x;
+    if (b * 256u >= F) return;
+    const float gb = routed && a.gate_b && row < F ? a.gate_b[(uint64_t)e * a.Fr + row] : 0.0f;
+    const float ub = routed && a.up_b && row < F ? a.up_b[(uint64_t)e * a.Fr + row] : 0.0f;
+    const uint64_t NP = (uint64_t)a.T * a.n_slot;
+    uint32_t p[PM_TC_MID_TG];
+    float g[PM_TC_MID_TG], u[PM_TC_MID_TG];
+#pragma unroll
+    for (uint32_t t = 0; t < PM_TC_MID_TG; t++) {
+        p[t] = t < nt ? __ldcg(a.pairs + s0 + t0 + t) : 0u;
+        g[t] = u[t] = 0.0f;
+    }
+    for (uint32_t ks = 0; ks < KS; ks++) {
+#pragma unroll
+        for (uint32_t t = 0; t < PM_TC_MID_TG; t++) {
+            if (t < nt && row < F) {
+                const float *src = a.tcp + ((ks * NP + p[t]) * 2u) * a.Fmax + row;
+                g[t] += __ldcg(src);
+                u[t] += __ldcg(src + a.Fmax);
+            }
+        }
+    }
+#pragma unroll
+    for (uint32_t t = 0; t < PM_TC_MID_TG; t++) {
+        if (t < nt) {
+            const float v = row < F ? pm_glu(g[t] + gb, u[t] + ub, a.act) * __ldcg(a.w + p[t]) : 0.0f;
+            if (row < F) a.mid[(uint64_t)p[t] * a.Fmax + row] = v;
+            s_v[t][threadIdx.x] = v;
+        }
+    }
+    __syncthreads();
+    /* q8_K of each token's 256-block: warp t */
+    const uint32_t warp = threadIdx.x >> 5;
+    if (warp < nt) {
+        const uint32_t bn = F - b * 256u < 256u ? F - b * 256u : 256u;
+        pm_q8k_warp(s_v[warp], bn, a.midq + (uint64_t)p[warp] * a.fb + b);
+    }
+}
+
 /* ================================================= 6: combine */
 
 /* out[t][r] = sum over the token's local slots (slot order) of the down
@@ -640,6 +966,7 @@ extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t
     v->work_item = (uint32_t *)(b + L.work_item);
     v->work_t0 = (uint32_t *)(b + L.work_t0);
     v->partial = (float *)(b + L.partial);
+    v->tc_tile = (uint32_t *)(b + L.tc_tile);
     v->n_slot = L.n_slot;
     v->f_max = L.Fmax;
     return 1;
@@ -708,13 +1035,31 @@ static inline void pm_ev(void *const *ev, int i, cudaStream_t st) {
     if (ev && ev[i]) cudaEventRecord((cudaEvent_t)ev[i], st);
 }
 
+template <int QR, int QS, int NMAT>
+static int pm_tc_launch(const pm_layer_args &a, cudaStream_t st) {
+    static uint64_t done = 0;
+    static int occ[64];
+    static uint32_t occ_smem[64];
+    const uint32_t smem = pm_tcg<NMAT>::SMEM;
+    auto k = pm_tc_kernel<QR, QS, NMAT>;
+    if (!pm_smem_attr(k, smem, &done)) return 0;
+    const uint32_t g = pm_sk_grid(k, smem, occ, occ_smem);
+    if (!g) return 0;
+    k<<<g, PM_THREADS, smem, st>>>(a);
+    return pm_ok(cudaGetLastError(), "moe layer tensor-core launch");
+}
+
 template <int QR, int QS>
 static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st, void *const *ev) {
     static uint64_t done_gu = 0, done_dn = 0;
     static int occ_gu[64], occ_dn[64];
     static uint32_t sm_gu[64], sm_dn[64];
     const bool grid = QR == PM_QUANT_IQ2_XXS || QS == PM_QUANT_IQ2_XXS;
-    /* 4: gate/up -> mid */
+    constexpr bool TC = QR == PM_QUANT_Q4_K || QS == PM_QUANT_Q4_K;
+    const bool tc = TC && (a.tc_r || a.tc_s) && L.T >= PM_TC_MIN; /* an expert can reach the threshold */
+    /* 4: gate/up -> tensor-core split-K sums, dp4a work units -> mid */
+    if constexpr (TC)
+        if (tc && !pm_tc_launch<QR, QS, 2>(a, st)) return 0;
     const pm_skind gr = pm_kind_for(2, a.rb_gu_r, a.H);
     const pm_skp pg = pm_skp_for(2, gr, a.S ? pm_kind_for(2, a.rb_gu_s, a.H) : gr, grid);
     auto kgu = pm_layer_sk_kernel<QR, QS, 2, 0>;
@@ -723,8 +1068,15 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     if (!g_gu) return 0;
     kgu<<<g_gu, PM_THREADS, pg.smem, st>>>(a, pg);
     if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
+    if (tc) { /* tensor-core pairs: mid and its q8_K */
+        dim3 gm(L.max_tc * (PM_TC_N / PM_TC_MID_TG), (L.Fmax + 255u) / 256u);
+        pm_tc_mid_kernel<<<gm, 256, 0, st>>>(a);
+        if (!pm_ok(cudaGetLastError(), "moe layer tensor-core mid launch")) return 0;
+    }
     pm_ev(ev, 4, st);
     /* 5: down -> partial rows */
+    if constexpr (TC)
+        if (tc && !pm_tc_launch<QR, QS, 1>(a, st)) return 0;
     const pm_skind dr = pm_kind_for(1, a.rb_dn_r, a.Fr);
     const pm_skp pd = pm_skp_for(1, dr, a.S ? pm_kind_for(1, a.rb_dn_s, a.Fs) : dr, grid);
     auto kdn = pm_layer_sk_kernel<QR, QS, 1, 1>;
@@ -799,6 +1151,13 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.work_t0 = (uint32_t *)(b + L.work_t0);
     a.wd = (uint4 *)(b + L.wd);
     a.sk_c = (uint32_t *)(b + L.sk_c);
+    a.tc_tile = (uint2 *)(b + L.tc_tile);
+    a.midq = (pm_block_q8K *)(b + L.midq);
+    a.tcp = (float *)(b + L.tcp);
+    a.ks_max = L.ks_max;
+    a.tc_r = pm_tc_fmt(d->quant) && L.H % 64 == 0 && L.Fr % 64 == 0;
+    a.tc_s = L.S && pm_tc_fmt(d->shared_quant) && L.H % 64 == 0 && L.Fs % 64 == 0;
+    a.n_sm = (uint32_t)pm_sm_count();
     a.mid = (float *)(b + L.mid);
     a.partial = (float *)(b + L.partial);
     a.sel_done = (uint32_t *)(b + L.sel_done);

@@ -8,6 +8,8 @@ from helpers import HostLayer, rel_l2
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
+TC_MIN = 128  # experts with at least this many tokens take the tensor-core path (moe_layer.cu PM_TC_MIN)
+
 
 @pytest.mark.parametrize("T", [8, 9, 16, 17])
 @pytest.mark.parametrize("shared", [None, (2, 512)])
@@ -46,7 +48,7 @@ def test_work_list_and_stages(oracle, rep):
     torch.cuda.synchronize()
     v = dl.ws_view(wst, T)
     ws, base = wst.cpu().numpy(), wst.data_ptr()
-    n = _ws(ws, base, v.n_items, 3, np.uint32)
+    n = _ws(ws, base, v.n_items, 6, np.uint32)
     ie = _ws(ws, base, v.item_expert, n[0], np.uint32)
     st = _ws(ws, base, v.item_start, n[0] + 1, np.uint32)
     pairs = _ws(ws, base, v.pairs, st[-1], np.uint32)
@@ -57,9 +59,15 @@ def test_work_list_and_stages(oracle, rep):
     want = sorted((int(sel[t, s]), t * ns + s) for t in range(T) for s in range(k))
     got = sorted((int(ie[i]), int(p)) for i in range(n[0]) for p in pairs[st[i]:st[i + 1]])
     assert got == want, "CSR mismatch"
-    # work units cover each item's tokens in chunks of 8
+    # items of >= TC_MIN tokens go to tensor-core tiles of 64 tokens (Q4_K),
+    # the rest to work units of 8; together they cover every item once
+    tc = _ws(ws, base, v.tc_tile, 2 * n[4], np.uint32).reshape(-1, 2)
+    size = {i: int(st[i + 1] - st[i]) for i in range(n[0])}
+    tc_items = {int(i) for i in tc[:, 0]}
+    assert tc_items == {i for i in range(n[0]) if size[i] >= TC_MIN}, "tensor-core item choice"
+    assert sorted(map(tuple, tc.tolist())) == sorted((i, c) for i in tc_items for c in range(0, size[i], 64))
     units = sorted(zip(wi.tolist(), w0.tolist()))
-    exp_units = sorted((i, c) for i in range(n[0]) for c in range(0, int(st[i + 1] - st[i]), 8))
+    exp_units = sorted((i, c) for i in range(n[0]) if i not in tc_items for c in range(0, size[i], 8))
     assert units == exp_units, "work list mismatch"
     mid = _ws(ws, base, v.mid, T * ns * v.f_max, np.float32).reshape(T * ns, v.f_max)
     ref, ref_mid = L.oracle_ffn(x, sel, w, return_mid=True)

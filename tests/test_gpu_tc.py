@@ -1,0 +1,44 @@
+"""Large batches: experts with >= 128 tokens (and the shared expert) run on
+the tcgen05 tensor-core tiles (fp16 hi + lo split operands, fp32
+accumulation); the rest on the dp4a engine.  Outputs and mid rows must
+match the CPU oracle within the expert-FFN tolerance."""
+import numpy as np
+import pytest
+
+from helpers import HostLayer, rel_l2
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def _ws(ws, base, ptr, n, dt):
+    off = ptr - base
+    return ws[off:off + n * np.dtype(dt).itemsize].view(dt)
+
+
+@pytest.mark.parametrize("shared", [None, (2, 512)])
+@pytest.mark.parametrize("T", [300, 512])
+def test_tensor_core_tiles(oracle, T, shared):
+    L = HostLayer(H=512, F=512, E=8, k=2, quant=2, seed=11, router_mode=0, zipf=(1.1, "select"), shared=shared)
+    x = np.random.default_rng(5).normal(0, 1, (T, L.H)).astype(np.float32)
+    _, sel, w = L.oracle_route(x)
+    ref, ref_mid = L.oracle_ffn(x, sel, w, return_mid=True)
+    dl = L.to_device()
+    wst = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
+    dl.forward(torch.from_numpy(x).cuda(), out, wst)
+    torch.cuda.synchronize()
+    v = dl.ws_view(wst, T)
+    ws, base = wst.cpu().numpy(), wst.data_ptr()
+    n = _ws(ws, base, v.n_items, 6, np.uint32)
+    assert n[4] > 0, "no tensor-core tiles at this batch"
+    ns = v.n_slot
+    mid = _ws(ws, base, v.mid, T * ns * v.f_max, np.float32).reshape(T * ns, v.f_max)[:, :ref_mid.shape[-1]]
+    rm = ref_mid.reshape(T * ns, -1)
+    got = out.cpu().numpy()
+    print(T, shared is not None, "tiles", int(n[4]), "splits", int(n[5]), "out", rel_l2(got, ref),
+          "mid", rel_l2(mid, rm))
+    assert rel_l2(mid, rm) < TOL
+    assert rel_l2(got, ref) < TOL
