@@ -46,6 +46,12 @@ import torch  # noqa: E402
 
 CFG = dict(name="C2", n_embd=2048, n_ff=512, n_expert=256, n_used=8, layers=40, zipf=1.1, batches=(1, 8, 64))
 METRIC = "MoE-layer tokens/s and % of HBM/tensor roofline at 1/2/4/8 B200"
+# DRAM bytes (read + write) per gate/up launch over the launch's algorithmic bytes, from one
+# ncu capture of this workload (profiles/pm_layer_sk_kernel_c2_b64.md: 228.3 + 18.3 MB
+# against 221.2 MB); the reported traffic scales it to this run's launch.
+TRAFFIC_RATIO = (228.26 + 18.35) / 221.2
+TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of pm_layer_sk_kernel gate/up (config 2, "
+                "batch 64) / algorithmic bytes, times this run's algorithmic bytes per launch")
 UNIT = "tokens/s"
 
 
@@ -429,7 +435,8 @@ def main():
             layer_ms = float(st_ms.sum())
             roof = {"bound": "hbm", "kernel": "pm_layer_gu_kernel (gate/up + glu + q8_K of mid)",
                     "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
-                    "traffic": None, "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms,
+                    "traffic": TRAFFIC_RATIO * gu_bytes, "traffic_note": TRAFFIC_NOTE,
+                    "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms,
                     "stage_ms": dict(zip(["router_logits+q8k_x", "(fused)", "select_csr", "gate_up", "down_combine"],
                                          map(float, st_ms))),
                     "layer": {"algorithmic_bytes": layer_bytes, "eager_ms": layer_ms,
