@@ -539,12 +539,23 @@ __global__ void __launch_bounds__(PM_THREADS, 2)
     };
     pm_it iti = it_init(), itc = iti;
     uint32_t ni = 0, ci = 0;
-    auto issue = [&](uint32_t slot) {
-        const pm_segi s = pm_seg_get<EPI>(a, tab, sl, iti.k);
+    auto issue = [&](uint32_t slot) { /* lane 0: the stage iti points at */
         const uint8_t *src[NMAT];
-        uint32_t r, rows;
-        pm_stage_src<NMAT>(s, P.k[s.kind], iti, src, r, rows);
-        pm_issue_stage<NMAT>(ring + (size_t)slot * P.stage, bars + slot, src, rows * (uint32_t)P.k[s.kind].rb);
+        uint32_t r, rows, kind;
+        if (iti.k < PM_SK_MAXSEG) { /* the fields it needs, straight from the table */
+            const pm_segi *t = tab + iti.k;
+            kind = t->kind;
+            const pm_skind &kd = P.k[kind];
+            r = t->r0 + (iti.g - iti.g0) * kd.rw;
+            rows = t->r1 - r < kd.rw ? t->r1 - r : kd.rw;
+#pragma unroll
+            for (int m = 0; m < NMAT; m++) src[m] = t->base[m] + (uint64_t)r * kd.rb;
+        } else {
+            const pm_segi sg = pm_seg_get<EPI>(a, tab, sl, iti.k);
+            kind = sg.kind;
+            pm_stage_src<NMAT>(sg, P.k[kind], iti, src, r, rows);
+        }
+        pm_issue_stage<NMAT>(ring + (size_t)slot * P.stage, bars + slot, src, rows * (uint32_t)P.k[kind].rb);
     };
     while (ni < P.S && iti.k < sl.n_seg) {
         if (lane == 0) issue(ni);
@@ -574,6 +585,22 @@ __global__ void __launch_bounds__(PM_THREADS, 2)
         }
         if (tid < s.nt) s_tok[tid] = __ldcg(s.pairs + tid);
         __syncthreads();
+        /* the segment's fixed job fields */
+        pm_rowjob jb;
+        jb.rb = kd.rb;
+        jb.npair = kd.npair;
+        jb.n_units = kd.n_units;
+        jb.nt = s.nt;
+        jb.act = a.act;
+        jb.ostride = EPI == 0 ? a.Fmax : a.H;
+        jb.acts = acts;
+        jb.grid = grid;
+        jb.tokpair = s_tok;
+        jb.out = EPI == 0 ? a.mid : a.partial;
+        jb.b0 = s.b0;
+        jb.b1 = s.b1;
+        jb.wts = a.w;
+        const uint32_t bytes_row = (uint32_t)kd.rb;
         while (itc.k == k) {
             const uint32_t slot = ci % P.S;
             if (!pm_mbar_wait_sleep(bars + slot, (ci / P.S) & 1u, a.err)) {
@@ -584,29 +611,12 @@ __global__ void __launch_bounds__(PM_THREADS, 2)
             uint32_t r, rows;
             pm_stage_src<NMAT>(s, kd, itc, src, r, rows);
             const uint8_t *stg = ring + (size_t)slot * P.stage;
-            pm_rowjob jb;
-#pragma unroll
-            for (int m = 0; m < NMAT; m++) jb.w[m] = pm_stage_ptr<NMAT>(stg, src, rows * (uint32_t)kd.rb, m);
-            if (NMAT == 1) jb.w[1] = nullptr;
-            jb.rb = kd.rb;
-            jb.rows = rows;
-            jb.npair = kd.npair;
-            jb.n_units = kd.n_units;
-            jb.row_g = r;
-            jb.nt = s.nt;
-            jb.act = a.act;
-            jb.ostride = EPI == 0 ? a.Fmax : a.H;
-            jb.acts = acts;
-            jb.grid = grid;
-            jb.tokpair = s_tok;
-            jb.out = EPI == 0 ? a.mid : a.partial;
-            jb.b0 = s.b0;
-            jb.b1 = s.b1;
-            jb.wts = a.w;
+            const uint8_t *w0 = pm_stage_ptr<NMAT>(stg, src, rows * bytes_row, 0);
+            const uint8_t *w1 = NMAT == 2 ? pm_stage_ptr<NMAT>(stg, src, rows * bytes_row, 1) : nullptr;
             if (s.kind == 0)
-                pm_rows_any<QR, NMAT, EPI>(jb, kd.lpr);
+                pm_rows_any<QR, NMAT, EPI>(jb, kd.lpr, w0, w1, rows, r);
             else
-                pm_rows_any<QS, NMAT, EPI>(jb, kd.lpr);
+                pm_rows_any<QS, NMAT, EPI>(jb, kd.lpr, w0, w1, rows, r);
             __syncwarp();
             if (iti.k < sl.n_seg) { /* refill the slot just consumed */
                 if (lane == 0) {

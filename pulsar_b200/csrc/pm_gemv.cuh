@@ -355,10 +355,11 @@ struct pm_rs {
 
 /* ------------------------------------------------------ one stage */
 
+/* what stays fixed over a segment (one work unit's rows); the stage's row
+ * pointers, row count and first row are passed per call */
 struct pm_rowjob {
-    const uint8_t *w[2]; /* the stage's row 0 of each matrix (shared memory) */
     uint64_t rb;
-    uint32_t rows, npair, n_units, row_g, nt, act, ostride;
+    uint32_t npair, n_units, nt, act, ostride;
     pm_acts acts;
     const uint64_t *grid;
     const uint32_t *tokpair; /* (token, slot) pair id of each token of the unit */
@@ -369,7 +370,8 @@ struct pm_rowjob {
 
 /* EPI 0: gate/up -> mid = glu(g + bg, u + bu) * w;  EPI 1: down -> partial */
 template <int Q, int NMAT, int NT, int LPR, int EPI>
-__device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
+__device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, const uint8_t *w1, uint32_t rows,
+                                     uint32_t row_g) {
     constexpr int RPP = 32 / LPR;
     constexpr int NTP = NT <= 1 ? 1 : (NT <= 2 ? 2 : (NT <= 4 ? 4 : 8));
     constexpr int V = NMAT * NTP;
@@ -377,9 +379,9 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
     const uint32_t lane = threadIdx.x & 31u, sub = lane / LPR, sl = lane % LPR;
     const pm_acts &ac = jb.acts;
     const uint32_t P = ac.P;
-    for (uint32_t j0 = 0; j0 < jb.rows; j0 += RPP) {
+    for (uint32_t j0 = 0; j0 < rows; j0 += RPP) {
         const uint32_t j = j0 + sub;
-        const bool rv = j < jb.rows;
+        const bool rv = j < rows;
         float v[V];
 #pragma unroll
         for (int i = 0; i < V; i++) v[i] = 0.0f;
@@ -388,7 +390,7 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
                 const bool two = 2u * p + 1u < jb.n_units;
                 pm_wp W[NMAT];
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) pm_decode_pair<Q>(jb.w[m] + (size_t)j * jb.rb, p, two, jb.grid, W[m]);
+                for (int m = 0; m < NMAT; m++) pm_decode_pair<Q>((m == 0 ? w0 : w1) + (size_t)j * jb.rb, p, two, jb.grid, W[m]);
                 const uint32_t blk = p >> 2;
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
@@ -421,7 +423,7 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
                 for (int i = 0; i < K; i++) {
                     const uint32_t t = (uint32_t)(idx + i);
                     if (t < jb.nt) {
-                        const uint32_t row = jb.row_g + j, pr = jb.tokpair[t];
+                        const uint32_t row = row_g + j, pr = jb.tokpair[t];
                         float g = v[i], up = u[i];
                         if (jb.b0) g += jb.b0[row];
                         if (jb.b1) up += jb.b1[row];
@@ -434,7 +436,7 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
 #pragma unroll
                 for (int i = 0; i < K; i++) {
                     const uint32_t t = (uint32_t)(idx + i);
-                    if (t < jb.nt) jb.out[(size_t)jb.tokpair[t] * jb.ostride + jb.row_g + j] = v[i];
+                    if (t < jb.nt) jb.out[(size_t)jb.tokpair[t] * jb.ostride + row_g + j] = v[i];
                 }
             }
         }
@@ -442,24 +444,26 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb) {
 }
 
 template <int Q, int NMAT, int LPR, int EPI>
-__device__ __forceinline__ void pm_rows_nt(const pm_rowjob &jb) {
+__device__ __forceinline__ void pm_rows_nt(const pm_rowjob &jb, const uint8_t *w0, const uint8_t *w1, uint32_t rows,
+                                           uint32_t row_g) {
     switch (jb.nt) {
-    case 1: pm_rows<Q, NMAT, 1, LPR, EPI>(jb); break;
-    case 2: pm_rows<Q, NMAT, 2, LPR, EPI>(jb); break;
-    case 3: pm_rows<Q, NMAT, 3, LPR, EPI>(jb); break;
-    case 4: pm_rows<Q, NMAT, 4, LPR, EPI>(jb); break;
+    case 1: pm_rows<Q, NMAT, 1, LPR, EPI>(jb, w0, w1, rows, row_g); break;
+    case 2: pm_rows<Q, NMAT, 2, LPR, EPI>(jb, w0, w1, rows, row_g); break;
+    case 3: pm_rows<Q, NMAT, 3, LPR, EPI>(jb, w0, w1, rows, row_g); break;
+    case 4: pm_rows<Q, NMAT, 4, LPR, EPI>(jb, w0, w1, rows, row_g); break;
     case 5:
-    case 6: pm_rows<Q, NMAT, 6, LPR, EPI>(jb); break;
-    default: pm_rows<Q, NMAT, 8, LPR, EPI>(jb); break;
+    case 6: pm_rows<Q, NMAT, 6, LPR, EPI>(jb, w0, w1, rows, row_g); break;
+    default: pm_rows<Q, NMAT, 8, LPR, EPI>(jb, w0, w1, rows, row_g); break;
     }
 }
 
 template <int Q, int NMAT, int EPI>
-__device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, uint32_t lpr) {
+__device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, uint32_t lpr, const uint8_t *w0, const uint8_t *w1,
+                                            uint32_t rows, uint32_t row_g) {
     if (lpr == 16u)
-        pm_rows_nt<Q, NMAT, 16, EPI>(jb);
+        pm_rows_nt<Q, NMAT, 16, EPI>(jb, w0, w1, rows, row_g);
     else
-        pm_rows_nt<Q, NMAT, 4, EPI>(jb);
+        pm_rows_nt<Q, NMAT, 4, EPI>(jb, w0, w1, rows, row_g);
 }
 
 /* ------------------------------------------------------ stage copies */
