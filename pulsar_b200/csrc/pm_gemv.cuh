@@ -177,16 +177,11 @@ __device__ __forceinline__ void pm_decode_pair(const uint8_t *row, uint32_t p, b
         /* 6-bit scale/min of sub-blocks 2sp and 2sp+1 (k4 packing, cu:1699) */
         const uint32_t sh = 16u * (sp & 1u);
         const uint32_t ea = (sa >> sh) & 0xffffu, eb = (sb >> sh) & 0xffffu, ec = (sc >> sh) & 0xffffu;
-        int32_t s0, s1, n0, n1;
-        if (sp < 2) {
-            s0 = (int32_t)(ea & 63u), s1 = (int32_t)((ea >> 8) & 63u);
-            n0 = (int32_t)(eb & 63u), n1 = (int32_t)((eb >> 8) & 63u);
-        } else {
-            s0 = (int32_t)((ec & 15u) | ((ea >> 6) & 3u) << 4);
-            s1 = (int32_t)(((ec >> 8) & 15u) | ((ea >> 14) & 3u) << 4);
-            n0 = (int32_t)(((ec >> 4) & 15u) | ((eb >> 6) & 3u) << 4);
-            n1 = (int32_t)(((ec >> 12) & 15u) | ((eb >> 14) & 3u) << 4);
-        }
+        /* both sub-blocks at once, branch-free (lanes of a warp hold all four sp) */
+        const uint32_t sv = sp < 2 ? (ea & 0x3f3fu) : ((ec & 0x0f0fu) | ((ea >> 2) & 0x3030u));
+        const uint32_t mv = sp < 2 ? (eb & 0x3f3fu) : (((ec >> 4) & 0x0f0fu) | ((eb >> 2) & 0x3030u));
+        const int32_t s0 = (int32_t)(sv & 0xffu), s1 = (int32_t)(sv >> 8);
+        const int32_t n0 = (int32_t)(mv & 0xffu), n1 = (int32_t)(mv >> 8);
         const uint4 *qp = (const uint4 *)(b + 16 + 32 * sp);
         const uint4 q0 = qp[0], q1 = qp[1];
         const uint32_t raw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};

@@ -139,16 +139,9 @@ __device__ __forceinline__ void pm_tc_q4k_row(const uint8_t *row, uint32_t c, ui
     const uint4 h = __ldg((const uint4 *)b);
     const uint32_t sh = 16u * (sp & 1u);
     const uint32_t ea = (h.y >> sh) & 0xffffu, eb = (h.z >> sh) & 0xffffu, ec = (h.w >> sh) & 0xffffu;
-    uint32_t s0, s1, n0, n1;
-    if (sp < 2) {
-        s0 = ea & 63u, s1 = (ea >> 8) & 63u;
-        n0 = eb & 63u, n1 = (eb >> 8) & 63u;
-    } else {
-        s0 = (ec & 15u) | ((ea >> 6) & 3u) << 4;
-        s1 = ((ec >> 8) & 15u) | ((ea >> 14) & 3u) << 4;
-        n0 = ((ec >> 4) & 15u) | ((eb >> 6) & 3u) << 4;
-        n1 = ((ec >> 12) & 15u) | ((eb >> 14) & 3u) << 4;
-    }
+    const uint32_t sv = sp < 2 ? (ea & 0x3f3fu) : ((ec & 0x0f0fu) | ((ea >> 2) & 0x3030u));
+    const uint32_t mv = sp < 2 ? (eb & 0x3f3fu) : (((ec >> 4) & 0x0f0fu) | ((eb >> 2) & 0x3030u));
+    const uint32_t s0 = sv & 0xffu, s1 = sv >> 8, n0 = mv & 0xffu, n1 = mv >> 8;
     const float d = pm_h2f(h.x & 0xffffu), dm = pm_h2f(h.x >> 16);
     const float S0 = d * (float)s0, M0 = -dm * (float)n0;
     const float S1 = d * (float)s1 * 0.0625f, M1 = -dm * (float)n1; /* high nibbles come x16 */
