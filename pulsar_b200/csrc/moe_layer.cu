@@ -460,7 +460,7 @@ __device__ __forceinline__ void pm_stage_src(const pm_segi &s, const pm_skind &k
  * unit, glu * route weight -> mid.  EPI 1: down of every work unit (mid
  * rows quantized to q8_K while staging) -> one partial row per pair. */
 template <int QR, int QS, int NMAT, int EPI>
-__global__ void __launch_bounds__(PM_THREADS, 2)
+__global__ void __launch_bounds__(PM_THREADS, pm_sk_minb(NMAT))
     pm_layer_sk_kernel(const __grid_constant__ pm_layer_args a, const __grid_constant__ pm_skp P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t s_cnt[2], s_lim[4], s_tok[PM_TT];
@@ -1016,7 +1016,7 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
     off = P.off_acts + pm_acts_bytes(P.P, P.NB);
     P.off_bar = (off + 15u) & ~15u;
     P.off_ring = (P.off_bar + PM_WARPS * 8u * 8u + 127u) & ~127u;
-    const uint32_t budget = 110u * 1024u;
+    const uint32_t budget = pm_sk_minb(nmat) == 1 ? 200u * 1024u : 110u * 1024u;
     uint32_t S = budget > P.off_ring ? (budget - P.off_ring) / (PM_WARPS * P.stage) : 2u;
     P.S = S < 2 ? 2 : (S > 8 ? 8 : S);
     P.smem = P.off_ring + PM_WARPS * P.S * P.stage;

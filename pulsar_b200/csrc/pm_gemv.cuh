@@ -45,6 +45,10 @@
 #define PM_SK_CR 2u   /* per-row decode cost, in token-dot units */
 #define PM_SK_RQ 8u   /* slice boundaries fall on multiples of this many rows */
 #define PM_SK_MAXSEG 64u
+/* resident CTAs per SM the stream-K kernels are compiled for: gate/up (two
+ * matrices, the larger register tile) runs one CTA per SM with the whole
+ * register file and a deep ring; down runs two */
+__host__ __device__ constexpr int pm_sk_minb(int nmat) { return nmat == 2 ? 1 : 2; }
 
 /* ------------------------------------------------------- activations */
 
