@@ -14,9 +14,10 @@ value     tokens/s with inputs resident in HBM: K replays of a captured CUDA
           graph of the step, CUDA events on the launching stream, max over ranks.
 e2e       the same through the public API each step: pinned host x -> device,
           the stack, device -> pinned host of the final hidden rows.
-roofline  the dominant kernel (gate/up, pm_layer_gu_kernel): algorithmic bytes
-          per launch (distinct routed experts x gate+up bytes + shared gate+up +
-          q8_K activations) / its CUDA-event duration, vs measured HBM.
+roofline  the dominant kernel (the stream-K gate/up pass, pm_layer_sk_kernel
+          <.., 2, 0>): algorithmic bytes per launch (distinct routed experts x
+          gate+up bytes + shared gate+up + q8_K activations) / its CUDA-event
+          duration, vs the measured HBM copy bandwidth; traffic from ncu.
 cpu_baseline  the C restatement of the reference CPU expert lane (oracle/,
           all host threads) on a bounded sample of the same stack.
 
@@ -433,7 +434,7 @@ def main():
             gu_ms = float(st_ms[3])
             ach = gu_bytes / (gu_ms / 1e3) / 1e9
             layer_ms = float(st_ms.sum())
-            roof = {"bound": "hbm", "kernel": "pm_layer_gu_kernel (gate/up + glu + q8_K of mid)",
+            roof = {"bound": "hbm", "kernel": "pm_layer_sk_kernel gate/up (dp4a stream-K: gate + up + glu -> mid)",
                     "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
                     "traffic": TRAFFIC_RATIO * gu_bytes, "traffic_note": TRAFFIC_NOTE,
                     "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms,
