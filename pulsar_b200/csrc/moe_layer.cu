@@ -182,9 +182,13 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
     const uint32_t token = blockIdx.x * PM_SEL_WARPS + wid;
     if (token < a.T) {
-        float *score = (float *)sm + (size_t)wid * 2 * a.E;
-        pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0, a.n_group,
-                        a.topk_group, score, score + a.E, a.n_slot);
+        float *score = (float *)sm + (size_t)wid * 2 * (a.E > 256u ? a.E : 256u);
+        if (a.E <= 256u && a.k <= 32u && a.mode <= 1u && (a.n_group <= 1u || a.topk_group >= a.n_group))
+            pm_select_fast(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, score,
+                           score + 256, a.n_slot);
+        else
+            pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0, a.n_group,
+                            a.topk_group, score, score + a.E, a.n_slot);
         if (lane < a.S) { /* shared experts: always-on slots k.., ids E + s, weight 1 */
             a.sel[token * a.n_slot + a.k + lane] = (int32_t)(a.E + lane);
             a.w[token * a.n_slot + a.k + lane] = 1.0f;
@@ -204,7 +208,7 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
     uint32_t *mask = cnt + a.E; /* [E][mw] token masks (small batches) */
     const bool masks = a.T <= PM_SEL_MASK_T;
     /* the selections, read once with independent loads (u16; 0xffff = not in this shard) */
-    uint16_t *ss = (uint16_t *)(sm + (size_t)PM_SEL_WARPS * 2 * a.E * 4);
+    uint16_t *ss = (uint16_t *)(sm + (size_t)PM_SEL_WARPS * 2 * (a.E > 256u ? a.E : 256u) * 4);
     const bool staged = n_routed <= PM_SEL_STAGE && a.E < 65535u;
     auto sel_at = [&](uint32_t q) -> uint32_t {
         uint32_t e;
@@ -1182,7 +1186,8 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     pm_ev(ev, 2, st); /* q8_K of x is written by the router kernel */
     /* 3: select + CSR */
     const uint32_t n_routed = L.T * L.k;
-    const uint32_t smem_sel = PM_SEL_WARPS * 2u * L.E * 4u + (n_routed <= PM_SEL_STAGE ? 2u * n_routed : 0u);
+    const uint32_t per_warp = 2u * (L.E > 256u ? L.E : 256u) * 4u; /* scores + probabilities */
+    const uint32_t smem_sel = PM_SEL_WARPS * per_warp + (n_routed <= PM_SEL_STAGE ? 2u * n_routed : 0u);
     static uint64_t done_sel = 0;
     if (!pm_smem_attr(pm_layer_select_kernel, smem_sel, &done_sel)) return 0;
     pm_layer_select_kernel<<<(L.T + PM_SEL_WARPS - 1) / PM_SEL_WARPS, PM_SEL_WARPS * 32u, smem_sel, st>>>(a);

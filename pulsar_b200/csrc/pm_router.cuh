@@ -138,3 +138,114 @@ __device__ __forceinline__ void pm_select_token(int32_t *selected, float *weight
     }
 }
 
+
+/* Fast path of pm_select_token for the fused layer: modes 0 and 1, no group
+ * limit, n_expert <= 256, k_used <= 32.  Same operations and tie rule as
+ * pm_select_token (and the CPU restatement), so the same bits:
+ *   - the lane's logits and biases are read with independent loads, the
+ *     sigmoid loop stages scores / probabilities in shared memory and each
+ *     lane then holds its 8 experts e = lane + 32 i in registers;
+ *   - each round is one warp argmax over the lanes' local bests (ties -> lower
+ *     index); only the winning lane marks its expert taken (-inf) and rescans
+ *     its 8 registers;
+ *   - the weight sums keep the sequential slot order; the divisions run on
+ *     lanes 0..k-1 in parallel, and lane s writes slot s. */
+__device__ __forceinline__ void pm_select_fast(int32_t *selected, float *weights, const float *logits,
+                                               const float *bias, uint32_t n_expert, uint32_t k_used,
+                                               float weight_scale, uint32_t token, uint32_t mode, float *score,
+                                               float *prob, uint32_t out_stride) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const float *lg = logits + (uint64_t)token * n_expert;
+    float raw[8], bv8[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t e = lane + 32u * (uint32_t)i;
+        raw[i] = e < n_expert ? __ldcg(lg + e) : 0.0f;
+        bv8[i] = bias && e < n_expert ? __ldg(bias + e) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        score[lane + 32 * i] = raw[i];
+        prob[lane + 32 * i] = bv8[i];
+    }
+    __syncwarp();
+    for (uint32_t e = lane; e < 32u * 8u; e += 32u) { /* compact loop: sigmoid, score */
+        const float r = score[e];
+        const float p = mode == 1u ? r : pm_sigmoid(r);
+        score[e] = __fadd_rn(p, prob[e]);
+        prob[e] = p;
+    }
+    __syncwarp();
+    float sc[8], pr[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t e = lane + 32u * (uint32_t)i;
+        sc[i] = score[e];
+        pr[i] = prob[e];
+    }
+    auto local_best = [&](float &bv, uint32_t &bi) {
+        bv = -INFINITY;
+        bi = UINT32_MAX;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t e = lane + 32u * (uint32_t)i;
+            if (e < n_expert && pm_better(sc[i], e, bv, bi)) {
+                bv = sc[i];
+                bi = e;
+            }
+        }
+    };
+    float lbv;
+    uint32_t lbi;
+    local_best(lbv, lbi);
+    float sum = 0.0f, myw = 0.0f;
+    int32_t mysel = -1;
+    for (uint32_t r = 0; r < k_used; r++) {
+        float bv = lbv;
+        uint32_t bi = lbi;
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, m);
+            if (pm_better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        const bool hit = bi < n_expert;
+        const bool owner = hit && (bi & 31u) == lane;
+        float mine = 0.0f;
+        if (owner) {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if ((uint32_t)i == (bi >> 5)) {
+                    mine = pr[i];
+                    sc[i] = -INFINITY;
+                }
+            local_best(lbv, lbi);
+        }
+        /* only NaN scores left: the slot stays unrouted (-1, weight 0) */
+        const float bp = hit ? __shfl_sync(0xffffffffu, mine, bi & 31u) : 0.0f;
+        if (lane == r) {
+            mysel = hit ? (int32_t)bi : -1;
+            myw = bp;
+        }
+        sum = __fadd_rn(sum, bp);
+    }
+    float w = myw;
+    if (mode == 1u) {
+        float m = lane < k_used ? myw : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float ex = lane < k_used ? pm_expf(__fsub_rn(myw, m)) : 0.0f;
+        float es = 0.0f;
+        for (uint32_t s = 0; s < k_used; s++) es = __fadd_rn(es, __shfl_sync(0xffffffffu, ex, s));
+        w = __fmul_rn(__fdiv_rn(ex, es), weight_scale);
+    } else {
+        w = __fmul_rn(__fdiv_rn(myw, fmaxf(sum, 6.103515625e-5f)), weight_scale);
+    }
+    if (lane < k_used) {
+        selected[(uint64_t)token * out_stride + lane] = mysel;
+        weights[(uint64_t)token * out_stride + lane] = w;
+    }
+}
