@@ -139,24 +139,32 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
  * j and c ascending, xor butterfly), so the bits equal the per-warp
  * kernel's.  With xq set, the CTAs of expert column 0 also write the
  * tile's q8_K rows (CPU-lane quantizer, pm_q8k_warp). */
-#define PM_RT_G 8 /* 128-wide chunks of a W row in flight per warp */
-template <int TPB>
+/* EPW experts per warp: 1 for small batches (more CTAs), 4 for larger ones
+ * (each x value read from shared memory serves 4 experts); G 128-wide W
+ * chunks per expert are in flight per warp */
+template <int TPB, int EPW>
 __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, const float *__restrict__ w,
                                                              const float *__restrict__ x,
                                                              const float *__restrict__ lbias, uint32_t n_expert,
                                                              uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq) {
+    constexpr int G = EPW == 1 ? 8 : 2;
     extern __shared__ double2 xs[]; /* [TPB][in_dim / 2] */
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t t0 = blockIdx.y * TPB;
     const uint32_t nt = n_tok - t0 < (uint32_t)TPB ? n_tok - t0 : (uint32_t)TPB;
-    const uint32_t e = blockIdx.x * (blockDim.x >> 5) + warp;
+    const uint32_t e0 = (blockIdx.x * (blockDim.x >> 5) + warp) * EPW;
     const uint32_t nj = in_dim / 128u;
-    const float *wr = w + (uint64_t)(e < n_expert ? e : 0u) * in_dim;
-    /* the first group of W chunks is in flight while x is staged */
-    float4 wv[PM_RT_G];
+    const float *wr[EPW];
 #pragma unroll
-    for (int q = 0; q < PM_RT_G; q++)
-        wv[q] = (uint32_t)q < nj ? __ldg((const float4 *)(wr + 128u * q + 4u * lane)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int ee = 0; ee < EPW; ee++) wr[ee] = w + (uint64_t)(e0 + ee < n_expert ? e0 + ee : 0u) * in_dim;
+    /* the first group of W chunks is in flight while x is staged */
+    float4 wv[G][EPW];
+#pragma unroll
+    for (int q = 0; q < G; q++)
+#pragma unroll
+        for (int ee = 0; ee < EPW; ee++)
+            wv[q][ee] = (uint32_t)q < nj ? __ldg((const float4 *)(wr[ee] + 128u * q + 4u * lane))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
     const uint32_t h4 = in_dim / 4u;
     for (uint32_t i = threadIdx.x; i < nt * h4; i += blockDim.x) {
         /* chunk j of token t: lane l's four values at [64 j + l] and [64 j + 32 + l] */
@@ -176,60 +184,76 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
         }
     }
     __syncthreads();
-    if (e >= n_expert) return;
-    double p[TPB];
+    if (e0 >= n_expert) return;
+    double p[EPW][TPB];
 #pragma unroll
-    for (int t = 0; t < TPB; t++) p[t] = 0.0; /* rows t >= nt hold stale data and are never written */
+    for (int ee = 0; ee < EPW; ee++)
+#pragma unroll
+        for (int t = 0; t < TPB; t++) p[ee][t] = 0.0; /* rows t >= nt hold stale data and are never written */
     const uint32_t h2 = in_dim / 2u;
-    for (uint32_t g = 0; g < nj; g += PM_RT_G) {
-        float4 nx[PM_RT_G]; /* the next group, loaded while this one is used */
+    for (uint32_t g = 0; g < nj; g += G) {
+        float4 nx[G][EPW]; /* the next group, loaded while this one is used */
 #pragma unroll
-        for (int q = 0; q < PM_RT_G; q++) {
-            const uint32_t jn = g + PM_RT_G + q;
-            nx[q] = jn < nj ? __ldg((const float4 *)(wr + 128u * jn + 4u * lane)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < G; q++) {
+            const uint32_t jn = g + G + q;
+#pragma unroll
+            for (int ee = 0; ee < EPW; ee++)
+                nx[q][ee] = jn < nj ? __ldg((const float4 *)(wr[ee] + 128u * jn + 4u * lane))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int q = 0; q < PM_RT_G; q++) {
+        for (int q = 0; q < G; q++) {
             const uint32_t j = g + q;
             if (j < nj) {
-                const double w0 = wv[q].x, w1 = wv[q].y, w2 = wv[q].z, w3 = wv[q].w;
 #pragma unroll
                 for (int t = 0; t < TPB; t++) {
                     const double2 a = xs[t * h2 + 64u * j + lane], b = xs[t * h2 + 64u * j + 32u + lane];
-                    p[t] = fma(w0, a.x, p[t]);
-                    p[t] = fma(w1, a.y, p[t]);
-                    p[t] = fma(w2, b.x, p[t]);
-                    p[t] = fma(w3, b.y, p[t]);
+#pragma unroll
+                    for (int ee = 0; ee < EPW; ee++) {
+                        p[ee][t] = fma((double)wv[q][ee].x, a.x, p[ee][t]);
+                        p[ee][t] = fma((double)wv[q][ee].y, a.y, p[ee][t]);
+                        p[ee][t] = fma((double)wv[q][ee].z, b.x, p[ee][t]);
+                        p[ee][t] = fma((double)wv[q][ee].w, b.y, p[ee][t]);
+                    }
                 }
             }
         }
 #pragma unroll
-        for (int q = 0; q < PM_RT_G; q++) wv[q] = nx[q];
+        for (int q = 0; q < G; q++)
+#pragma unroll
+            for (int ee = 0; ee < EPW; ee++) wv[q][ee] = nx[q][ee];
     }
 #pragma unroll
-    for (int t = 0; t < TPB; t++) {
-#pragma unroll
-        for (int m = 16; m > 0; m >>= 1) p[t] = p[t] + __shfl_xor_sync(0xffffffffu, p[t], m);
-    }
-    if (lane == 0) {
+    for (int ee = 0; ee < EPW; ee++)
 #pragma unroll
         for (int t = 0; t < TPB; t++) {
-            if ((uint32_t)t >= nt) break;
-            float l = __double2float_rn(p[t]);
-            if (lbias) l = __fadd_rn(l, lbias[e]);
-            logits[(uint64_t)(t0 + t) * n_expert + e] = l;
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) p[ee][t] = p[ee][t] + __shfl_xor_sync(0xffffffffu, p[ee][t], m);
+        }
+    if (lane == 0) {
+#pragma unroll
+        for (int ee = 0; ee < EPW; ee++) {
+            const uint32_t e = e0 + ee;
+            if (e >= n_expert) break;
+#pragma unroll
+            for (int t = 0; t < TPB; t++) {
+                if ((uint32_t)t >= nt) break;
+                float l = __double2float_rn(p[ee][t]);
+                if (lbias) l = __fadd_rn(l, lbias[e]);
+                logits[(uint64_t)(t0 + t) * n_expert + e] = l;
+            }
         }
     }
 }
 
-template <int TPB>
+template <int TPB, int EPW>
 static int pm_launch_router_tile(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
                                  uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq, cudaStream_t st) {
     static uint64_t done = 0;
     const uint32_t smem = TPB * in_dim * 8u;
-    if (!pm_smem_attr(pm_router_tile_kernel<TPB>, smem, &done)) return 0;
-    dim3 grid((n_expert + 7u) / 8u, (n_tok + TPB - 1) / TPB);
-    pm_router_tile_kernel<TPB><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq);
+    if (!pm_smem_attr(pm_router_tile_kernel<TPB, EPW>, smem, &done)) return 0;
+    dim3 grid((n_expert + 8u * EPW - 1u) / (8u * EPW), (n_tok + TPB - 1) / TPB);
+    pm_router_tile_kernel<TPB, EPW><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq);
     return pm_ok(cudaGetLastError(), "router logits launch");
 }
 
@@ -241,10 +265,12 @@ int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, co
         uint32_t tpb = n_tok >= 4 ? 4u : (n_tok >= 2 ? 2u : 1u);
         while (tpb > 1 && tpb * in_dim * 8u > 200u * 1024u) tpb >>= 1;
         pm_block_q8K *q = (pm_block_q8K *)xq;
+        if (tpb == 4 && n_tok >= 16) /* enough token tiles: 4 experts per warp */
+            return pm_launch_router_tile<4, 4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
         switch (tpb) {
-        case 4: return pm_launch_router_tile<4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
-        case 2: return pm_launch_router_tile<2>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
-        default: return pm_launch_router_tile<1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        case 4: return pm_launch_router_tile<4, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        case 2: return pm_launch_router_tile<2, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        default: return pm_launch_router_tile<1, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
         }
     }
     dim3 grid((n_expert + 3u) / 4u, (n_tok + PM_RT_TOK - 1) / PM_RT_TOK);
