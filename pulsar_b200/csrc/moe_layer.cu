@@ -988,7 +988,7 @@ extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t
 
 /* geometry of one matrix kind: 16 lanes per row when a row has at least
  * 32 unit pairs (2+ pairs per lane), else 4; a stage holds whole passes
- * of the warp (32 / lpr rows) and about 4.5 KB */
+ * of the warp (32 / lpr rows) */
 static pm_skind pm_kind_for(uint32_t nmat, uint64_t rb, uint32_t n) {
     pm_skind k;
     k.rb = rb;
@@ -996,7 +996,9 @@ static pm_skind pm_kind_for(uint32_t nmat, uint64_t rb, uint32_t n) {
     k.npair = (k.n_units + 1u) / 2u;
     k.lpr = k.npair >= 32u ? 16u : 4u;
     const uint32_t rpp = 32u / k.lpr;
-    uint64_t passes = 4608u / (nmat * rb * rpp);
+    /* ~9 KB stages where one CTA holds the SM (fewer stage hand-offs per row), ~4.5 KB otherwise */
+    const uint32_t target = pm_sk_minb((int)nmat) == 1 ? 9216u : 4608u;
+    uint64_t passes = target / (nmat * rb * rpp);
     if (passes < 1) passes = 1;
     k.rw = (uint32_t)(rpp * passes);
     return k;
