@@ -106,7 +106,7 @@ int pulsar_moe_down_bias(void *out, const void *ptrs, const void *weights, uint3
 int pulsar_add_bias_rows(void *x, const void *bias, uint32_t dim, uint32_t rows);
 
 /* replaces cu:6526 pulsar_matmul_f32 (klib:93), the router logits GEMV:
- * out[t][r] = W[r] . x[t] accumulated in binary64 in a fixed order */
+ * out[t][r] = W[r] . x[t] accumulated in f32 fused multiply-adds in a fixed order */
 int pulsar_matmul_f32(void *out, const void *w, const void *x, uint32_t in_dim, uint32_t out_dim, uint32_t n_tok);
 
 /* replaces cu:6494 pulsar_rms_norm (klib:88): out = x / rms(x) * w per

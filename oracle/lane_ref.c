@@ -39,14 +39,14 @@ float orc_glu(float g, float u, uint32_t op) {
 /* ------------------------------------------------------------- router */
 
 /* Router logits, the contract the CUDA router keeps bit-for-bit:
- * logit[t][e] = (float) S(t, e) + logit_bias[e], where S is the binary64
- * dot of the f32 router row with the f32 hidden row in a fixed order:
- * 32 partial sums p_L (L = 0..31) over the indices i = 128 j + 4 L + c
- * (j ascending, then c = 0..3), each product exact in binary64, followed
- * by the butterfly p_L += p_(L^m) for m = 16, 8, 4, 2, 1.  The reference
- * computes the same dot in f32 with a 256-way tree (cu:6504-6524); the
- * binary64 order is this project's choice so that top-k ties resolve
- * identically on host and device. */
+ * logit[t][e] = S(t, e) + logit_bias[e], where S is the f32 dot of the f32
+ * router row with the f32 hidden row in a fixed order: 32 partial sums p_L
+ * (L = 0..31) over the indices i = 128 j + 4 L + c (j ascending, then
+ * c = 0..3), each step one fused multiply-add, followed by the butterfly
+ * p_L += p_(L^m) for m = 16, 8, 4, 2, 1.  The reference computes the same dot
+ * in f32 with a 256-way tree (cu:6504-6524); the fixed order is this
+ * project's choice so that top-k ties resolve identically on host and
+ * device. */
 void orc_router_logits(float *logits, const float *w, const float *x, const float *logit_bias,
                        uint32_t n_expert, uint32_t in_dim, uint32_t n_tok) {
     const uint32_t nj = (in_dim + 127) / 128;
@@ -54,22 +54,22 @@ void orc_router_logits(float *logits, const float *w, const float *x, const floa
         const float *xr = x + (size_t)t * in_dim;
         for (uint32_t e = 0; e < n_expert; e++) {
             const float *wr = w + (size_t)e * in_dim;
-            double p[32];
+            float p[32];
             for (int L = 0; L < 32; L++) {
-                double s = 0.0;
+                float s = 0.0f;
                 for (uint32_t j = 0; j < nj; j++)
                     for (int c = 0; c < 4; c++) {
                         uint32_t i = 128 * j + 4 * (uint32_t)L + (uint32_t)c;
-                        if (i < in_dim) s = fma((double)wr[i], (double)xr[i], s);
+                        if (i < in_dim) s = fmaf(wr[i], xr[i], s);
                     }
                 p[L] = s;
             }
             for (int m = 16; m >= 1; m >>= 1) {
-                double q[32];
+                float q[32];
                 for (int L = 0; L < 32; L++) q[L] = p[L] + p[L ^ m];
                 memcpy(p, q, sizeof(p));
             }
-            float l = (float)p[0];
+            float l = p[0];
             if (logit_bias) l = l + logit_bias[e];
             logits[(size_t)t * n_expert + e] = l;
         }

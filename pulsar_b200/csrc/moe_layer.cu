@@ -6,7 +6,7 @@
  * the per-(token, slot) pointer array on the host, writes it back and then
  * launches pair / q8_K / down.  Here the whole layer stays on the device:
  *
- *   1 router logits (binary64 fixed-order GEMV) ........ router_q8k.cu
+ *   1 router logits (f32 fixed-order GEMV) + q8_K(x) ... router_q8k.cu
  *   2 q8_K of the hidden rows ........................... router_q8k.cu
  *   3 top-k per token (warp per token); the last CTA to finish groups the
  *     (token, slot) pairs by expert into a CSR work list (ascending expert

@@ -12,10 +12,10 @@
  *    point, 8 digits of 2 bits); the dot kernels expand digit d to the
  *    integer {8, 25, 43}[d] and the encoder to the odd coordinate 2d+1
  *    (crates/quant/src/iq.rs:17-52, cpu_dot_tables.rs:176).
- *  - pm_expf is this project's own single-precision exponential, evaluated
- *    in double precision with explicit fma so that host and device produce
- *    identical bits.  The router's selection scores go through it, which is
- *    what makes the top-k indices reproducible bit-for-bit on the CPU.
+ *  - pm_expf is this project's own single-precision exponential, built from
+ *    IEEE fma / mul steps only, so that host and device produce identical
+ *    bits.  The router's selection scores go through it, which is what makes
+ *    the top-k indices reproducible bit-for-bit on the CPU.
  */
 #ifndef PM_FORMAT_H
 #define PM_FORMAT_H
@@ -199,39 +199,40 @@ PM_HD float pm_mxfp4_scale_half(uint32_t e) {
 
 /* ------------------------------------------------- deterministic math */
 
-/* exp(x) for binary32 x, computed in binary64 and rounded once.
- * Method: Cody-Waite style range reduction x = k*ln2 + r with
- * k = nearest(x/ln2) and |r| <= ln2/2, then the degree-12 Taylor series
- * of exp(r) in Horner form (truncation error < 2e-17 relative), then an
- * exact scaling by 2^k built from the exponent field.  Every step uses
- * explicit fma or single IEEE operations, so a C host and a CUDA device
- * produce identical bits.  Max error vs the true value is well under
- * 1 ulp of binary32 (checked against libm expf in the tests). */
-PM_HD float pm_expf(float xf) {
-    if (xf != xf) return xf;
-    if (xf > 88.8f) return INFINITY;
-    if (xf < -104.0f) return 0.0f;
-    const double x = (double)xf;
-    const double kd = rint(x * 1.4426950408889634074);
-    const double r = fma(-kd, 1.9082149292705877000e-10, fma(-kd, 6.9314718036912381649e-01, x));
-    double p = 1.0 / 479001600.0;            /* 1/12! */
-    p = fma(p, r, 1.0 / 39916800.0);          /* 1/11! */
-    p = fma(p, r, 1.0 / 3628800.0);
-    p = fma(p, r, 1.0 / 362880.0);
-    p = fma(p, r, 1.0 / 40320.0);
-    p = fma(p, r, 1.0 / 5040.0);
-    p = fma(p, r, 1.0 / 720.0);
-    p = fma(p, r, 1.0 / 120.0);
-    p = fma(p, r, 1.0 / 24.0);
-    p = fma(p, r, 1.0 / 6.0);
-    p = fma(p, r, 0.5);
-    p = fma(p, r, 1.0);
-    p = fma(p, r, 1.0);
-    const int64_t k = (int64_t)kd;
-    uint64_t sbits = (uint64_t)(k + 1023) << 52;
-    double s;
-    memcpy(&s, &sbits, 8);
-    return (float)(p * s);
+/* exp(x) for binary32 x in binary32 arithmetic only (the GPUs this runs on
+ * have a slow binary64 pipe).  Method: Cody-Waite reduction x = k ln2 + r,
+ * k = nearest(x log2 e), with ln2 split into a head of 16 significant bits
+ * (k * head exact) and a tail, both applied with fma, so |r| <= ln2/2 to
+ * within an ulp of r; then the degree-7 Taylor series of exp(r) in Horner
+ * form with fma (truncation < 1e-8 relative); then 2^k as two exact powers
+ * of two built from the exponent field (one rounding, into the subnormal
+ * range for k < -126).  Only IEEE fma / mul / div steps: a C host and a CUDA
+ * device produce identical bits.  Error vs the true value: within 1 ulp
+ * (checked against libm exp in the tests). */
+PM_HD float pm_pow2i(int k) { /* 2^k for k in [-126, 127] */
+    const uint32_t bits = (uint32_t)(k + 127) << 23;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+PM_HD float pm_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    const float k = rintf(x * 1.44269504088896340736f);
+    float r = fmaf(-k, 0.693145751953125f, x);   /* head of ln 2: 16 significant bits */
+    r = fmaf(-k, 1.428606765330187045e-06f, r);  /* ln 2 - head */
+    float p = 1.0f / 5040.0f;
+    p = fmaf(p, r, 1.0f / 720.0f);
+    p = fmaf(p, r, 1.0f / 120.0f);
+    p = fmaf(p, r, 1.0f / 24.0f);
+    p = fmaf(p, r, 1.0f / 6.0f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ki = (int)k, k1 = ki / 2, k2 = ki - k1; /* both within the normal exponent range */
+    return (p * pm_pow2i(k1)) * pm_pow2i(k2);
 }
 
 /* router probability, same branch structure as the reference router

@@ -8,8 +8,8 @@
  *    quantizer (cu:1498, signed-max iscale with rint), because the CPU
  *    lane's bytes are the parity target.  Layout: the reference's
  *    292-byte block_q8_K (cu:1492), tail elements beyond in_dim zero.
- *  - logits are a binary64 dot in a fixed order (32 lane partials over
- *    i = 128 j + 4 lane + c, then an xor butterfly), rounded once to f32;
+ *  - logits are an f32 fused-multiply-add dot in a fixed order (32 lane
+ *    partials over i = 128 j + 4 lane + c, then an xor butterfly);
  *    selection scores use pm_expf, so top-k indices and route weights
  *    reproduce exactly on the host.
  */
@@ -48,9 +48,9 @@ extern "C" int pulsar_quantize_q8_K(void *out_dev, const void *x_dev, uint32_t i
 
 /* ----------------------------------------------------------- logits */
 
-/* warp per (expert, token group of 4): binary64 partials in the fixed
- * order, xor butterfly, one rounding.  W rows may be any length; the
- * float4 path needs in_dim % 4 == 0 (16-byte aligned rows). */
+/* warp per (expert, token group of 4): f32 fma partials in the fixed
+ * order, then the xor butterfly.  W rows may be any length; the float4
+ * path needs in_dim % 4 == 0 (16-byte aligned rows). */
 #define PM_RT_TOK 4
 __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, const float *__restrict__ w,
                                                                const float *__restrict__ x,
@@ -62,9 +62,9 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
     if (e >= n_expert) return;
     const uint32_t nt = n_tok - t0 < PM_RT_TOK ? n_tok - t0 : PM_RT_TOK;
     const float *wr = w + (uint64_t)e * in_dim;
-    double p[PM_RT_TOK];
+    float p[PM_RT_TOK];
 #pragma unroll
-    for (int t = 0; t < PM_RT_TOK; t++) p[t] = 0.0;
+    for (int t = 0; t < PM_RT_TOK; t++) p[t] = 0.0f;
     const uint32_t nj = (in_dim + 127u) / 128u;
     if ((in_dim & 127u) == 0) {
         /* whole 128-wide chunks: four chunks of W and x in flight per step */
@@ -84,10 +84,10 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
             for (int q = 0; q < 4; q++)
 #pragma unroll
                 for (int t = 0; t < PM_RT_TOK; t++) {
-                    p[t] = fma((double)wv[q].x, (double)xv[q][t].x, p[t]);
-                    p[t] = fma((double)wv[q].y, (double)xv[q][t].y, p[t]);
-                    p[t] = fma((double)wv[q].z, (double)xv[q][t].z, p[t]);
-                    p[t] = fma((double)wv[q].w, (double)xv[q][t].w, p[t]);
+                    p[t] = fmaf(wv[q].x, xv[q][t].x, p[t]);
+                    p[t] = fmaf(wv[q].y, xv[q][t].y, p[t]);
+                    p[t] = fmaf(wv[q].z, xv[q][t].z, p[t]);
+                    p[t] = fmaf(wv[q].w, xv[q][t].w, p[t]);
                 }
         }
         for (; j < nj; j++) {
@@ -96,10 +96,10 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
             for (int t = 0; t < PM_RT_TOK; t++) {
                 if ((uint32_t)t >= nt) break;
                 const float4 xv = __ldg((const float4 *)(x + (uint64_t)(t0 + t) * in_dim + 128u * j + 4u * lane));
-                p[t] = fma((double)wv.x, (double)xv.x, p[t]);
-                p[t] = fma((double)wv.y, (double)xv.y, p[t]);
-                p[t] = fma((double)wv.z, (double)xv.z, p[t]);
-                p[t] = fma((double)wv.w, (double)xv.w, p[t]);
+                p[t] = fmaf(wv.x, xv.x, p[t]);
+                p[t] = fmaf(wv.y, xv.y, p[t]);
+                p[t] = fmaf(wv.z, xv.z, p[t]);
+                p[t] = fmaf(wv.w, xv.w, p[t]);
             }
         }
     } else {
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
                 const float *xr = x + (uint64_t)(t0 + t) * in_dim;
 #pragma unroll
                 for (int c = 0; c < 4; c++)
-                    if (i0 + c < in_dim) p[t] = fma((double)wr[i0 + c], (double)xr[i0 + c], p[t]);
+                    if (i0 + c < in_dim) p[t] = fmaf(wr[i0 + c], xr[i0 + c], p[t]);
             }
         }
     }
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
 #pragma unroll
         for (int t = 0; t < PM_RT_TOK; t++) {
             if ((uint32_t)t >= nt) break;
-            float l = __double2float_rn(p[t]);
+            float l = p[t];
             if (lbias) l = __fadd_rn(l, lbias[e]);
             logits[(uint64_t)(t0 + t) * n_expert + e] = l;
         }
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(128) pm_router_logits_kernel(float *logits, co
 }
 
 /* Token-tiled variant (in_dim % 128 == 0): a CTA stages TPB tokens' rows
- * of x in shared memory once, already widened to binary64, and its 8
+ * of x in shared memory once, and its 8
  * warps each take one expert, so x is read from L2 and converted once
  * per 8 experts instead of once per expert.  Every (expert, token) dot
  * keeps the fixed order above (lane partials over i = 128 j + 4 lane + c,
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
                                                              const float *__restrict__ lbias, uint32_t n_expert,
                                                              uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq) {
     constexpr int G = EPW == 1 ? 8 : 2;
-    extern __shared__ double2 xs[]; /* [TPB][in_dim / 2] */
+    extern __shared__ float4 xs[]; /* [TPB][in_dim / 4] */
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t t0 = blockIdx.y * TPB;
     const uint32_t nt = n_tok - t0 < (uint32_t)TPB ? n_tok - t0 : (uint32_t)TPB;
@@ -166,14 +166,8 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
             wv[q][ee] = (uint32_t)q < nj ? __ldg((const float4 *)(wr[ee] + 128u * q + 4u * lane))
                                          : make_float4(0.f, 0.f, 0.f, 0.f);
     const uint32_t h4 = in_dim / 4u;
-    for (uint32_t i = threadIdx.x; i < nt * h4; i += blockDim.x) {
-        /* chunk j of token t: lane l's four values at [64 j + l] and [64 j + 32 + l] */
-        const uint32_t t = i / h4, r = i % h4;
-        const float4 v = __ldg((const float4 *)(x + (uint64_t)(t0 + t) * in_dim) + r);
-        const uint32_t o = t * (in_dim / 2u) + 64u * (r >> 5) + (r & 31u);
-        xs[o] = make_double2((double)v.x, (double)v.y);
-        xs[o + 32u] = make_double2((double)v.z, (double)v.w);
-    }
+    for (uint32_t i = threadIdx.x; i < nt * h4; i += blockDim.x)
+        xs[i] = __ldg((const float4 *)(x + (uint64_t)(t0 + i / h4) * in_dim) + i % h4);
     if (xq && blockIdx.x == 0) {
         const uint32_t nb = (in_dim + 255u) / 256u;
         for (uint32_t job = warp; job < nt * nb; job += blockDim.x >> 5) {
@@ -185,12 +179,11 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
     }
     __syncthreads();
     if (e0 >= n_expert) return;
-    double p[EPW][TPB];
+    float p[EPW][TPB];
 #pragma unroll
     for (int ee = 0; ee < EPW; ee++)
 #pragma unroll
-        for (int t = 0; t < TPB; t++) p[ee][t] = 0.0; /* rows t >= nt hold stale data and are never written */
-    const uint32_t h2 = in_dim / 2u;
+        for (int t = 0; t < TPB; t++) p[ee][t] = 0.0f; /* rows t >= nt hold stale data and are never written */
     for (uint32_t g = 0; g < nj; g += G) {
         float4 nx[G][EPW]; /* the next group, loaded while this one is used */
 #pragma unroll
@@ -207,13 +200,13 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
             if (j < nj) {
 #pragma unroll
                 for (int t = 0; t < TPB; t++) {
-                    const double2 a = xs[t * h2 + 64u * j + lane], b = xs[t * h2 + 64u * j + 32u + lane];
+                    const float4 a = xs[t * h4 + 32u * j + lane];
 #pragma unroll
                     for (int ee = 0; ee < EPW; ee++) {
-                        p[ee][t] = fma((double)wv[q][ee].x, a.x, p[ee][t]);
-                        p[ee][t] = fma((double)wv[q][ee].y, a.y, p[ee][t]);
-                        p[ee][t] = fma((double)wv[q][ee].z, b.x, p[ee][t]);
-                        p[ee][t] = fma((double)wv[q][ee].w, b.y, p[ee][t]);
+                        p[ee][t] = fmaf(wv[q][ee].x, a.x, p[ee][t]);
+                        p[ee][t] = fmaf(wv[q][ee].y, a.y, p[ee][t]);
+                        p[ee][t] = fmaf(wv[q][ee].z, a.z, p[ee][t]);
+                        p[ee][t] = fmaf(wv[q][ee].w, a.w, p[ee][t]);
                     }
                 }
             }
@@ -238,7 +231,7 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
 #pragma unroll
             for (int t = 0; t < TPB; t++) {
                 if ((uint32_t)t >= nt) break;
-                float l = __double2float_rn(p[ee][t]);
+                float l = p[ee][t];
                 if (lbias) l = __fadd_rn(l, lbias[e]);
                 logits[(uint64_t)(t0 + t) * n_expert + e] = l;
             }
@@ -250,7 +243,7 @@ template <int TPB, int EPW>
 static int pm_launch_router_tile(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
                                  uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq, cudaStream_t st) {
     static uint64_t done = 0;
-    const uint32_t smem = TPB * in_dim * 8u;
+    const uint32_t smem = TPB * in_dim * 4u;
     if (!pm_smem_attr(pm_router_tile_kernel<TPB, EPW>, smem, &done)) return 0;
     dim3 grid((n_expert + 8u * EPW - 1u) / (8u * EPW), (n_tok + TPB - 1) / TPB);
     pm_router_tile_kernel<TPB, EPW><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq);
@@ -263,7 +256,7 @@ int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, co
     if (in_dim % 128u == 0 && in_dim <= 25600u) {
         /* tokens per tile: no more than the batch, x tile within 200 KB */
         uint32_t tpb = n_tok >= 4 ? 4u : (n_tok >= 2 ? 2u : 1u);
-        while (tpb > 1 && tpb * in_dim * 8u > 200u * 1024u) tpb >>= 1;
+        while (tpb > 1 && tpb * in_dim * 4u > 200u * 1024u) tpb >>= 1;
         pm_block_q8K *q = (pm_block_q8K *)xq;
         if (tpb == 4 && n_tok >= 16) /* enough token tiles: 4 experts per warp */
             return pm_launch_router_tile<4, 4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
@@ -285,8 +278,7 @@ int pm_launch_router_logits(float *logits, const float *w, const float *x, const
 }
 
 /* cu:6526 pulsar_matmul_f32: out[t][r] = W[r] . x[t], here in the fixed
- * binary64 order above (deterministic; equal to the f32 dot within f32
- * rounding) */
+ * f32 order above (deterministic) */
 extern "C" int pulsar_matmul_f32(void *out_dev, const void *w_dev, const void *x_dev, uint32_t in_dim,
                                  uint32_t out_dim, uint32_t n_tok) {
     if (!out_dev || !w_dev || !x_dev || in_dim == 0 || out_dim == 0 || n_tok == 0) return 0;
