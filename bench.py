@@ -48,9 +48,9 @@ import torch  # noqa: E402
 CFG = dict(name="C2", n_embd=2048, n_ff=512, n_expert=256, n_used=8, layers=40, zipf=1.1, batches=(1, 8, 64))
 METRIC = "MoE-layer tokens/s and % of HBM/tensor roofline at 1/2/4/8 B200"
 # DRAM bytes (read + write) per gate/up launch over the launch's algorithmic bytes, from one
-# ncu capture of this workload (profiles/pm_layer_sk_kernel_c2_b64.md: 228.3 + 18.3 MB
+# ncu capture of this workload (profiles/pm_layer_sk_kernel_c2_b64.md: 228.4 + 13.2 MB
 # against 221.2 MB); the reported traffic scales it to this run's launch.
-TRAFFIC_RATIO = (228.26 + 18.35) / 221.2
+TRAFFIC_RATIO = (228.40 + 13.16) / 221.2
 TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of pm_layer_sk_kernel gate/up (config 2, "
                 "batch 64) / algorithmic bytes, times this run's algorithmic bytes per launch")
 UNIT = "tokens/s"
@@ -189,6 +189,12 @@ class Runner:
         with torch.cuda.stream(self.stream):
             self.x.copy_(x_dev, non_blocking=True)
             self.graph.replay()
+
+
+def launches_per_layer(T: int) -> int:
+    """kernels one layer step launches: rms_norm, router (+ q8_K of x), selection, gate/up,
+    down, combine, plus the three tensor-core kernels when an expert can reach 128 tokens"""
+    return 6 + (3 if T >= 128 else 0)
 
 
 def max_over_ranks(ms: float, world: int) -> float:
@@ -462,7 +468,7 @@ def main():
                 "config": config,
                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
-                "gpu_launches": 7 * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
+                "gpu_launches": launches_per_layer(T) * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
                 "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
     if line is not None:
         print(json.dumps(line), flush=True)
