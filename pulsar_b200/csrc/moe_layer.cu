@@ -464,7 +464,7 @@ __device__ __forceinline__ void pm_stage_src(const pm_segi &s, const pm_skind &k
  * unit, glu * route weight -> mid.  EPI 1: down of every work unit (mid
  * rows quantized to q8_K while staging) -> one partial row per pair. */
 template <int QR, int QS, int NMAT, int EPI>
-__global__ void __launch_bounds__(PM_THREADS, pm_sk_minb(NMAT))
+__global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
     pm_layer_sk_kernel(const __grid_constant__ pm_layer_args a, const __grid_constant__ pm_skp P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t s_cnt[2], s_lim[4], s_tok[PM_TT];
@@ -564,7 +564,7 @@ __global__ void __launch_bounds__(PM_THREADS, pm_sk_minb(NMAT))
     while (ni < P.S && iti.k < sl.n_seg) {
         if (lane == 0) issue(ni);
         ni++;
-        iti.g += PM_WARPS;
+        iti.g += (uint32_t)pm_sk_warps(NMAT);
         pm_it_norm<EPI>(iti, a, tab, sl, P);
     }
 
@@ -628,11 +628,11 @@ __global__ void __launch_bounds__(PM_THREADS, pm_sk_minb(NMAT))
                     issue(slot);
                 }
                 ni++;
-                iti.g += PM_WARPS;
+                iti.g += (uint32_t)pm_sk_warps(NMAT);
                 pm_it_norm<EPI>(iti, a, tab, sl, P);
             }
             ci++;
-            itc.g += PM_WARPS;
+            itc.g += (uint32_t)pm_sk_warps(NMAT);
             pm_it_norm<EPI>(itc, a, tab, sl, P);
         }
     }
@@ -997,7 +997,7 @@ static pm_skind pm_kind_for(uint32_t nmat, uint64_t rb, uint32_t n) {
     k.lpr = k.npair >= 32u ? 16u : 4u;
     const uint32_t rpp = 32u / k.lpr;
     /* ~9 KB stages where one CTA holds the SM (fewer stage hand-offs per row), ~4.5 KB otherwise */
-    const uint32_t target = pm_sk_minb((int)nmat) == 1 ? 9216u : 4608u;
+    const uint32_t target = pm_sk_minb((int)nmat) == 1 && pm_sk_warps((int)nmat) <= 8 ? 9216u : 4608u;
     uint64_t passes = target / (nmat * rb * rpp);
     if (passes < 1) passes = 1;
     k.rw = (uint32_t)(rpp * passes);
@@ -1021,17 +1021,18 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
     P.off_acts = (off + 15u) & ~15u;
     off = P.off_acts + pm_acts_bytes(P.P, P.NB);
     P.off_bar = (off + 15u) & ~15u;
-    P.off_ring = (P.off_bar + PM_WARPS * 8u * 8u + 127u) & ~127u;
+    const uint32_t W = (uint32_t)pm_sk_warps((int)nmat);
+    P.off_ring = (P.off_bar + W * 8u * 8u + 127u) & ~127u;
     const uint32_t budget = pm_sk_minb(nmat) == 1 ? 200u * 1024u : 110u * 1024u;
-    uint32_t S = budget > P.off_ring ? (budget - P.off_ring) / (PM_WARPS * P.stage) : 2u;
+    uint32_t S = budget > P.off_ring ? (budget - P.off_ring) / (W * P.stage) : 2u;
     P.S = S < 2 ? 2 : (S > 8 ? 8 : S);
-    P.smem = P.off_ring + PM_WARPS * P.S * P.stage;
+    P.smem = P.off_ring + W * P.S * P.stage;
     return P;
 }
 
 /* persistent grid: resident CTAs per SM x SMs, cached per device */
 template <class K>
-static uint32_t pm_sk_grid(K kernel, uint32_t smem, int *occ, uint32_t *occ_smem) {
+static uint32_t pm_sk_grid(K kernel, uint32_t smem, int *occ, uint32_t *occ_smem, uint32_t threads = PM_THREADS) {
     static int sms[64];
     const int dev = pm_cur_device();
     if (dev < 0 || dev >= 64) return 0;
@@ -1039,7 +1040,7 @@ static uint32_t pm_sk_grid(K kernel, uint32_t smem, int *occ, uint32_t *occ_smem
         return 0;
     if (occ_smem[dev] != smem || occ[dev] <= 0) {
         int n = 0;
-        if (!pm_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, PM_THREADS, smem), "occupancy"))
+        if (!pm_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, (int)threads, smem), "occupancy"))
             return 0;
         occ[dev] = n;
         occ_smem[dev] = smem;
@@ -1080,9 +1081,9 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     const pm_skp pg = pm_skp_for(2, gr, a.S ? pm_kind_for(2, a.rb_gu_s, a.H) : gr, grid);
     auto kgu = pm_layer_sk_kernel<QR, QS, 2, 0>;
     if (!pm_smem_attr(kgu, pg.smem, &done_gu)) return 0;
-    const uint32_t g_gu = pm_sk_grid(kgu, pg.smem, occ_gu, sm_gu);
+    const uint32_t g_gu = pm_sk_grid(kgu, pg.smem, occ_gu, sm_gu, 32u * pm_sk_warps(2));
     if (!g_gu) return 0;
-    kgu<<<g_gu, PM_THREADS, pg.smem, st>>>(a, pg);
+    kgu<<<g_gu, 32u * pm_sk_warps(2), pg.smem, st>>>(a, pg);
     if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
     if (tc) { /* tensor-core pairs: mid and its q8_K */
         dim3 gm(L.max_tc * (PM_TC_N / PM_TC_MID_TG), (L.Fmax + 255u) / 256u);
@@ -1097,9 +1098,9 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     const pm_skp pd = pm_skp_for(1, dr, a.S ? pm_kind_for(1, a.rb_dn_s, a.Fs) : dr, grid);
     auto kdn = pm_layer_sk_kernel<QR, QS, 1, 1>;
     if (!pm_smem_attr(kdn, pd.smem, &done_dn)) return 0;
-    const uint32_t g_dn = pm_sk_grid(kdn, pd.smem, occ_dn, sm_dn);
+    const uint32_t g_dn = pm_sk_grid(kdn, pd.smem, occ_dn, sm_dn, 32u * pm_sk_warps(1));
     if (!g_dn) return 0;
-    kdn<<<g_dn, PM_THREADS, pd.smem, st>>>(a, pd);
+    kdn<<<g_dn, 32u * pm_sk_warps(1), pd.smem, st>>>(a, pd);
     if (!pm_ok(cudaGetLastError(), "moe layer down launch")) return 0;
     /* 6: combine */
     const uint64_t tot = (uint64_t)a.T * a.H;

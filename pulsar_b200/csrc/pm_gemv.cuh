@@ -45,10 +45,15 @@
 #define PM_SK_CR 2u   /* per-row decode cost, in token-dot units */
 #define PM_SK_RQ 8u   /* slice boundaries fall on multiples of this many rows */
 #define PM_SK_MAXSEG 64u
+#ifndef PM_SK_GU_WARPS
+#define PM_SK_GU_WARPS 12
+#endif
 /* resident CTAs per SM the stream-K kernels are compiled for: gate/up (two
  * matrices, the larger register tile) runs one CTA per SM with the whole
  * register file and a deep ring; down runs two */
 __host__ __device__ constexpr int pm_sk_minb(int nmat) { return nmat == 2 ? 1 : 2; }
+/* warps per CTA of the stream-K kernels */
+__host__ __device__ constexpr int pm_sk_warps(int nmat) { return nmat == 2 ? PM_SK_GU_WARPS : 8; }
 
 /* ------------------------------------------------------- activations */
 
