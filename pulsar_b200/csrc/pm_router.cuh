@@ -139,6 +139,42 @@ __device__ __forceinline__ void pm_select_token(int32_t *selected, float *weight
 }
 
 
+/* compare-exchange by (score desc, index asc) */
+__device__ __forceinline__ void pm_cx(float &as, uint32_t &ai, float &bs, uint32_t &bi) {
+    if (pm_better(bs, bi, as, ai)) {
+        const float ts = as;
+        const uint32_t ti = ai;
+        as = bs, ai = bi;
+        bs = ts, bi = ti;
+    }
+}
+
+/* 8 pairs into descending order (Batcher odd-even merge sort, 19 exchanges) */
+__device__ __forceinline__ void pm_sort8(float *s, uint32_t *i) {
+#define PM_CX(a, b) pm_cx(s[a], i[a], s[b], i[b])
+    PM_CX(0, 1); PM_CX(2, 3); PM_CX(4, 5); PM_CX(6, 7);
+    PM_CX(0, 2); PM_CX(1, 3); PM_CX(4, 6); PM_CX(5, 7);
+    PM_CX(1, 2); PM_CX(5, 6);
+    PM_CX(0, 4); PM_CX(1, 5); PM_CX(2, 6); PM_CX(3, 7);
+    PM_CX(2, 4); PM_CX(3, 5);
+    PM_CX(1, 2); PM_CX(3, 4); PM_CX(5, 6);
+#undef PM_CX
+}
+
+/* a (sorted desc) := the 8 best of a and b (both sorted desc), sorted desc:
+ * a[i] vs b[7 - i] keeps the top 8 as a bitonic sequence, then a bitonic
+ * merge of 8 */
+__device__ __forceinline__ void pm_merge8(float *as, uint32_t *ai, const float *bs, const uint32_t *bi) {
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+        if (pm_better(bs[7 - k], bi[7 - k], as[k], ai[k])) as[k] = bs[7 - k], ai[k] = bi[7 - k];
+#define PM_CX(a, b) pm_cx(as[a], ai[a], as[b], ai[b])
+    PM_CX(0, 4); PM_CX(1, 5); PM_CX(2, 6); PM_CX(3, 7);
+    PM_CX(0, 2); PM_CX(1, 3); PM_CX(4, 6); PM_CX(5, 7);
+    PM_CX(0, 1); PM_CX(2, 3); PM_CX(4, 5); PM_CX(6, 7);
+#undef PM_CX
+}
+
 /* Fast path of pm_select_token for the fused layer: modes 0 and 1, no group
  * limit, n_expert <= 256, k_used <= 32.  Same operations and tie rule as
  * pm_select_token (and the CPU restatement), so the same bits:
@@ -182,6 +218,67 @@ __device__ __forceinline__ void pm_select_fast(int32_t *selected, float *weights
         const uint32_t e = lane + 32u * (uint32_t)i;
         sc[i] = score[e];
         pr[i] = prob[e];
+    }
+    /* top-k by a warp merge when k <= 8 and at least k scores are finite (then the
+     * rounds below would pick exactly the k best by (score desc, index asc), in that
+     * order); otherwise the rounds, which also cover picks among -inf scores */
+    if (k_used <= 8u) {
+        float ks[8];
+        uint32_t ki[8];
+        uint32_t nfin = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t e = lane + 32u * (uint32_t)i;
+            const bool ok = e < n_expert && sc[i] > -INFINITY; /* false for NaN */
+            ks[i] = ok ? sc[i] : -INFINITY;
+            ki[i] = ok ? e : UINT32_MAX;
+            nfin += ok ? 1u : 0u;
+        }
+        for (int o = 16; o > 0; o >>= 1) nfin += __shfl_xor_sync(0xffffffffu, nfin, o);
+        if (nfin >= k_used) {
+            pm_sort8(ks, ki);
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) {
+                float os[8];
+                uint32_t oi[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    os[i] = __shfl_xor_sync(0xffffffffu, ks[i], m);
+                    oi[i] = __shfl_xor_sync(0xffffffffu, ki[i], m);
+                }
+                pm_merge8(ks, ki, os, oi);
+            }
+            /* every lane holds the 8 best in pick order; lane s takes slot s */
+            uint32_t e_s = UINT32_MAX;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if ((uint32_t)i == lane) e_s = ki[i];
+            float sum = 0.0f, bp_s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if ((uint32_t)i >= k_used) break;
+                const float bp = prob[ki[i]];
+                if ((uint32_t)i == lane) bp_s = bp;
+                sum = __fadd_rn(sum, bp);
+            }
+            float w;
+            if (mode == 1u) {
+                float m = lane < k_used ? bp_s : -INFINITY;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                const float ex = lane < k_used ? pm_expf(__fsub_rn(bp_s, m)) : 0.0f;
+                float es = 0.0f;
+                for (uint32_t s2 = 0; s2 < k_used; s2++) es = __fadd_rn(es, __shfl_sync(0xffffffffu, ex, s2));
+                w = __fmul_rn(__fdiv_rn(ex, es), weight_scale);
+            } else {
+                w = __fmul_rn(__fdiv_rn(bp_s, fmaxf(sum, 6.103515625e-5f)), weight_scale);
+            }
+            if (lane < k_used) {
+                selected[(uint64_t)token * out_stride + lane] = (int32_t)e_s;
+                weights[(uint64_t)token * out_stride + lane] = w;
+            }
+            return;
+        }
     }
     auto local_best = [&](float &bv, uint32_t &bi) {
         bv = -INFINITY;
