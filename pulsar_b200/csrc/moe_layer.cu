@@ -49,7 +49,10 @@ __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 #define PM_TC_MIN 128u /* experts with at least this many tokens take the tensor-core path */
 
 /* formats with a tensor-core (fp16 dequant) path */
-static bool pm_tc_fmt(uint32_t q) { return q == PM_QUANT_Q4_K; }
+static bool pm_tc_fmt(uint32_t q) {
+    return q == PM_QUANT_Q4_K || q == PM_QUANT_Q2_K || q == PM_QUANT_IQ2_XXS || q == PM_QUANT_MXFP4 ||
+           q == PM_QUANT_Q8_0;
+}
 
 static int pm_sm_count() {
     static int sms[64];
@@ -652,13 +655,82 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
  * (M 128, N PM_TC_N, K 16) and commits them to the stage's mbarrier, which
  * frees the stage pm_tcg::S chunks later.  Tensor memory holds NMAT x N fp32
  * columns for the CTA's lifetime. */
+/* 8 weights of a row, values 64 c + 8 j .. + 7, in f32 (exact products of
+ * the block's integers and scales, as the dot functors use them: Q8_0 cu:2174,
+ * MXFP4 cu:2053 doubled e2m1 x 2^(e-128), Q2_K cu:1625, IQ2_XXS cu:1582).
+ * Rows of these formats are only 2- (Q8_0, IQ2_XXS), 4- (Q2_K) or 1-byte
+ * (MXFP4) aligned, so the loads are of that width. */
+template <int Q>
+__device__ __forceinline__ void pm_tc_group(const uint8_t *row, uint32_t c, uint32_t j, float *v) {
+    if constexpr (Q == PM_QUANT_Q8_0) {
+        const uint8_t *b = row + (size_t)(2u * c + (j >> 2)) * PM_Q8_0_BLOCK;
+        const float d = pm_h2f(__ldg((const uint16_t *)b));
+        const uint16_t *q = (const uint16_t *)(b + 2 + 8u * (j & 3u));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t w = __ldg(q + i);
+            v[2 * i] = d * (float)(int8_t)(w & 0xffu);
+            v[2 * i + 1] = d * (float)(int8_t)(w >> 8);
+        }
+    } else if constexpr (Q == PM_QUANT_MXFP4) {
+        const uint8_t *b = row + (size_t)(2u * c + (j >> 2)) * PM_MXFP4_BLOCK;
+        const float sc = pm_mxfp4_scale_half(__ldg(b));
+        const uint32_t e0 = 8u * (j & 3u); /* element of the block: low nibbles 0-15, high 16-31 */
+        const uint32_t sh = e0 < 16u ? 0u : 4u;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t code = (__ldg(b + 1 + ((e0 + (uint32_t)i) & 15u)) >> sh) & 15u;
+            const uint32_t m = code & 7u;
+            const float mag = (float)(m < 4u ? m : (m == 4u ? 4u : (m == 5u ? 6u : (m == 6u ? 8u : 12u))));
+            v[i] = (code & 8u ? -mag : mag) * sc;
+        }
+    } else if constexpr (Q == PM_QUANT_Q2_K) {
+        const uint8_t *b = row + (size_t)(c >> 2) * PM_Q2_K_BYTES;
+        const uint32_t i0 = 64u * (c & 3u) + 8u * j; /* element in the super-block */
+        const uint32_t n = i0 >> 7, sft = 2u * ((i0 & 127u) >> 5), jj = i0 & 31u;
+        const uint32_t scb = __ldg(b + (i0 >> 4));
+        const uint32_t dd = __ldg((const uint32_t *)(b + 80));
+        const float dsc = pm_h2f(dd & 0xffffu) * (float)(scb & 15u);
+        const float dmn = pm_h2f(dd >> 16) * (float)(scb >> 4);
+        const uint32_t *q = (const uint32_t *)(b + 16 + 32u * n + jj);
+        const uint32_t q0 = __ldg(q), q1 = __ldg(q + 1);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t byte = ((i < 4 ? q0 : q1) >> (8 * (i & 3))) & 0xffu;
+            v[i] = dsc * (float)((byte >> sft) & 3u) - dmn;
+        }
+    } else if constexpr (Q == PM_QUANT_IQ2_XXS) {
+        const uint8_t *b = row + (size_t)(c >> 2) * PM_IQ2_XXS_BYTES;
+        const uint32_t i0 = 64u * (c & 3u) + 8u * j, sb = i0 >> 5, g = (i0 & 31u) >> 3;
+        const uint16_t *h = (const uint16_t *)b;
+        const uint32_t aux0 = (uint32_t)__ldg(h + 1 + 4 * sb) | ((uint32_t)__ldg(h + 2 + 4 * sb) << 16);
+        const uint32_t aux1 = (uint32_t)__ldg(h + 3 + 4 * sb) | ((uint32_t)__ldg(h + 4 + 4 * sb) << 16);
+        const float dl = 0.125f * pm_h2f(__ldg(h)) * (float)(2u * (aux1 >> 28) + 1u);
+        const uint32_t grid = pm_kgrid_layer[(aux0 >> (8 * g)) & 0xffu];
+        const uint32_t signs = pm_ksigns_dev((aux1 >> (7 * g)) & 127u);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t dg = (grid >> (2 * i)) & 3u;
+            const float m = (float)(dg == 0 ? 8u : (dg == 1 ? 25u : 43u));
+            v[i] = dl * ((signs >> i) & 1u ? -m : m);
+        }
+    }
+}
+
 template <int Q, int HALF>
 __device__ __forceinline__ void pm_tc_weights(const uint8_t *row, uint32_t c, uint4 *oh, uint4 *ol) {
     if constexpr (Q == PM_QUANT_Q4_K) {
         pm_tc_q4k_row<HALF>(row, c, oh, ol);
-    } else { /* no tensor-core tiles are listed for other formats */
+    } else {
 #pragma unroll
-        for (int j = 0; j < 8; j++) oh[j] = ol[j] = make_uint4(0, 0, 0, 0);
+        for (uint32_t j = 0; j < 8; j++) {
+            if ((HALF == 1 && j >= 4) || (HALF == 2 && j < 4)) continue;
+            float v[8];
+            pm_tc_group<Q>(row, c, j, v);
+            uint32_t *hh = (uint32_t *)&oh[j], *ll = (uint32_t *)&ol[j];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pm_split2(v[2 * i], v[2 * i + 1], hh[i], ll[i]);
+        }
     }
 }
 
@@ -1072,7 +1144,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     static int occ_gu[64], occ_dn[64];
     static uint32_t sm_gu[64], sm_dn[64];
     const bool grid = QR == PM_QUANT_IQ2_XXS || QS == PM_QUANT_IQ2_XXS;
-    constexpr bool TC = QR == PM_QUANT_Q4_K || QS == PM_QUANT_Q4_K;
+    constexpr bool TC = true; /* every supported format has a tensor-core fill */
     const bool tc = TC && (a.tc_r || a.tc_s) && L.T >= PM_TC_MIN; /* an expert can reach the threshold */
     /* 4: gate/up -> tensor-core split-K sums, dp4a work units -> mid */
     if constexpr (TC)

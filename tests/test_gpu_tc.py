@@ -1,6 +1,6 @@
 """Large batches: experts with >= 128 tokens (and the shared expert) run on
 the tcgen05 tensor-core tiles (fp16 hi + lo split operands, fp32
-accumulation); the rest on the dp4a engine.  Outputs and mid rows must
+accumulation) in every supported block format; the rest on the dp4a engine.  Outputs and mid rows must
 match the CPU oracle within the expert-FFN tolerance."""
 import numpy as np
 import pytest
@@ -18,10 +18,14 @@ def _ws(ws, base, ptr, n, dt):
     return ws[off:off + n * np.dtype(dt).itemsize].view(dt)
 
 
-@pytest.mark.parametrize("shared", [None, (2, 512)])
-@pytest.mark.parametrize("T", [300, 512])
-def test_tensor_core_tiles(oracle, T, shared):
-    L = HostLayer(H=512, F=512, E=8, k=2, quant=2, seed=11, router_mode=0, zipf=(1.1, "select"), shared=shared)
+CASES = [  # (routed format, shared (format, F) or None, T)
+    (2, None, 300), (2, (2, 512), 300), (2, None, 512), (2, (2, 512), 512),
+    (0, None, 300), (1, None, 300), (10, None, 300), (12, None, 300), (1, (10, 512), 300)]
+
+
+@pytest.mark.parametrize("quant,shared,T", CASES, ids=[f"q{q}-sh{s}-T{t}" for q, s, t in CASES])
+def test_tensor_core_tiles(oracle, quant, shared, T):
+    L = HostLayer(H=512, F=512, E=8, k=2, quant=quant, seed=11, router_mode=0, zipf=(1.1, "select"), shared=shared)
     x = np.random.default_rng(5).normal(0, 1, (T, L.H)).astype(np.float32)
     _, sel, w = L.oracle_route(x)
     ref, ref_mid = L.oracle_ffn(x, sel, w, return_mid=True)
@@ -38,7 +42,7 @@ def test_tensor_core_tiles(oracle, T, shared):
     mid = _ws(ws, base, v.mid, T * ns * v.f_max, np.float32).reshape(T * ns, v.f_max)[:, :ref_mid.shape[-1]]
     rm = ref_mid.reshape(T * ns, -1)
     got = out.cpu().numpy()
-    print(T, shared is not None, "tiles", int(n[4]), "splits", int(n[5]), "out", rel_l2(got, ref),
+    print(quant, shared, T, "tiles", int(n[4]), "splits", int(n[5]), "out", rel_l2(got, ref),
           "mid", rel_l2(mid, rm))
     assert rel_l2(mid, rm) < TOL
     assert rel_l2(got, ref) < TOL
