@@ -191,7 +191,7 @@ class Runner:
             self.graph.replay()
 
 
-def launches_per_layer(T: int) -> int:
+def launches_per_layer(T: int) -> int:  # T: the tokens one layer call sees (all ranks under EP)
     """kernels one layer step launches: rms_norm, router (+ q8_K of x), selection, gate/up,
     down, combine, plus the three tensor-core kernels when an expert can reach 128 tokens"""
     return 6 + (3 if T >= 128 else 0)
@@ -468,7 +468,7 @@ def main():
                 "config": config,
                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
-                "gpu_launches": launches_per_layer(T) * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
+                "gpu_launches": launches_per_layer(T * world) * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
                 "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
     if line is not None:
         print(json.dumps(line), flush=True)
