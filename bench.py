@@ -191,10 +191,13 @@ class Runner:
             self.graph.replay()
 
 
-def launches_per_layer(T: int) -> int:  # T: the tokens one layer call sees (all ranks under EP)
-    """kernels one layer step launches: rms_norm, router (+ q8_K of x), selection, gate/up,
-    down, combine, plus the three tensor-core kernels when an expert can reach 128 tokens"""
-    return 6 + (3 if T >= 128 else 0)
+def launches_per_layer(T: int) -> int:
+    """kernels one layer step launches for a layer call over T tokens (all ranks' tokens under
+    expert parallelism): rms_norm, router (+ q8_K of x), selection, gate/up, down, combine, and
+    when an expert can reach 128 tokens the tensor-core passes - per pass (gate/up, down) the
+    token-image pack plus one expand + one gemm (the workloads here fit one expert wave) - and
+    the tensor-core mid kernel"""
+    return 6 + (7 if T >= 128 else 0)
 
 
 def max_over_ranks(ms: float, world: int) -> float:
@@ -335,6 +338,98 @@ def cpu_baseline(stack, T: int, x0: np.ndarray, threads: int, budget_s: float = 
     return T / step_s, done
 
 
+def measured_peak_tensor():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    return 1590.0, "fallback"
+
+
+def prefill_c3(args):
+    """C3 prefill: one layer of H 2880, 32 MXFP4 experts (softmax top-4, F 2880,
+    biases, swiglu_oai) at T = 2048 tokens, one GPU.  Every expert sees
+    about 256 tokens, so the routed FFN runs on the tcgen05 tiles.  The
+    roofline is the tensor pipe: algorithmic FLOPs 2 T k 3 H F + 2 T E H per
+    step over the step's CUDA-event time against the measured bf16 dense
+    peak; the tiles issue three fp16 MMAs per product (hi + lo operand
+    split), reported beside it as issued FLOPs."""
+    from pulsar_b200 import lib, make_layer
+    from pulsar_b200.configs import CONFIGS
+    lib()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and int(os.environ.get("RANK", "0")) != 0:
+        return
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    spec = CONFIGS["C3"]["spec"]
+    T, H, F, E, k = 2048, spec.n_embd, spec.n_ff, spec.n_expert, spec.n_used
+    L = make_layer(spec, seed=3000, device=dev)
+    ws = torch.zeros(L.workspace_bytes(T), dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev)
+    xs = []
+    for i in range(8):
+        g.manual_seed(3_000_000 + i)
+        xs.append(torch.randn((T, H), generator=g, device=dev))
+    x = torch.zeros((T, H), dtype=torch.float32, device=dev)
+    out = torch.zeros_like(x)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for _ in range(2):
+            L.forward(x, out, ws, stream=st)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        L.forward(x, out, ws, stream=st)
+    torch.cuda.synchronize()
+
+    def one(i, host=None, out_h=None):
+        with torch.cuda.stream(st):
+            x.copy_(host[i % len(host)] if host is not None else xs[i % len(xs)], non_blocking=True)
+            graph.replay()
+            if out_h is not None:
+                out_h.copy_(out, non_blocking=True)
+
+    def time_loop(**kw):
+        for i in range(args.warmup):
+            one(i, **kw)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(args.steps):
+            one(args.warmup + i, **kw)
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    with ClockSampler(dev.index) as clk:
+        ms = time_loop()
+    host = [t.cpu().pin_memory() for t in xs]
+    out_h = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    e2e_ms = time_loop(host=host, out_h=out_h)
+    v = L.ws_view(ws, T)
+    n = ws.view(torch.int32)[(v.n_items - ws.data_ptr()) // 4:(v.n_items - ws.data_ptr()) // 4 + 6].cpu().tolist()
+    flops = 2.0 * T * k * 3 * H * F + 2.0 * T * E * H
+    issued = 3 * 2.0 * T * k * 3 * H * F
+    peak, peak_kind = measured_peak_tensor()
+    ach = flops / (ms / 1e3) / 1e12
+    cfg = {"workload": "C3 prefill, one layer (BASELINE configs[2] shapes)", "n_embd": H, "n_ff": F,
+           "n_expert": E, "n_used": k, "quant": "MXFP4", "router": "softmax top-4, router + expert biases",
+           "act": "swiglu_oai", "tokens": T, "parallelism": "single",
+           "l2": "32 experts x 13.2 MB = 423 MB of weights per step exceed the 126 MB L2 (no flush)"}
+    print(json.dumps({
+        "metric": METRIC, "value": T / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 hi+lo split operands (tcgen05 kind::f16), f32 accumulate", "data": "synthetic (seeded)",
+        "config": cfg,
+        "e2e": {"value": T / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": (launches_per_layer(T) - 1) * args.steps, "clocks": clk.summary(),
+        "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                     "peak_kind": peak_kind, "traffic": None, "algorithmic_flops_per_step": flops,
+                     "issued_mma_flops_per_step": issued, "issued_tflops": issued / (ms / 1e3) / 1e12,
+                     "scope": "whole layer step (router, selection, tensor-core tiles, mid, combine)"},
+        "tc_tiles": n[4], "tc_splits": n[5], "cpu_baseline": None}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -346,7 +441,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel roofline leg")
     ap.add_argument("--all-batches", action="store_true", help="also time decode batches 1 and 8")
+    ap.add_argument("--workload", default="c2-decode", choices=["c2-decode", "c3-prefill"],
+                    help="c3-prefill: one C3 layer at T 2048 on the tensor-core path (a secondary line)")
     args = ap.parse_args()
+    if args.workload == "c3-prefill":
+        return prefill_c3(args)
     CFG["layers"] = args.layers
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -47,6 +47,36 @@ __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 
 #define PM_TC_N 64u  /* tokens per tensor-core tile (MMA N) */
 #define PM_TC_MIN 128u /* experts with at least this many tokens take the tensor-core path */
+#define PM_TC_G 4u                   /* tiles per MMA group */
+#define PM_TC_IMG 16384u             /* one 128 x 64 fp16 operand image */
+#define PM_TC_BIMG (PM_TC_N * 128u)  /* one 64-token x 64 fp16 image */
+#define PM_TC_XP 288u                /* raw row pitch of the expand kernel (>= 272 + 4, 16-byte multiple) */
+#define PM_TC_SCRATCH_CAP (4ull << 30) /* bound of the expanded-image region of the workspace */
+
+/* per item kind: operand rows, 128-row blocks, 64-wide K chunks, matrices */
+struct pm_tcgeo {
+    uint32_t rows, rt_n, nch, nm;
+};
+__host__ __device__ __forceinline__ pm_tcgeo pm_tc_geo(uint32_t H, uint32_t F, int nmat) {
+    pm_tcgeo g;
+    g.rows = nmat == 2 ? F : H;
+    g.rt_n = (g.rows + 127u) / 128u;
+    g.nch = (nmat == 2 ? H : F) / 64u;
+    g.nm = (uint32_t)nmat;
+    return g;
+}
+/* bytes of one expert's images (hi + lo) for a pass */
+__host__ __device__ __forceinline__ uint64_t pm_tc_img_bytes(uint32_t H, uint32_t F, int nmat) {
+    const pm_tcgeo g = pm_tc_geo(H, F, nmat);
+    return (uint64_t)g.nm * g.rt_n * g.nch * 2u * PM_TC_IMG;
+}
+/* bytes of 256 weights of a row (a super-block; 8 blocks of 32) */
+__host__ __device__ constexpr uint32_t pm_tc_sb_bytes(int q) {
+    return q == PM_QUANT_Q4_K ? PM_Q4_K_BYTES
+           : q == PM_QUANT_Q2_K ? PM_Q2_K_BYTES
+           : q == PM_QUANT_IQ2_XXS ? PM_IQ2_XXS_BYTES
+           : q == PM_QUANT_MXFP4 ? 8u * PM_MXFP4_BLOCK : 8u * PM_Q8_0_BLOCK;
+}
 
 /* formats with a tensor-core (fp16 dequant) path */
 static bool pm_tc_fmt(uint32_t q) {
@@ -71,12 +101,22 @@ static int pm_sm_count() {
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
     uint32_t max_work;
-    uint32_t max_tc, ks_max;
+    uint32_t max_tc, ks_max, tc_slots, tc_waves;
+    uint64_t tc_slot_bytes;
+    size_t tc_ord, tc_first, tcb, tcx;
     size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, tc_tile, pairs, mid,
         midq, tcp, partial, sel_done, err, total;
 };
 
 static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
+
+/* tensor-core path available for the routed / shared experts */
+static bool pm_tc_on_r(const pulsar_moe_layer_desc *d) {
+    return pm_tc_fmt(d->quant) && d->n_embd % 64 == 0 && d->n_ff % 64 == 0;
+}
+static bool pm_tc_on_s(const pulsar_moe_layer_desc *d) {
+    return d->n_shared && pm_tc_fmt(d->shared_quant) && d->n_embd % 64 == 0 && d->shared_n_ff % 64 == 0;
+}
 
 static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     pm_layout L;
@@ -110,6 +150,37 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     L.max_tc = (uint32_t)(routed / PM_TC_MIN + (routed + PM_TC_N - 1) / PM_TC_N + 1 +
                           (uint64_t)L.S * ((T + PM_TC_N - 1) / PM_TC_N));
     L.tc_tile = o, o = pm_al(o + (size_t)L.max_tc * 8);
+    L.tc_ord = o, o = pm_al(o + (size_t)L.max_tc * 4);
+    L.tc_first = o, o = pm_al(o + (size_t)L.max_tc * 4);
+    /* tensor-core operand images: token images of every tile, expanded
+     * weight images of up to tc_slots experts at a time */
+    {
+        const bool tr = pm_tc_on_r(d), ts = pm_tc_on_s(d);
+        const uint64_t n_r = tr ? (routed / PM_TC_MIN < L.E ? routed / PM_TC_MIN : L.E) : 0;
+        const uint64_t n_items = T >= PM_TC_MIN ? n_r + (ts ? L.S : 0u) : 0;
+        uint64_t sb = 0;
+        if (tr) sb = pm_tc_img_bytes(L.H, L.Fr, 2) > pm_tc_img_bytes(L.H, L.Fr, 1) ? pm_tc_img_bytes(L.H, L.Fr, 2)
+                                                                                     : pm_tc_img_bytes(L.H, L.Fr, 1);
+        if (ts) {
+            const uint64_t s2 = pm_tc_img_bytes(L.H, L.Fs, 2), s1 = pm_tc_img_bytes(L.H, L.Fs, 1);
+            sb = sb > s2 ? sb : s2;
+            sb = sb > s1 ? sb : s1;
+        }
+        L.tc_slot_bytes = sb;
+        L.tc_slots = L.tc_waves = 0;
+        size_t nb = 0, nx = 0;
+        if (n_items && sb) {
+            uint64_t ew = PM_TC_SCRATCH_CAP / sb;
+            ew = ew < 1 ? 1 : ew;
+            L.tc_slots = (uint32_t)(n_items < ew ? n_items : ew);
+            L.tc_waves = (uint32_t)((n_items + L.tc_slots - 1) / L.tc_slots);
+            const uint32_t kmax = L.H > L.Fmax ? L.H : L.Fmax;
+            nb = (size_t)(kmax / 64u) * 2u * L.max_tc * PM_TC_BIMG;
+            nx = (size_t)L.tc_slots * sb;
+        }
+        L.tcb = o, o = pm_al(o + nb);
+        L.tcx = o, o = pm_al(o + nx);
+    }
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
     L.midq = o, o = pm_al(o + (size_t)T * L.n_slot * L.fb * PM_Q8_K_BYTES);
@@ -142,11 +213,17 @@ struct pm_layer_args {
     float *w;
     pm_block_q8K *xq;
     uint32_t *n_items; /* [0] all items, [1] routed items, [2] work units, [3] routed work units,
-                        * [4] tensor-core tiles, [5] their gate/up K splits */
+                        * [4] tensor-core tiles, [5] their gate/up K splits, [6] tensor-core items */
     uint32_t *item_expert, *item_start, *pairs;
     uint32_t *work_item, *work_t0; /* work unit = (item, first token of its chunk of <= PM_TT) */
     uint4 *wd;      /* per work unit: expert id (E + s for shared s), first pair, token count */
     uint2 *tc_tile; /* tensor-core tiles: (item, first token) */
+    uint32_t *tc_ord;   /* per tile: dense ordinal of its item among the tensor-core items */
+    uint32_t *tc_first; /* per ordinal: the item's first tile */
+    uint8_t *tcb;       /* token images ((chunk * 2 + hl) * max_tc + tile) */
+    uint8_t *tcx;       /* expanded weight images of the current wave, tc_slot_bytes per item */
+    uint64_t tc_slot_bytes;
+    uint32_t tc_slots, max_tc;
     pm_block_q8K *midq; /* q8_K of the mid rows of tensor-core pairs */
     float *tcp;     /* [ks][pair][2][Fmax] split-K gate/up sums of tensor-core tiles */
     uint32_t ks_max, tc_r, tc_s, n_sm; /* split bound; tensor-core path on for routed / shared */
@@ -344,13 +421,50 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
         for (uint32_t j = threadIdx.x; j < sh_tiles; j += blockDim.x)
             a.tc_tile[tot_tc + s * sh_tiles + j] = make_uint2(item, j * PM_TC_N);
     }
+    /* tensor-core items: dense ordinals (expand slots) and MMA groups */
+    const uint32_t n_tc = tot_tc + n_sh * sh_tiles;
+    uint32_t n_ti = 0, n_grp = 0;
+    {
+        __shared__ uint32_t s_cnt[2][32];
+        __syncthreads(); /* tile writes of this block are visible */
+        const uint32_t nwarp = blockDim.x >> 5;
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < n_tc; c0 += blockDim.x) {
+            const uint32_t j = c0 + threadIdx.x;
+            const uint32_t ty = j < n_tc ? a.tc_tile[j].y : 1u;
+            const uint32_t bf = __ballot_sync(0xffffffffu, j < n_tc && ty == 0u);
+            const uint32_t bg = __ballot_sync(0xffffffffu, j < n_tc && ty % (PM_TC_G * PM_TC_N) == 0u);
+            if (lane == 0) {
+                s_cnt[0][wid] = __popc(bf);
+                s_cnt[1][wid] = __popc(bg);
+            }
+            __syncthreads();
+            uint32_t pre = n_ti, tf = 0, tg = 0;
+            for (uint32_t w2 = 0; w2 < nwarp; w2++) {
+                if (w2 < wid) pre += s_cnt[0][w2];
+                tf += s_cnt[0][w2];
+                tg += s_cnt[1][w2];
+            }
+            if (j < n_tc) {
+                const uint32_t ord = pre + __popc(bf & ((2u << lane) - 1u)) - 1u;
+                a.tc_ord[j] = ord;
+                if (ty == 0u) a.tc_first[ord] = j;
+            }
+            __syncthreads();
+            n_ti += tf;
+            n_grp += tg;
+        }
+    }
     if (threadIdx.x == 0) {
-        const uint32_t n_tc = tot_tc + n_sh * sh_tiles;
-        /* K splits of the tensor-core gate/up pass: about one unit per SM */
-        const uint32_t units = n_tc * ((a.Fmax + 127u) / 128u);
+        /* K splits of the tensor-core gate/up pass: about one unit per SM,
+         * and no split left without chunks */
+        const uint32_t units = n_grp * 2u * ((a.Fmax + 127u) / 128u);
         uint32_t ks = units ? (a.n_sm + units - 1) / units : 1u;
         const uint32_t ks_cap = a.ks_max < a.H / 64u ? a.ks_max : a.H / 64u;
         ks = ks < 1u ? 1u : (ks > ks_cap ? ks_cap : ks);
+        const uint32_t cps = (a.H / 64u + ks - 1) / ks;
+        ks = (a.H / 64u + cps - 1) / cps;
+        a.n_items[6] = n_ti;
         a.item_start[tot_items + n_sh] = tot_pairs + n_sh * a.T;
         a.n_items[0] = tot_items + n_sh;
         a.n_items[1] = tot_items;
@@ -645,41 +759,60 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
 
 /* ============================== 4b, 5b: tensor-core expert tiles */
 
-/* A tensor-core UNIT is (tile of <= PM_TC_N tokens of one expert, block of
- * 128 matrix rows, K split).  NMAT 2: gate and up rows (K = H) into two
- * accumulators, split-K sums to tcp.  NMAT 1: down rows (K = F) against the
- * q8_K mid rows, one partial row per pair.  Per 64-wide K chunk every
- * thread dequantizes operand rows to fp16 straight into a 128-byte-swizzled
- * stage (Q4_K weights: one (matrix, row) or one half row per thread; q8_K
- * tokens: 16 values per thread), then one thread issues the tcgen05 MMAs
- * (M 128, N PM_TC_N, K 16) and commits them to the stage's mbarrier, which
- * frees the stage pm_tcg::S chunks later.  Tensor memory holds NMAT x N fp32
- * columns for the CTA's lifetime. */
+/* Experts with >= PM_TC_MIN tokens (prefill, large batches) run on tcgen05
+ * in three kernels per pass (gate/up, then down):
+ *  - expand: every tensor-core expert's weights are dequantized ONCE per
+ *    layer call into fp16 hi + lo operand images (w = hi + lo to ~2^-22, the
+ *    exact f32 value of the block formula), each a 128-row x 64-K tile in the
+ *    128-byte-swizzled K-major layout the MMA descriptors read.  Raw rows are
+ *    staged through shared memory with coalesced 4-byte loads, 256 weights of
+ *    every row at a time.  The images of up to tc_slots experts live in the
+ *    workspace at once; more experts run in waves of that many.
+ *  - pack: the q8_K token rows of every tile (x for gate/up, q8_K(mid) for
+ *    down) become fp16 hi + lo images of 64 tokens x 64 K, stored so that
+ *    the consecutive tiles of one expert are adjacent: a group of up to
+ *    PM_TC_G tiles is one MMA operand of N = 64 x tiles (<= 256).
+ *  - gemm: a persistent warp-specialized kernel.  One thread streams the
+ *    images of each (group, matrix, 128-row block, K split) unit into a
+ *    two-stage shared-memory ring with 1-D bulk copies, one thread issues
+ *    the MMAs (w x = wh xh + wh xl + wl xh per K-16 slice, fp32 in tensor
+ *    memory), and four warps drain the accumulators (double-buffered in
+ *    tensor memory, so the next unit's MMAs overlap the epilogue) into the
+ *    split-K gate/up sums or the down partial rows. */
+
 /* 8 weights of a row, values 64 c + 8 j .. + 7, in f32 (exact products of
  * the block's integers and scales, as the dot functors use them: Q8_0 cu:2174,
  * MXFP4 cu:2053 doubled e2m1 x 2^(e-128), Q2_K cu:1625, IQ2_XXS cu:1582).
  * Rows of these formats are only 2- (Q8_0, IQ2_XXS), 4- (Q2_K) or 1-byte
- * (MXFP4) aligned, so the loads are of that width. */
-template <int Q>
+ * (MXFP4) aligned, so the loads are of that width.  RAW: `row` points into
+ * a shared-memory copy of the row's bytes (plain loads), else to global
+ * memory (read-only loads). */
+template <bool RAW, class T>
+__device__ __forceinline__ T pm_ldw(const T *p) {
+    if constexpr (RAW) return *p;
+    else return __ldg(p);
+}
+
+template <int Q, bool RAW>
 __device__ __forceinline__ void pm_tc_group(const uint8_t *row, uint32_t c, uint32_t j, float *v) {
     if constexpr (Q == PM_QUANT_Q8_0) {
         const uint8_t *b = row + (size_t)(2u * c + (j >> 2)) * PM_Q8_0_BLOCK;
-        const float d = pm_h2f(__ldg((const uint16_t *)b));
+        const float d = pm_h2f(pm_ldw<RAW>((const uint16_t *)b));
         const uint16_t *q = (const uint16_t *)(b + 2 + 8u * (j & 3u));
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const uint32_t w = __ldg(q + i);
+            const uint32_t w = pm_ldw<RAW>(q + i);
             v[2 * i] = d * (float)(int8_t)(w & 0xffu);
             v[2 * i + 1] = d * (float)(int8_t)(w >> 8);
         }
     } else if constexpr (Q == PM_QUANT_MXFP4) {
         const uint8_t *b = row + (size_t)(2u * c + (j >> 2)) * PM_MXFP4_BLOCK;
-        const float sc = pm_mxfp4_scale_half(__ldg(b));
+        const float sc = pm_mxfp4_scale_half(pm_ldw<RAW>(b));
         const uint32_t e0 = 8u * (j & 3u); /* element of the block: low nibbles 0-15, high 16-31 */
         const uint32_t sh = e0 < 16u ? 0u : 4u;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const uint32_t code = (__ldg(b + 1 + ((e0 + (uint32_t)i) & 15u)) >> sh) & 15u;
+            const uint32_t code = (pm_ldw<RAW>(b + 1 + ((e0 + (uint32_t)i) & 15u)) >> sh) & 15u;
             const uint32_t m = code & 7u;
             const float mag = (float)(m < 4u ? m : (m == 4u ? 4u : (m == 5u ? 6u : (m == 6u ? 8u : 12u))));
             v[i] = (code & 8u ? -mag : mag) * sc;
@@ -688,12 +821,12 @@ __device__ __forceinline__ void pm_tc_group(const uint8_t *row, uint32_t c, uint
         const uint8_t *b = row + (size_t)(c >> 2) * PM_Q2_K_BYTES;
         const uint32_t i0 = 64u * (c & 3u) + 8u * j; /* element in the super-block */
         const uint32_t n = i0 >> 7, sft = 2u * ((i0 & 127u) >> 5), jj = i0 & 31u;
-        const uint32_t scb = __ldg(b + (i0 >> 4));
-        const uint32_t dd = __ldg((const uint32_t *)(b + 80));
+        const uint32_t scb = pm_ldw<RAW>(b + (i0 >> 4));
+        const uint32_t dd = pm_ldw<RAW>((const uint32_t *)(b + 80));
         const float dsc = pm_h2f(dd & 0xffffu) * (float)(scb & 15u);
         const float dmn = pm_h2f(dd >> 16) * (float)(scb >> 4);
         const uint32_t *q = (const uint32_t *)(b + 16 + 32u * n + jj);
-        const uint32_t q0 = __ldg(q), q1 = __ldg(q + 1);
+        const uint32_t q0 = pm_ldw<RAW>(q), q1 = pm_ldw<RAW>(q + 1);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const uint32_t byte = ((i < 4 ? q0 : q1) >> (8 * (i & 3))) & 0xffu;
@@ -703,9 +836,9 @@ __device__ __forceinline__ void pm_tc_group(const uint8_t *row, uint32_t c, uint
         const uint8_t *b = row + (size_t)(c >> 2) * PM_IQ2_XXS_BYTES;
         const uint32_t i0 = 64u * (c & 3u) + 8u * j, sb = i0 >> 5, g = (i0 & 31u) >> 3;
         const uint16_t *h = (const uint16_t *)b;
-        const uint32_t aux0 = (uint32_t)__ldg(h + 1 + 4 * sb) | ((uint32_t)__ldg(h + 2 + 4 * sb) << 16);
-        const uint32_t aux1 = (uint32_t)__ldg(h + 3 + 4 * sb) | ((uint32_t)__ldg(h + 4 + 4 * sb) << 16);
-        const float dl = 0.125f * pm_h2f(__ldg(h)) * (float)(2u * (aux1 >> 28) + 1u);
+        const uint32_t aux0 = (uint32_t)pm_ldw<RAW>(h + 1 + 4 * sb) | ((uint32_t)pm_ldw<RAW>(h + 2 + 4 * sb) << 16);
+        const uint32_t aux1 = (uint32_t)pm_ldw<RAW>(h + 3 + 4 * sb) | ((uint32_t)pm_ldw<RAW>(h + 4 + 4 * sb) << 16);
+        const float dl = 0.125f * pm_h2f(pm_ldw<RAW>(h)) * (float)(2u * (aux1 >> 28) + 1u);
         const uint32_t grid = pm_kgrid_layer[(aux0 >> (8 * g)) & 0xffu];
         const uint32_t signs = pm_ksigns_dev((aux1 >> (7 * g)) & 127u);
 #pragma unroll
@@ -717,16 +850,16 @@ __device__ __forceinline__ void pm_tc_group(const uint8_t *row, uint32_t c, uint
     }
 }
 
-template <int Q, int HALF>
+template <int Q, int HALF, bool RAW>
 __device__ __forceinline__ void pm_tc_weights(const uint8_t *row, uint32_t c, uint4 *oh, uint4 *ol) {
     if constexpr (Q == PM_QUANT_Q4_K) {
-        pm_tc_q4k_row<HALF>(row, c, oh, ol);
+        pm_tc_q4k_row<HALF, RAW>(row, c, oh, ol);
     } else {
 #pragma unroll
         for (uint32_t j = 0; j < 8; j++) {
             if ((HALF == 1 && j >= 4) || (HALF == 2 && j < 4)) continue;
             float v[8];
-            pm_tc_group<Q>(row, c, j, v);
+            pm_tc_group<Q, RAW>(row, c, j, v);
             uint32_t *hh = (uint32_t *)&oh[j], *ll = (uint32_t *)&ol[j];
 #pragma unroll
             for (int i = 0; i < 4; i++) pm_split2(v[2 * i], v[2 * i + 1], hh[i], ll[i]);
@@ -734,193 +867,299 @@ __device__ __forceinline__ void pm_tc_weights(const uint8_t *row, uint32_t c, ui
     }
 }
 
-/* operand stages of the tensor-core kernels (fp16 hi + lo tiles) */
-template <int NMAT>
-struct pm_tcg {
-    static constexpr uint32_t N = PM_TC_N;
-    static constexpr uint32_t A = 128u * 128u;  /* one 128 x 64 fp16 tile */
-    static constexpr uint32_t B = N * 128u;     /* one N x 64 fp16 tile */
-    static constexpr uint32_t STAGE = NMAT * 2u * A + 2u * B;
-    static constexpr uint32_t S = NMAT == 2 ? 2u : 3u;
-    static constexpr uint32_t SMEM = 1024u + S * STAGE;
+/* Expand: block (slot, (matrix, 128-row block, 256-weight span)); thread r
+ * owns row 128 rt + r.  The span's raw bytes of all 128 rows are copied to
+ * shared memory (a warp per row at a time, 4-byte words from the word
+ * boundary below the span), then each thread writes the hi + lo images of
+ * the span's (up to) four 64-wide chunks of its row.  Rows past the end are
+ * written as zeros. */
+template <int Q, int NM>
+__device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_t *sraw, const uint8_t *mat,
+                                                  uint64_t rb, const pm_tcgeo &g, uint32_t K, uint32_t m,
+                                                  uint32_t rt, uint32_t sp, uint8_t *img) {
+    constexpr uint32_t SB = pm_tc_sb_bytes(Q);
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+    const uint64_t sb0 = (uint64_t)sp * SB;
+    const uint32_t bytes = rb - sb0 < SB ? (uint32_t)(rb - sb0) : SB;
+    for (uint32_t r = warp; r < 128u; r += 4u) {
+        const uint32_t grow = rt * 128u + r;
+        if (grow >= g.rows) continue;
+        const uintptr_t src = (uintptr_t)(mat + (uint64_t)grow * rb + sb0);
+        const uintptr_t a0 = src & ~(uintptr_t)3;
+        const uint32_t nw = (uint32_t)((src + bytes - a0 + 3u) >> 2);
+        for (uint32_t w = lane; w < nw; w += 32u)
+            *(uint32_t *)(sraw + r * PM_TC_XP + 4u * w) = __ldg((const uint32_t *)(a0 + 4u * w));
+    }
+    __syncthreads();
+    const uint32_t r = tid, grow = rt * 128u + r;
+    const uint32_t c_end = 4u * sp + 4u < g.nch ? 4u * sp + 4u : g.nch;
+    const uint8_t *rowp = nullptr;
+    if (grow < g.rows) {
+        const uint32_t mis = (uint32_t)((uintptr_t)(mat + (uint64_t)grow * rb + sb0) & 3u);
+        rowp = sraw + r * PM_TC_XP + mis - sb0;
+    }
+    (void)K;
+    for (uint32_t c = 4u * sp; c < c_end; c++) {
+        uint4 vh[8], vl[8];
+        if (rowp) {
+            pm_tc_weights<Q, 0, true>(rowp, c, vh, vl);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) vh[j] = vl[j] = make_uint4(0, 0, 0, 0);
+        }
+        uint8_t *ih = img + (((uint64_t)(m * g.rt_n + rt) * g.nch + c) * 2u) * PM_TC_IMG + (r >> 3) * 1024u +
+                      (r & 7u) * 128u;
+#pragma unroll
+        for (uint32_t j = 0; j < 8; j++) {
+            const uint32_t off = (j ^ (r & 7u)) << 4;
+            *(uint4 *)(ih + off) = vh[j];
+            *(uint4 *)(ih + PM_TC_IMG + off) = vl[j];
+        }
+    }
+}
+
+template <int QR, int QS, int NM>
+__global__ void __launch_bounds__(128) pm_tc_expand_kernel(const __grid_constant__ pm_layer_args a, uint32_t wave) {
+    __shared__ __align__(16) uint8_t sraw[128u * PM_TC_XP];
+    const uint32_t o = wave * a.tc_slots + blockIdx.y;
+    if (blockIdx.y >= a.tc_slots || o >= __ldcg(a.n_items + 6)) return;
+    const uint32_t item = __ldcg(&a.tc_tile[__ldcg(a.tc_first + o)].x);
+    const uint32_t e = __ldcg(a.item_expert + item);
+    const bool routed = e < a.E;
+    const uint32_t F = routed ? a.Fr : a.Fs;
+    const pm_tcgeo g = pm_tc_geo(a.H, F, NM);
+    const uint32_t K = NM == 2 ? a.H : F, nsp = (K + 255u) / 256u;
+    const uint32_t bx = blockIdx.x;
+    if (bx >= g.nm * g.rt_n * nsp) return;
+    const uint32_t sp = bx % nsp, rt = (bx / nsp) % g.rt_n, m = bx / (nsp * g.rt_n);
+    const uint8_t *mat;
+    uint64_t rb;
+    if (NM == 2) {
+        mat = m == 0 ? (routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate)
+                     : (routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup);
+        rb = routed ? a.rb_gu_r : a.rb_gu_s;
+    } else {
+        mat = routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown;
+        rb = routed ? a.rb_dn_r : a.rb_dn_s;
+    }
+    uint8_t *img = a.tcx + (uint64_t)(o - wave * a.tc_slots) * a.tc_slot_bytes;
+    if (routed)
+        pm_tc_expand_span<QR, NM>(a, sraw, mat, rb, g, K, m, rt, sp, img);
+    else
+        pm_tc_expand_span<QS, NM>(a, sraw, mat, rb, g, K, m, rt, sp, img);
+}
+
+/* Pack: block (64-wide K chunk, tile); thread (token tok = tid / 4, quarter
+ * q = tid % 4) converts 16 q8_K values to fp16 hi + lo.  Image (chunk c,
+ * part hl, tile j) sits at ((c * 2 + hl) * max_tc + j) * PM_TC_BIMG. */
+template <int NM>
+__global__ void __launch_bounds__(256) pm_tc_pack_kernel(const __grid_constant__ pm_layer_args a) {
+    const uint32_t tile = blockIdx.y, c = blockIdx.x;
+    if (tile >= __ldcg(a.n_items + 4)) return;
+    const uint2 tt = __ldcg(a.tc_tile + tile);
+    const uint32_t item = tt.x, t0 = tt.y, e = __ldcg(a.item_expert + item);
+    const uint32_t s0 = __ldcg(a.item_start + item), cnt = __ldcg(a.item_start + item + 1) - s0;
+    const uint32_t nt = cnt - t0 < PM_TC_N ? cnt - t0 : PM_TC_N;
+    const uint32_t K = NM == 2 ? a.H : (e < a.E ? a.Fr : a.Fs);
+    if (c * 64u >= K) return;
+    const uint32_t tok = threadIdx.x >> 2, bq = threadIdx.x & 3u;
+    uint4 vh[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, vl[2] = {vh[0], vh[1]};
+    if (tok < nt) {
+        const uint32_t p = __ldcg(a.pairs + s0 + t0 + tok);
+        const pm_block_q8K *src = NM == 2 ? a.xq + (uint64_t)(p / a.n_slot) * a.hb : a.midq + (uint64_t)p * a.fb;
+        pm_tc_q8_16(src, 64u * c + 16u * bq, vh, vl);
+    }
+    uint8_t *bh = a.tcb + ((uint64_t)(c * 2u) * a.max_tc + tile) * PM_TC_BIMG + (tok >> 3) * 1024u + (tok & 7u) * 128u;
+    uint8_t *bl = bh + (uint64_t)a.max_tc * PM_TC_BIMG;
+#pragma unroll
+    for (uint32_t j = 0; j < 2; j++) {
+        const uint32_t off = ((2u * bq + j) ^ (tok & 7u)) << 4;
+        *(uint4 *)(bh + off) = vh[j];
+        *(uint4 *)(bl + off) = vl[j];
+    }
+}
+
+/* one gemm unit: (group of tiles, matrix, 128-row block, K split) */
+struct pm_tcu {
+    uint32_t tile, item, s0, t0, ng, ntile, m, rt, ks, c0, c1, rows, rt_n, nch, slot;
 };
 
-template <int QR, int QS, int NMAT>
-__global__ void __launch_bounds__(PM_THREADS, 1) pm_tc_kernel(const __grid_constant__ pm_layer_args a) {
+template <int NM>
+__device__ __forceinline__ bool pm_tc_unit(const pm_layer_args &a, uint32_t u, uint32_t wave, uint32_t rt_max,
+                                           uint32_t KS, pm_tcu &x) {
+    const uint32_t per = NM * rt_max * KS;
+    x.tile = u / per;
+    const uint32_t rem = u % per;
+    x.m = rem / (rt_max * KS);
+    x.rt = (rem % (rt_max * KS)) / KS;
+    x.ks = rem % KS;
+    const uint2 tt = __ldcg(a.tc_tile + x.tile);
+    if (tt.y % (PM_TC_G * PM_TC_N)) return false; /* not the first tile of a group */
+    const uint32_t ord = __ldcg(a.tc_ord + x.tile);
+    if (ord / a.tc_slots != wave) return false;
+    x.slot = ord % a.tc_slots;
+    x.item = tt.x;
+    x.t0 = tt.y;
+    const uint32_t e = __ldcg(a.item_expert + x.item);
+    x.s0 = __ldcg(a.item_start + x.item);
+    const uint32_t cnt = __ldcg(a.item_start + x.item + 1) - x.s0;
+    x.ng = cnt - x.t0 < PM_TC_G * PM_TC_N ? cnt - x.t0 : PM_TC_G * PM_TC_N;
+    x.ntile = (x.ng + PM_TC_N - 1) / PM_TC_N;
+    const pm_tcgeo g = pm_tc_geo(a.H, e < a.E ? a.Fr : a.Fs, NM);
+    if (x.rt >= g.rt_n) return false;
+    x.rows = g.rows, x.rt_n = g.rt_n, x.nch = g.nch;
+    const uint32_t cps = (g.nch + KS - 1) / KS;
+    x.c0 = x.ks * cps;
+    x.c1 = x.c0 + cps < g.nch ? x.c0 + cps : g.nch;
+    return x.c0 < x.c1;
+}
+
+#define PM_TCG_S 2u
+#define PM_TCG_BMAX (PM_TC_G * PM_TC_BIMG)               /* one token operand (hi or lo) of a group */
+#define PM_TCG_STAGE (2u * PM_TC_IMG + 2u * PM_TCG_BMAX) /* A hi, A lo, B hi, B lo */
+#define PM_TCG_SMEM (1024u + PM_TCG_S * PM_TCG_STAGE)
+#define PM_TCG_COLS 512u /* two accumulator buffers of up to 256 columns */
+
+template <int NM>
+__global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constant__ pm_layer_args a, uint32_t wave) {
     extern __shared__ uint8_t smem_raw[];
-    using G = pm_tcg<NMAT>;
-    constexpr uint32_t N = G::N, S = G::S, A_BYTES = G::A, B_BYTES = G::B, STAGE = G::STAGE;
-    __shared__ uint64_t empty[S], done;
+    constexpr uint32_t S = PM_TCG_S;
+    __shared__ uint64_t full[S], empty[S], accf[2], acce[2], fin;
     __shared__ uint32_t tslot;
-    __shared__ uint32_t s_pair[N];
-    __shared__ const pm_block_q8K *s_src[N];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023u) & ~(uintptr_t)1023u);
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t n_tiles = __ldcg(a.n_items + 4);
-    const uint32_t KS = NMAT == 2 ? __ldcg(a.n_items + 5) : 1u;
-    const uint32_t rt_n = ((NMAT == 2 ? a.Fmax : a.H) + 127u) / 128u;
-    const uint32_t units = n_tiles * rt_n * KS;
+    const uint32_t KS = NM == 2 ? __ldcg(a.n_items + 5) : 1u;
+    const uint32_t rt_max = ((NM == 2 ? a.Fmax : a.H) + 127u) / 128u;
+    const uint32_t units = n_tiles * NM * rt_max * KS;
     if (blockIdx.x >= units) return;
-    if (warp == 0) pm_tmem_alloc(&tslot, NMAT * N);
+    if (warp == 0) pm_tmem_alloc(&tslot, PM_TCG_COLS);
     if (tid == 0) {
-        for (uint32_t i = 0; i < S; i++) pm_mbar_init(&empty[i], 1);
-        pm_mbar_init(&done, 1);
+        for (uint32_t i = 0; i < S; i++) {
+            pm_mbar_init(&full[i], 1);
+            pm_mbar_init(&empty[i], 1);
+        }
+        for (uint32_t i = 0; i < 2; i++) {
+            pm_mbar_init(&accf[i], 1);
+            pm_mbar_init(&acce[i], 4);
+        }
+        pm_mbar_init(&fin, 1);
         pm_fence_barrier_init();
     }
     pm_tc_fence_before();
     __syncthreads();
     pm_tc_fence_after();
     const uint32_t tmem = tslot;
-    const uint32_t idesc = pm_idesc_f16(128, N);
-    uint32_t it = 0, nu = 0;
-    bool ok = true;
-    for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const uint32_t tile = u / (rt_n * KS), rem = u % (rt_n * KS), rt = rem / KS, ks = rem % KS;
-        const uint2 tt = __ldcg(a.tc_tile + tile);
-        const uint32_t item = tt.x, t0 = tt.y, e = __ldcg(a.item_expert + item);
-        const uint32_t s0 = __ldcg(a.item_start + item), cnt = __ldcg(a.item_start + item + 1) - s0;
-        const uint32_t nt = cnt - t0 < N ? cnt - t0 : N;
-        const bool routed = e < a.E;
-        const uint32_t rows = NMAT == 2 ? (routed ? a.Fr : a.Fs) : a.H;
-        const uint32_t K = NMAT == 2 ? a.H : (routed ? a.Fr : a.Fs);
-        const uint32_t nch = K / 64u, cps = (nch + KS - 1) / KS;
-        const uint32_t c0 = ks * cps, c1 = c0 + cps < nch ? c0 + cps : nch;
-        if (rt * 128u >= rows || c0 >= c1) continue; /* uniform over the CTA */
-        const uint64_t rb = NMAT == 2 ? (routed ? a.rb_gu_r : a.rb_gu_s) : (routed ? a.rb_dn_r : a.rb_dn_s);
-        const uint8_t *mat[2];
-        if (NMAT == 2) {
-            mat[0] = routed ? a.gate + (uint64_t)e * a.st_gu_r : a.sgate;
-            mat[1] = routed ? a.up + (uint64_t)e * a.st_gu_r : a.sup;
-        } else {
-            mat[0] = routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown;
-            mat[1] = nullptr;
-        }
-        if (tid < N) {
-            const uint32_t p = tid < nt ? __ldcg(a.pairs + s0 + t0 + tid) : 0u;
-            s_pair[tid] = p;
-            s_src[tid] = tid >= nt ? nullptr
-                         : NMAT == 2 ? a.xq + (uint64_t)(p / a.n_slot) * a.hb
-                                     : a.midq + (uint64_t)p * a.fb;
-        }
-        __syncthreads();
-        /* this thread's operand rows: (matrix, row) for gate/up, (row, half) for down */
-        const uint32_t r = tid & 127u, hsel = tid >> 7;
-        const uint32_t grow = rt * 128u + r;
-        const uint8_t *wrow = grow < rows ? mat[NMAT == 2 ? hsel : 0] + (uint64_t)grow * rb : nullptr;
-        const uint32_t btok = tid >> 2, bq = tid & 3u;
-        for (uint32_t c = c0; c < c1; c++, it++) {
-            const uint32_t st = it % S;
-            /* the stage's previous MMAs are done (bounded wait; its outcome is
-             * made uniform by the barrier below) */
-            const bool got = it < S || pm_mbar_wait(&empty[st], ((it / S) + 1u) & 1u, a.err);
-            uint8_t *stage = sm + st * STAGE;
-            /* A: weights, hi tiles then lo tiles */
-            {
-                uint4 vh[8], vl[8];
-                if (wrow) {
-                    if (NMAT == 2) {
-                        if (routed) pm_tc_weights<QR, 0>(wrow, c, vh, vl); else pm_tc_weights<QS, 0>(wrow, c, vh, vl);
-                    } else if (hsel == 0) {
-                        if (routed) pm_tc_weights<QR, 1>(wrow, c, vh, vl); else pm_tc_weights<QS, 1>(wrow, c, vh, vl);
-                    } else {
-                        if (routed) pm_tc_weights<QR, 2>(wrow, c, vh, vl); else pm_tc_weights<QS, 2>(wrow, c, vh, vl);
+    const uint64_t NP = (uint64_t)a.T * a.n_slot;
+    if (warp == 0) {
+        if (lane == 0) { /* producer */
+            uint32_t it = 0;
+            pm_tcu x;
+            for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
+                if (!pm_tc_unit<NM>(a, u, wave, rt_max, KS, x)) continue;
+                const uint8_t *ab = a.tcx + (uint64_t)x.slot * a.tc_slot_bytes +
+                                    ((uint64_t)(x.m * x.rt_n + x.rt) * x.nch) * 2u * PM_TC_IMG;
+                const uint32_t bb = x.ntile * PM_TC_BIMG;
+                bool ok = true;
+                for (uint32_t c = x.c0; c < x.c1; c++, it++) {
+                    const uint32_t st = it % S;
+                    if (it >= S && !pm_mbar_wait(&empty[st], ((it / S) + 1u) & 1u, a.err)) {
+                        ok = false;
+                        break;
                     }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; j++) vh[j] = vl[j] = make_uint4(0, 0, 0, 0);
+                    uint8_t *stage = sm + st * PM_TCG_STAGE;
+                    const uint8_t *bsrc = a.tcb + ((uint64_t)(c * 2u) * a.max_tc + x.tile) * PM_TC_BIMG;
+                    pm_mbar_expect_tx(&full[st], 2u * PM_TC_IMG + 2u * bb);
+                    pm_bulk_g2s(stage, ab + (uint64_t)c * 2u * PM_TC_IMG, 2u * PM_TC_IMG, &full[st]);
+                    pm_bulk_g2s(stage + 2u * PM_TC_IMG, bsrc, bb, &full[st]);
+                    pm_bulk_g2s(stage + 2u * PM_TC_IMG + PM_TCG_BMAX, bsrc + (uint64_t)a.max_tc * PM_TC_BIMG, bb,
+                                &full[st]);
                 }
-                const uint32_t m = NMAT == 2 ? hsel : 0u;
-                uint8_t *ah = stage + m * A_BYTES + (r >> 3) * 1024u + (r & 7u) * 128u;
-                uint8_t *al = ah + NMAT * A_BYTES;
-#pragma unroll
-                for (uint32_t j = 0; j < 8; j++) {
-                    if (NMAT == 1 && (j >> 2) != hsel) continue; /* down: this thread's half row */
-                    const uint32_t off = (j ^ (r & 7u)) << 4;
-                    *(uint4 *)(ah + off) = vh[j];
-                    *(uint4 *)(al + off) = vl[j];
-                }
+                if (!ok) break;
             }
-            /* B: token activations (q8_K -> f32 -> fp16 hi + lo), 16 values per thread */
-            {
-                uint4 vh[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)}, vl[2] = {vh[0], vh[1]};
-                const pm_block_q8K *src = s_src[btok];
-                if (src) pm_tc_q8_16(src, 64u * c + 16u * bq, vh, vl);
-                uint8_t *bh = stage + 2u * NMAT * A_BYTES + (btok >> 3) * 1024u + (btok & 7u) * 128u;
-#pragma unroll
-                for (uint32_t j = 0; j < 2; j++) {
-                    const uint32_t off = ((2u * bq + j) ^ (btok & 7u)) << 4;
-                    *(uint4 *)(bh + off) = vh[j];
-                    *(uint4 *)(bh + B_BYTES + off) = vl[j];
-                }
-            }
-            pm_fence_proxy_async();
-            if (!__syncthreads_and(got)) {
-                ok = false;
-                break;
-            }
-            if (tid == 0) {
+            /* the copies still in flight land before the CTA leaves */
+            for (uint32_t d = it > S ? it - S : 0u; d < it; d++) pm_mbar_wait(&full[d % S], (d / S) & 1u, nullptr);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) { /* MMA issue */
+            uint32_t it = 0, nu = 0;
+            pm_tcu x;
+            bool ok = true;
+            for (uint32_t u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                if (!pm_tc_unit<NM>(a, u, wave, rt_max, KS, x)) continue;
+                const uint32_t b = nu & 1u;
+                if (nu >= 2 && !pm_mbar_wait(&acce[b], ((nu / 2u) + 1u) & 1u, a.err)) break;
                 pm_tc_fence_after();
-                const uint64_t bh = pm_desc_sw128(stage + 2u * NMAT * A_BYTES);
-                const uint64_t bl = pm_desc_sw128(stage + 2u * NMAT * A_BYTES + B_BYTES);
-#pragma unroll
-                for (uint32_t m = 0; m < NMAT; m++) {
-                    const uint64_t ah = pm_desc_sw128(stage + m * A_BYTES);
-                    const uint64_t al = pm_desc_sw128(stage + (NMAT + m) * A_BYTES);
+                const uint32_t idesc = pm_idesc_f16(128, x.ntile * PM_TC_N);
+                const uint32_t d = tmem + b * 256u;
+                for (uint32_t c = x.c0; c < x.c1; c++, it++) {
+                    const uint32_t st = it % S;
+                    if (!pm_mbar_wait(&full[st], (it / S) & 1u, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    pm_tc_fence_after();
+                    uint8_t *stage = sm + st * PM_TCG_STAGE;
+                    const uint64_t ah = pm_desc_sw128(stage), al = pm_desc_sw128(stage + PM_TC_IMG);
+                    const uint64_t bh = pm_desc_sw128(stage + 2u * PM_TC_IMG);
+                    const uint64_t bl = pm_desc_sw128(stage + 2u * PM_TC_IMG + PM_TCG_BMAX);
 #pragma unroll
                     for (uint32_t kk = 0; kk < 4; kk++) {
                         /* w x = wh xh + wh xl + wl xh (+ wl xl, below fp32 rounding) */
-                        pm_mma_f16(tmem + m * N, ah + 2 * kk, bh + 2 * kk, idesc, (c > c0 || kk > 0) ? 1u : 0u);
-                        pm_mma_f16(tmem + m * N, ah + 2 * kk, bl + 2 * kk, idesc, 1u);
-                        pm_mma_f16(tmem + m * N, al + 2 * kk, bh + 2 * kk, idesc, 1u);
+                        pm_mma_f16(d, ah + 2 * kk, bh + 2 * kk, idesc, (c > x.c0 || kk > 0) ? 1u : 0u);
+                        pm_mma_f16(d, ah + 2 * kk, bl + 2 * kk, idesc, 1u);
+                        pm_mma_f16(d, al + 2 * kk, bh + 2 * kk, idesc, 1u);
                     }
+                    pm_mma_commit(&empty[st]);
                 }
-                pm_mma_commit(&empty[st]);
+                if (!ok) break;
+                pm_mma_commit(&accf[b]);
+                nu++;
             }
+            /* every MMA issued has completed before tensor memory is released */
+            pm_mma_commit(&fin);
+            pm_mbar_wait(&fin, 0, a.err);
         }
-        if (!ok) break;
-        /* ---- epilogue: accumulators -> global ---- */
-        if (tid == 0) pm_mma_commit(&done);
-        if (!__syncthreads_and(pm_mbar_wait(&done, nu & 1u, a.err))) {
-            ok = false;
-            break;
-        }
-        nu++;
-        pm_tc_fence_after();
-        {
-            const uint32_t lq = warp & 3u, ch = warp >> 2; /* lanes 32 lq.., tokens 32 ch.. */
-            const uint32_t row = rt * 128u + lq * 32u + lane;
+    } else { /* epilogue: warps 2-5 read tensor-memory lanes 32 (warp % 4) .. + 31 */
+        const uint32_t lq = warp & 3u;
+        uint32_t nu = 0;
+        pm_tcu x;
+        for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
+            if (!pm_tc_unit<NM>(a, u, wave, rt_max, KS, x)) continue;
+            const uint32_t b = nu & 1u;
+            if (!pm_mbar_wait(&accf[b], (nu / 2u) & 1u, a.err)) break;
+            pm_tc_fence_after();
+            const uint32_t row = x.rt * 128u + lq * 32u + lane;
+            for (uint32_t h = 0; h < x.ntile * (PM_TC_N / 16u); h++) {
+                float v[16];
+                pm_tmem_ld16(tmem + ((lq * 32u) << 16) + b * 256u + h * 16u, v);
+                if (row < x.rows) {
 #pragma unroll
-            for (uint32_t m = 0; m < NMAT; m++) {
-#pragma unroll
-                for (uint32_t h = 0; h < 2; h++) {
-                    float v[16];
-                    const uint32_t col = m * N + ch * 32u + h * 16u;
-                    pm_tmem_ld16(tmem + ((lq * 32u) << 16) + col, v);
-                    if (row < rows) {
-#pragma unroll
-                        for (uint32_t i = 0; i < 16; i++) {
-                            const uint32_t t = ch * 32u + h * 16u + i;
-                            if (t < nt) {
-                                const uint32_t p = s_pair[t];
-                                if (NMAT == 2)
-                                    a.tcp[(((uint64_t)ks * a.T * a.n_slot + p) * 2u + m) * a.Fmax + row] = v[i];
-                                else
-                                    a.partial[(uint64_t)p * a.H + row] = v[i];
-                            }
+                    for (uint32_t i = 0; i < 16; i++) {
+                        const uint32_t t = h * 16u + i;
+                        if (t < x.ng) {
+                            const uint32_t p = __ldcg(a.pairs + x.s0 + x.t0 + t);
+                            if (NM == 2)
+                                a.tcp[((x.ks * NP + p) * 2u + x.m) * a.Fmax + row] = v[i];
+                            else
+                                a.partial[(uint64_t)p * a.H + row] = v[i];
                         }
                     }
                 }
             }
+            pm_tc_fence_before();
+            __syncwarp();
+            if (lane == 0) pm_mbar_arrive(&acce[b]);
+            nu++;
         }
-        pm_tc_fence_before();
-        __syncthreads();
     }
-    /* every issued MMA completed (each unit waits for `done`), except after a
-     * wait that timed out; release tensor memory in all cases */
     pm_tc_fence_before();
     __syncthreads();
     pm_tc_fence_after();
-    if (warp == 0) pm_tmem_free(tmem, NMAT * N);
+    if (warp == 0) {
+        __syncwarp();
+        pm_tmem_free(tmem, PM_TCG_COLS);
+    }
 }
 
 /* mid rows of tensor-core pairs: the K-split gate/up sums (fixed order),
@@ -1124,18 +1363,29 @@ static inline void pm_ev(void *const *ev, int i, cudaStream_t st) {
     if (ev && ev[i]) cudaEventRecord((cudaEvent_t)ev[i], st);
 }
 
-template <int QR, int QS, int NMAT>
-static int pm_tc_launch(const pm_layer_args &a, cudaStream_t st) {
+/* one tensor-core pass: token images, then per wave the expanded weight
+ * images and the MMA units of that wave's items */
+template <int QR, int QS, int NM>
+static int pm_tc_launch(const pm_layer_args &a, const pm_layout &L, cudaStream_t st) {
     static uint64_t done = 0;
     static int occ[64];
     static uint32_t occ_smem[64];
-    const uint32_t smem = pm_tcg<NMAT>::SMEM;
-    auto k = pm_tc_kernel<QR, QS, NMAT>;
-    if (!pm_smem_attr(k, smem, &done)) return 0;
-    const uint32_t g = pm_sk_grid(k, smem, occ, occ_smem);
+    const uint32_t kmax = NM == 2 ? L.H : L.Fmax;
+    pm_tc_pack_kernel<NM><<<dim3(kmax / 64u, L.max_tc), 256, 0, st>>>(a);
+    if (!pm_ok(cudaGetLastError(), "moe layer tensor-core pack launch")) return 0;
+    const uint32_t nx = NM == 2 ? 2u * ((L.Fmax + 127u) / 128u) * ((L.H + 255u) / 256u)
+                                : ((L.H + 127u) / 128u) * ((L.Fmax + 255u) / 256u);
+    auto kg = pm_tc_gemm_kernel<NM>;
+    if (!pm_smem_attr(kg, PM_TCG_SMEM, &done)) return 0;
+    const uint32_t g = pm_sk_grid(kg, PM_TCG_SMEM, occ, occ_smem, 192u);
     if (!g) return 0;
-    k<<<g, PM_THREADS, smem, st>>>(a);
-    return pm_ok(cudaGetLastError(), "moe layer tensor-core launch");
+    for (uint32_t w = 0; w < L.tc_waves; w++) {
+        pm_tc_expand_kernel<QR, QS, NM><<<dim3(nx, L.tc_slots), 128, 0, st>>>(a, w);
+        if (!pm_ok(cudaGetLastError(), "moe layer tensor-core expand launch")) return 0;
+        kg<<<g, 192, PM_TCG_SMEM, st>>>(a, w);
+        if (!pm_ok(cudaGetLastError(), "moe layer tensor-core gemm launch")) return 0;
+    }
+    return 1;
 }
 
 template <int QR, int QS>
@@ -1148,7 +1398,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     const bool tc = TC && (a.tc_r || a.tc_s) && L.T >= PM_TC_MIN; /* an expert can reach the threshold */
     /* 4: gate/up -> tensor-core split-K sums, dp4a work units -> mid */
     if constexpr (TC)
-        if (tc && !pm_tc_launch<QR, QS, 2>(a, st)) return 0;
+        if (tc && !pm_tc_launch<QR, QS, 2>(a, L, st)) return 0;
     const pm_skind gr = pm_kind_for(2, a.rb_gu_r, a.H);
     const pm_skp pg = pm_skp_for(2, gr, a.S ? pm_kind_for(2, a.rb_gu_s, a.H) : gr, grid);
     auto kgu = pm_layer_sk_kernel<QR, QS, 2, 0>;
@@ -1165,7 +1415,7 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     pm_ev(ev, 4, st);
     /* 5: down -> partial rows */
     if constexpr (TC)
-        if (tc && !pm_tc_launch<QR, QS, 1>(a, st)) return 0;
+        if (tc && !pm_tc_launch<QR, QS, 1>(a, L, st)) return 0;
     const pm_skind dr = pm_kind_for(1, a.rb_dn_r, a.Fr);
     const pm_skp pd = pm_skp_for(1, dr, a.S ? pm_kind_for(1, a.rb_dn_s, a.Fs) : dr, grid);
     auto kdn = pm_layer_sk_kernel<QR, QS, 1, 1>;
@@ -1241,11 +1491,18 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.wd = (uint4 *)(b + L.wd);
     a.sk_c = (uint32_t *)(b + L.sk_c);
     a.tc_tile = (uint2 *)(b + L.tc_tile);
+    a.tc_ord = (uint32_t *)(b + L.tc_ord);
+    a.tc_first = (uint32_t *)(b + L.tc_first);
+    a.tcb = b + L.tcb;
+    a.tcx = b + L.tcx;
+    a.tc_slot_bytes = L.tc_slot_bytes;
+    a.tc_slots = L.tc_slots;
+    a.max_tc = L.max_tc;
     a.midq = (pm_block_q8K *)(b + L.midq);
     a.tcp = (float *)(b + L.tcp);
     a.ks_max = L.ks_max;
-    a.tc_r = pm_tc_fmt(d->quant) && L.H % 64 == 0 && L.Fr % 64 == 0;
-    a.tc_s = L.S && pm_tc_fmt(d->shared_quant) && L.H % 64 == 0 && L.Fs % 64 == 0;
+    a.tc_r = pm_tc_on_r(d);
+    a.tc_s = pm_tc_on_s(d);
     a.n_sm = (uint32_t)pm_sm_count();
     a.mid = (float *)(b + L.mid);
     a.partial = (float *)(b + L.partial);

@@ -47,6 +47,11 @@ __device__ __forceinline__ void pm_mbar_expect_tx(uint64_t *bar, uint32_t bytes)
                  : "memory");
 }
 
+/* plain arrive (count 1) */
+__device__ __forceinline__ void pm_mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pm_smem_addr(bar)) : "memory");
+}
+
 /* 1-D bulk copy global -> shared, completion counted on bar.
  * dst, src 16-byte aligned; bytes a multiple of 16. */
 __device__ __forceinline__ void pm_bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

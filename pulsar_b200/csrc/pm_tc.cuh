@@ -131,12 +131,12 @@ __device__ __forceinline__ void pm_split2(float v0, float v1, uint32_t &hi, uint
  * ol[j] hold values 8 j .. 8 j + 7 (j 0-3: first sub-block, 4-7: second).
  * Nibbles become exact fp16 integers through the exponent trick
  * (0x6400 | n = 1024 + n).  HALF: 0 both sub-blocks, 1 first only, 2
- * second only. */
-template <int HALF>
+ * second only.  RAW: `row` is a 16-byte aligned shared-memory copy. */
+template <int HALF, bool RAW = false>
 __device__ __forceinline__ void pm_tc_q4k_row(const uint8_t *row, uint32_t c, uint4 *oh, uint4 *ol) {
     const uint8_t *b = row + (c >> 2) * PM_Q4_K_BYTES;
     const uint32_t sp = c & 3u;
-    const uint4 h = __ldg((const uint4 *)b);
+    const uint4 h = RAW ? *(const uint4 *)b : __ldg((const uint4 *)b);
     const uint32_t sh = 16u * (sp & 1u);
     const uint32_t ea = (h.y >> sh) & 0xffffu, eb = (h.z >> sh) & 0xffffu, ec = (h.w >> sh) & 0xffffu;
     const uint32_t sv = sp < 2 ? (ea & 0x3f3fu) : ((ec & 0x0f0fu) | ((ea >> 2) & 0x3030u));
@@ -146,7 +146,7 @@ __device__ __forceinline__ void pm_tc_q4k_row(const uint8_t *row, uint32_t c, ui
     const float S0 = d * (float)s0, M0 = -dm * (float)n0;
     const float S1 = d * (float)s1 * 0.0625f, M1 = -dm * (float)n1; /* high nibbles come x16 */
     const uint4 *qp = (const uint4 *)(b + 16 + 32 * sp);
-    const uint4 q0 = __ldg(qp), q1 = __ldg(qp + 1);
+    const uint4 q0 = RAW ? qp[0] : __ldg(qp), q1 = RAW ? qp[1] : __ldg(qp + 1);
     const uint32_t raw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
     const __half2 k1024 = __float2half2_rn(1024.0f);
 #pragma unroll

@@ -46,3 +46,24 @@ def test_tensor_core_tiles(oracle, quant, shared, T):
           "mid", rel_l2(mid, rm))
     assert rel_l2(mid, rm) < TOL
     assert rel_l2(got, ref) < TOL
+
+
+def test_tensor_core_c3_structure(oracle):
+    """C3's structure on the tensor-core path: H 2880 (11.25 q8_K blocks, a
+    zero-padded tail), MXFP4, gate/up/down and router biases, softmax
+    routing, swiglu_oai; F reduced to 640 (a 128-value tail block in the
+    q8_K mid rows) so the oracle finishes in seconds."""
+    T = 320
+    L = HostLayer(H=2880, F=640, E=4, k=2, quant=12, seed=23, router_mode=1, act_op=2, biases=True)
+    x = np.random.default_rng(9).normal(0, 1, (T, L.H)).astype(np.float32)
+    _, sel, w = L.oracle_route(x)
+    ref = L.oracle_ffn(x, sel, w)
+    dl = L.to_device()
+    wst = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
+    dl.forward(torch.from_numpy(x).cuda(), out, wst)
+    torch.cuda.synchronize()
+    v = dl.ws_view(wst, T)
+    n = _ws(wst.cpu().numpy(), wst.data_ptr(), v.n_items, 6, np.uint32)
+    assert n[4] > 0, "no tensor-core tiles at this batch"
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
