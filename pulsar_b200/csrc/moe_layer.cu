@@ -50,7 +50,7 @@ __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 #define PM_TC_G 4u                   /* tiles per MMA group */
 #define PM_TC_IMG 16384u             /* one 128 x 64 fp16 operand image */
 #define PM_TC_BIMG (PM_TC_N * 128u)  /* one 64-token x 64 fp16 image */
-#define PM_TC_XP 288u                /* raw row pitch of the expand kernel (>= 272 + 4, 16-byte multiple) */
+#define PM_TC_XP 276u                /* largest raw row pitch of the expand kernel */
 #define PM_TC_SCRATCH_CAP (4ull << 30) /* bound of the expanded-image region of the workspace */
 
 /* per item kind: operand rows, 128-row blocks, 64-wide K chunks, matrices */
@@ -69,6 +69,17 @@ __host__ __device__ __forceinline__ pm_tcgeo pm_tc_geo(uint32_t H, uint32_t F, i
 __host__ __device__ __forceinline__ uint64_t pm_tc_img_bytes(uint32_t H, uint32_t F, int nmat) {
     const pm_tcgeo g = pm_tc_geo(H, F, nmat);
     return (uint64_t)g.nm * g.rt_n * g.nch * 2u * PM_TC_IMG;
+}
+/* raw row pitch of the expand kernel: room for the span and the bytes
+ * below it to the word boundary.  Q4_K (read with 16-byte loads, rows
+ * 16-byte aligned) keeps 144 = 9 x 16: eight threads of a quarter warp hit
+ * distinct bank quads.  The others (byte, 2- and 4-byte loads) use an odd
+ * number of words, so the 32 rows of a warp fall in 32 distinct banks. */
+__host__ __device__ constexpr uint32_t pm_tc_xpitch(int q) {
+    return q == PM_QUANT_Q4_K ? 144u
+           : q == PM_QUANT_Q2_K ? 92u
+           : q == PM_QUANT_IQ2_XXS ? 76u
+           : q == PM_QUANT_MXFP4 ? 140u : 276u;
 }
 /* bytes of 256 weights of a row (a super-block; 8 blocks of 32) */
 __host__ __device__ constexpr uint32_t pm_tc_sb_bytes(int q) {
@@ -813,9 +824,9 @@ __device__ __forceinline__ void pm_tc_group(const uint8_t *row, uint32_t c, uint
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const uint32_t code = (pm_ldw<RAW>(b + 1 + ((e0 + (uint32_t)i) & 15u)) >> sh) & 15u;
-            const uint32_t m = code & 7u;
-            const float mag = (float)(m < 4u ? m : (m == 4u ? 4u : (m == 5u ? 6u : (m == 6u ? 8u : 12u))));
-            v[i] = (code & 8u ? -mag : mag) * sc;
+            /* doubled e2m1 magnitudes {0, 1, 2, 3, 4, 6, 8, 12} as nibbles; the sign is bit 3 */
+            const float mag = (float)((0xC8643210u >> (4u * (code & 7u))) & 15u);
+            v[i] = __uint_as_float(__float_as_uint(mag * sc) ^ ((code & 8u) << 28));
         }
     } else if constexpr (Q == PM_QUANT_Q2_K) {
         const uint8_t *b = row + (size_t)(c >> 2) * PM_Q2_K_BYTES;
@@ -877,7 +888,7 @@ template <int Q, int NM>
 __device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_t *sraw, const uint8_t *mat,
                                                   uint64_t rb, const pm_tcgeo &g, uint32_t K, uint32_t m,
                                                   uint32_t rt, uint32_t sp, uint8_t *img) {
-    constexpr uint32_t SB = pm_tc_sb_bytes(Q);
+    constexpr uint32_t SB = pm_tc_sb_bytes(Q), XP = pm_tc_xpitch(Q);
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint64_t sb0 = (uint64_t)sp * SB;
     const uint32_t bytes = rb - sb0 < SB ? (uint32_t)(rb - sb0) : SB;
@@ -888,7 +899,7 @@ __device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_
         const uintptr_t a0 = src & ~(uintptr_t)3;
         const uint32_t nw = (uint32_t)((src + bytes - a0 + 3u) >> 2);
         for (uint32_t w = lane; w < nw; w += 32u)
-            *(uint32_t *)(sraw + r * PM_TC_XP + 4u * w) = __ldg((const uint32_t *)(a0 + 4u * w));
+            *(uint32_t *)(sraw + r * XP + 4u * w) = __ldg((const uint32_t *)(a0 + 4u * w));
     }
     __syncthreads();
     const uint32_t r = tid, grow = rt * 128u + r;
@@ -896,7 +907,7 @@ __device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_
     const uint8_t *rowp = nullptr;
     if (grow < g.rows) {
         const uint32_t mis = (uint32_t)((uintptr_t)(mat + (uint64_t)grow * rb + sb0) & 3u);
-        rowp = sraw + r * PM_TC_XP + mis - sb0;
+        rowp = sraw + r * XP + mis - sb0;
     }
     (void)K;
     for (uint32_t c = 4u * sp; c < c_end; c++) {
