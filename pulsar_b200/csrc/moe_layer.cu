@@ -114,7 +114,7 @@ struct pm_layout {
     uint32_t max_work;
     uint32_t max_tc, ks_max, tc_slots, tc_waves;
     uint64_t tc_slot_bytes;
-    size_t tc_ord, tc_first, tcb, tcx;
+    size_t tc_ord, tc_first, tcb, tcx, tclo;
     size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, tc_tile, pairs, mid,
         midq, tcp, partial, sel_done, err, total;
 };
@@ -191,6 +191,7 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
         }
         L.tcb = o, o = pm_al(o + nb);
         L.tcx = o, o = pm_al(o + nx);
+        L.tclo = o, o = pm_al(o + (sb ? nx / (2u * PM_TC_IMG) : 0));
     }
     L.pairs = o, o = pm_al(o + (size_t)T * L.n_slot * 4);
     L.mid = o, o = pm_al(o + (size_t)T * L.n_slot * L.Fmax * 4);
@@ -233,6 +234,7 @@ struct pm_layer_args {
     uint32_t *tc_first; /* per ordinal: the item's first tile */
     uint8_t *tcb;       /* token images ((chunk * 2 + hl) * max_tc + tile) */
     uint8_t *tcx;       /* expanded weight images of the current wave, tc_slot_bytes per item */
+    uint8_t *tclo;      /* per image pair: 1 if its lo image is written (nonzero), 0 if all lo parts are 0 */
     uint64_t tc_slot_bytes;
     uint32_t tc_slots, max_tc;
     pm_block_q8K *midq; /* q8_K of the mid rows of tensor-core pairs */
@@ -887,7 +889,7 @@ __device__ __forceinline__ void pm_tc_weights(const uint8_t *row, uint32_t c, ui
 template <int Q, int NM>
 __device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_t *sraw, const uint8_t *mat,
                                                   uint64_t rb, const pm_tcgeo &g, uint32_t K, uint32_t m,
-                                                  uint32_t rt, uint32_t sp, uint8_t *img) {
+                                                  uint32_t rt, uint32_t sp, uint8_t *img, uint8_t *lo) {
     constexpr uint32_t SB = pm_tc_sb_bytes(Q), XP = pm_tc_xpitch(Q);
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint64_t sb0 = (uint64_t)sp * SB;
@@ -918,13 +920,22 @@ __device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_
 #pragma unroll
             for (int j = 0; j < 8; j++) vh[j] = vl[j] = make_uint4(0, 0, 0, 0);
         }
-        uint8_t *ih = img + (((uint64_t)(m * g.rt_n + rt) * g.nch + c) * 2u) * PM_TC_IMG + (r >> 3) * 1024u +
-                      (r & 7u) * 128u;
+        const uint32_t pi = (m * g.rt_n + rt) * g.nch + c; /* image pair */
+        uint8_t *ih = img + (uint64_t)pi * 2u * PM_TC_IMG + (r >> 3) * 1024u + (r & 7u) * 128u;
+        uint32_t nz = 0;
 #pragma unroll
         for (uint32_t j = 0; j < 8; j++) {
             const uint32_t off = (j ^ (r & 7u)) << 4;
             *(uint4 *)(ih + off) = vh[j];
-            *(uint4 *)(ih + PM_TC_IMG + off) = vl[j];
+            nz |= (vl[j].x | vl[j].y | vl[j].z | vl[j].w) & 0x7fff7fffu; /* -0 parts count as 0 */
+        }
+        /* the lo image is written only when some lo part of the tile is nonzero */
+        if (__syncthreads_or(nz != 0)) {
+#pragma unroll
+            for (uint32_t j = 0; j < 8; j++) *(uint4 *)(ih + PM_TC_IMG + (((j ^ (r & 7u)) << 4))) = vl[j];
+            if (r == 0) lo[pi] = 1;
+        } else if (r == 0) {
+            lo[pi] = 0;
         }
     }
 }
@@ -953,11 +964,13 @@ __global__ void __launch_bounds__(128) pm_tc_expand_kernel(const __grid_constant
         mat = routed ? a.down + (uint64_t)e * a.st_dn_r : a.sdown;
         rb = routed ? a.rb_dn_r : a.rb_dn_s;
     }
-    uint8_t *img = a.tcx + (uint64_t)(o - wave * a.tc_slots) * a.tc_slot_bytes;
+    const uint64_t slot = o - wave * a.tc_slots;
+    uint8_t *img = a.tcx + slot * a.tc_slot_bytes;
+    uint8_t *lo = a.tclo + slot * (a.tc_slot_bytes / (2u * PM_TC_IMG));
     if (routed)
-        pm_tc_expand_span<QR, NM>(a, sraw, mat, rb, g, K, m, rt, sp, img);
+        pm_tc_expand_span<QR, NM>(a, sraw, mat, rb, g, K, m, rt, sp, img, lo);
     else
-        pm_tc_expand_span<QS, NM>(a, sraw, mat, rb, g, K, m, rt, sp, img);
+        pm_tc_expand_span<QS, NM>(a, sraw, mat, rb, g, K, m, rt, sp, img, lo);
 }
 
 /* Pack: block (64-wide K chunk, tile); thread (token tok = tid / 4, quarter
@@ -1068,8 +1081,9 @@ __global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constan
             pm_tcu x;
             for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
                 if (!pm_tc_unit<NM>(a, u, wave, rt_max, KS, x)) continue;
-                const uint8_t *ab = a.tcx + (uint64_t)x.slot * a.tc_slot_bytes +
-                                    ((uint64_t)(x.m * x.rt_n + x.rt) * x.nch) * 2u * PM_TC_IMG;
+                const uint32_t pi0 = (x.m * x.rt_n + x.rt) * x.nch;
+                const uint8_t *ab = a.tcx + (uint64_t)x.slot * a.tc_slot_bytes + (uint64_t)pi0 * 2u * PM_TC_IMG;
+                const uint8_t *lo = a.tclo + (uint64_t)x.slot * (a.tc_slot_bytes / (2u * PM_TC_IMG)) + pi0;
                 const uint32_t bb = x.ntile * PM_TC_BIMG;
                 bool ok = true;
                 for (uint32_t c = x.c0; c < x.c1; c++, it++) {
@@ -1080,8 +1094,9 @@ __global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constan
                     }
                     uint8_t *stage = sm + st * PM_TCG_STAGE;
                     const uint8_t *bsrc = a.tcb + ((uint64_t)(c * 2u) * a.max_tc + x.tile) * PM_TC_BIMG;
-                    pm_mbar_expect_tx(&full[st], 2u * PM_TC_IMG + 2u * bb);
-                    pm_bulk_g2s(stage, ab + (uint64_t)c * 2u * PM_TC_IMG, 2u * PM_TC_IMG, &full[st]);
+                    const uint32_t na = __ldcg(lo + c) ? 2u * PM_TC_IMG : PM_TC_IMG; /* A hi (+ A lo) */
+                    pm_mbar_expect_tx(&full[st], na + 2u * bb);
+                    pm_bulk_g2s(stage, ab + (uint64_t)c * 2u * PM_TC_IMG, na, &full[st]);
                     pm_bulk_g2s(stage + 2u * PM_TC_IMG, bsrc, bb, &full[st]);
                     pm_bulk_g2s(stage + 2u * PM_TC_IMG + PM_TCG_BMAX, bsrc + (uint64_t)a.max_tc * PM_TC_BIMG, bb,
                                 &full[st]);
@@ -1103,6 +1118,8 @@ __global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constan
                 pm_tc_fence_after();
                 const uint32_t idesc = pm_idesc_f16(128, x.ntile * PM_TC_N);
                 const uint32_t d = tmem + b * 256u;
+                const uint8_t *lo = a.tclo + (uint64_t)x.slot * (a.tc_slot_bytes / (2u * PM_TC_IMG)) +
+                                    (x.m * x.rt_n + x.rt) * x.nch;
                 for (uint32_t c = x.c0; c < x.c1; c++, it++) {
                     const uint32_t st = it % S;
                     if (!pm_mbar_wait(&full[st], (it / S) & 1u, a.err)) {
@@ -1110,6 +1127,7 @@ __global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constan
                         break;
                     }
                     pm_tc_fence_after();
+                    const bool wl = __ldcg(lo + c) != 0;
                     uint8_t *stage = sm + st * PM_TCG_STAGE;
                     const uint64_t ah = pm_desc_sw128(stage), al = pm_desc_sw128(stage + PM_TC_IMG);
                     const uint64_t bh = pm_desc_sw128(stage + 2u * PM_TC_IMG);
@@ -1119,7 +1137,7 @@ __global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constan
                         /* w x = wh xh + wh xl + wl xh (+ wl xl, below fp32 rounding) */
                         pm_mma_f16(d, ah + 2 * kk, bh + 2 * kk, idesc, (c > x.c0 || kk > 0) ? 1u : 0u);
                         pm_mma_f16(d, ah + 2 * kk, bl + 2 * kk, idesc, 1u);
-                        pm_mma_f16(d, al + 2 * kk, bh + 2 * kk, idesc, 1u);
+                        if (wl) pm_mma_f16(d, al + 2 * kk, bh + 2 * kk, idesc, 1u);
                     }
                     pm_mma_commit(&empty[st]);
                 }
@@ -1506,6 +1524,7 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.tc_first = (uint32_t *)(b + L.tc_first);
     a.tcb = b + L.tcb;
     a.tcx = b + L.tcx;
+    a.tclo = b + L.tclo;
     a.tc_slot_bytes = L.tc_slot_bytes;
     a.tc_slots = L.tc_slots;
     a.max_tc = L.max_tc;
