@@ -894,14 +894,27 @@ __device__ __forceinline__ void pm_tc_expand_span(const pm_layer_args &a, uint8_
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint64_t sb0 = (uint64_t)sp * SB;
     const uint32_t bytes = rb - sb0 < SB ? (uint32_t)(rb - sb0) : SB;
-    for (uint32_t r = warp; r < 128u; r += 4u) {
-        const uint32_t grow = rt * 128u + r;
-        if (grow >= g.rows) continue;
-        const uintptr_t src = (uintptr_t)(mat + (uint64_t)grow * rb + sb0);
-        const uintptr_t a0 = src & ~(uintptr_t)3;
-        const uint32_t nw = (uint32_t)((src + bytes - a0 + 3u) >> 2);
-        for (uint32_t w = lane; w < nw; w += 32u)
-            *(uint32_t *)(sraw + r * XP + 4u * w) = __ldg((const uint32_t *)(a0 + 4u * w));
+    /* word i of the flattened (row, word) copy: batches of 8 loads in flight per thread */
+    constexpr uint32_t NW = XP / 4u, NI = NW; /* 128 threads x NW iterations = 128 rows x NW words */
+    (void)lane;
+    (void)warp;
+#pragma unroll 1
+    for (uint32_t i0 = 0; i0 < NI; i0 += 8u) {
+        uint32_t v[8];
+        bool ok[8];
+#pragma unroll
+        for (uint32_t k = 0; k < 8; k++) {
+            const uint32_t idx = tid + 128u * (i0 + k), r = idx / NW, w = idx % NW, grow = rt * 128u + r;
+            const uintptr_t src = (uintptr_t)(mat + (uint64_t)grow * rb + sb0);
+            const uintptr_t a0 = src & ~(uintptr_t)3;
+            ok[k] = i0 + k < NI && grow < g.rows && 4u * w < (uint32_t)(src + bytes - a0);
+            v[k] = ok[k] ? __ldg((const uint32_t *)(a0 + 4u * w)) : 0u;
+        }
+#pragma unroll
+        for (uint32_t k = 0; k < 8; k++) {
+            const uint32_t idx = tid + 128u * (i0 + k);
+            if (ok[k]) *(uint32_t *)(sraw + (idx / NW) * XP + 4u * (idx % NW)) = v[k];
+        }
     }
     __syncthreads();
     const uint32_t r = tid, grow = rt * 128u + r;

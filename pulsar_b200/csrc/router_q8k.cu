@@ -148,12 +148,13 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
                                                              const float *__restrict__ lbias, uint32_t n_expert,
                                                              uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq) {
     constexpr int G = EPW == 1 ? 8 : 2;
-    extern __shared__ float4 xs[]; /* [TPB][in_dim / 4] */
+    extern __shared__ float4 xs[]; /* [TPB][32 nj]: rows padded with zeros to whole 128-wide chunks */
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t t0 = blockIdx.y * TPB;
     const uint32_t nt = n_tok - t0 < (uint32_t)TPB ? n_tok - t0 : (uint32_t)TPB;
     const uint32_t e0 = (blockIdx.x * (blockDim.x >> 5) + warp) * EPW;
-    const uint32_t nj = in_dim / 128u;
+    const uint32_t nj = (in_dim + 127u) / 128u;
+    const bool tail = 128u * (nj - 1u) + 4u * lane < in_dim; /* this lane's float4 of the last chunk is real */
     const float *wr[EPW];
 #pragma unroll
     for (int ee = 0; ee < EPW; ee++) wr[ee] = w + (uint64_t)(e0 + ee < n_expert ? e0 + ee : 0u) * in_dim;
@@ -163,11 +164,13 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
     for (int q = 0; q < G; q++)
 #pragma unroll
         for (int ee = 0; ee < EPW; ee++)
-            wv[q][ee] = (uint32_t)q < nj ? __ldg((const float4 *)(wr[ee] + 128u * q + 4u * lane))
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    const uint32_t h4 = in_dim / 4u;
+            wv[q][ee] = (uint32_t)q < nj && ((uint32_t)q + 1u < nj || tail)
+                            ? __ldg((const float4 *)(wr[ee] + 128u * q + 4u * lane))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t h4 = 32u * nj, r4 = in_dim / 4u;
     for (uint32_t i = threadIdx.x; i < nt * h4; i += blockDim.x)
-        xs[i] = __ldg((const float4 *)(x + (uint64_t)(t0 + i / h4) * in_dim) + i % h4);
+        xs[i] = i % h4 < r4 ? __ldg((const float4 *)(x + (uint64_t)(t0 + i / h4) * in_dim) + i % h4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
     if (xq && blockIdx.x == 0) {
         const uint32_t nb = (in_dim + 255u) / 256u;
         for (uint32_t job = warp; job < nt * nb; job += blockDim.x >> 5) {
@@ -191,13 +194,14 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
             const uint32_t jn = g + G + q;
 #pragma unroll
             for (int ee = 0; ee < EPW; ee++)
-                nx[q][ee] = jn < nj ? __ldg((const float4 *)(wr[ee] + 128u * jn + 4u * lane))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                nx[q][ee] = jn < nj && (jn + 1u < nj || tail)
+                                ? __ldg((const float4 *)(wr[ee] + 128u * jn + 4u * lane))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int q = 0; q < G; q++) {
             const uint32_t j = g + q;
-            if (j < nj) {
+            if (j < nj && (j + 1u < nj || tail)) { /* indices past in_dim are skipped, as in the sequential order */
 #pragma unroll
                 for (int t = 0; t < TPB; t++) {
                     const float4 a = xs[t * h4 + 32u * j + lane];
@@ -243,7 +247,7 @@ template <int TPB, int EPW>
 static int pm_launch_router_tile(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
                                  uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq, cudaStream_t st) {
     static uint64_t done = 0;
-    const uint32_t smem = TPB * in_dim * 4u;
+    const uint32_t smem = TPB * ((in_dim + 127u) / 128u) * 512u;
     if (!pm_smem_attr(pm_router_tile_kernel<TPB, EPW>, smem, &done)) return 0;
     dim3 grid((n_expert + 8u * EPW - 1u) / (8u * EPW), (n_tok + TPB - 1) / TPB);
     pm_router_tile_kernel<TPB, EPW><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq);
@@ -253,10 +257,11 @@ static int pm_launch_router_tile(float *logits, const float *w, const float *x, 
 /* logits (and, with xq, the q8_K rows of x) on stream st */
 int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
                                uint32_t in_dim, uint32_t n_tok, void *xq, cudaStream_t st) {
-    if (in_dim % 128u == 0 && in_dim <= 25600u) {
-        /* tokens per tile: no more than the batch, x tile within 200 KB */
+    if (in_dim % 4u == 0 && in_dim <= 25600u) {
+        /* tokens per tile: no more than the batch, x tile (rows padded to 128) within 200 KB */
+        const uint32_t row = ((in_dim + 127u) / 128u) * 512u;
         uint32_t tpb = n_tok >= 4 ? 4u : (n_tok >= 2 ? 2u : 1u);
-        while (tpb > 1 && tpb * in_dim * 4u > 200u * 1024u) tpb >>= 1;
+        while (tpb > 1 && tpb * row > 200u * 1024u) tpb >>= 1;
         pm_block_q8K *q = (pm_block_q8K *)xq;
         if (tpb == 4 && n_tok >= 16) /* enough token tiles: 4 experts per warp */
             return pm_launch_router_tile<4, 4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
