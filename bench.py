@@ -351,8 +351,9 @@ def prefill_c3(args):
     about 256 tokens, so the routed FFN runs on the tcgen05 tiles.  The
     roofline is the tensor pipe: algorithmic FLOPs 2 T k 3 H F + 2 T E H per
     step over the step's CUDA-event time against the measured bf16 dense
-    peak; the tiles issue three fp16 MMAs per product (hi + lo operand
-    split), reported beside it as issued FLOPs."""
+    peak.  The tiles issue two fp16 MMAs per product here (weights hi x
+    tokens hi + lo; the weight lo images of MXFP4 are zero, so their MMA is
+    skipped), reported beside it as issued FLOPs."""
     from pulsar_b200 import lib, make_layer
     from pulsar_b200.configs import CONFIGS
     lib()
@@ -408,7 +409,7 @@ def prefill_c3(args):
     v = L.ws_view(ws, T)
     n = ws.view(torch.int32)[(v.n_items - ws.data_ptr()) // 4:(v.n_items - ws.data_ptr()) // 4 + 6].cpu().tolist()
     flops = 2.0 * T * k * 3 * H * F + 2.0 * T * E * H
-    issued = 3 * 2.0 * T * k * 3 * H * F
+    issued = 2 * 2.0 * T * k * 3 * H * F  # wh xh + wh xl: MXFP4 weights are exact in fp16 (zero lo images)
     peak, peak_kind = measured_peak_tensor()
     ach = flops / (ms / 1e3) / 1e12
     cfg = {"workload": "C3 prefill, one layer (BASELINE configs[2] shapes)", "n_embd": H, "n_ff": F,
