@@ -85,3 +85,24 @@ def test_row_bytes_match_block_layouts(L):
     from pulsar_b200 import row_bytes
     assert row_bytes(2, 2048) == 8 * 144 and row_bytes(0, 4096) == 16 * 84
     assert row_bytes(1, 7168) == 28 * 66 and row_bytes(12, 2880) == 90 * 17 and row_bytes(10, 7168) == 224 * 34
+
+
+def test_workspace_tensor_core_images(L):
+    """Calls of >= 128 tokens carry the tensor-core operand images: the
+    expanded weights of the experts that can reach 128 tokens (fp16 hi + lo,
+    4 B per weight of gate, up) and the token images; the weight-image region
+    is bounded (more experts run in waves)."""
+    from pulsar_b200 import LayerDesc
+    d = LayerDesc()  # C3 shapes: H 2880, F 2880, 32 MXFP4 experts, top-4
+    d.n_embd, d.n_ff, d.n_expert, d.n_used, d.quant, d.router_mode = 2880, 2880, 32, 4, 12, 1
+    d.row_bytes_gu = d.row_bytes_down = 90 * 17
+    d.gate = d.up = d.down = d.router_w = 1
+    below, at = L.pulsar_moe_layer_workspace(ctypes.byref(d), 127), L.pulsar_moe_layer_workspace(ctypes.byref(d), 128)
+    per_expert = 2 * 23 * 45 * 2 * 16384  # gate + up, 23 row blocks x 45 K chunks, hi + lo images
+    assert at - below >= 4 * per_expert   # 128 x 4 / 128 = 4 experts can reach the threshold
+    assert L.pulsar_moe_layer_workspace(ctypes.byref(d), 2048) >= 32 * per_expert
+    e = LayerDesc()  # C5 shapes: 256 IQ2_XXS experts of H 7168, F 2048: 30 GB if every expert were expanded at once
+    e.n_embd, e.n_ff, e.n_expert, e.n_used, e.quant, e.router_mode = 7168, 2048, 256, 8, 1, 0
+    e.row_bytes_gu, e.row_bytes_down = 28 * 66, 8 * 66
+    e.gate = e.up = e.down = e.router_w = 1
+    assert L.pulsar_moe_layer_workspace(ctypes.byref(e), 4096) < (10 << 30)
