@@ -194,10 +194,10 @@ class Runner:
 def launches_per_layer(T: int) -> int:
     """kernels one layer step launches for a layer call over T tokens (all ranks' tokens under
     expert parallelism): rms_norm, router (+ q8_K of x), selection, gate/up, down, combine, and
-    when an expert can reach 128 tokens the tensor-core passes - per pass (gate/up, down) the
+    when an expert can reach 192 tokens the tensor-core passes - per pass (gate/up, down) the
     token-image pack plus one expand + one gemm (the workloads here fit one expert wave) - and
     the tensor-core mid kernel"""
-    return 6 + (7 if T >= 128 else 0)
+    return 6 + (7 if T >= 192 else 0)
 
 
 def max_over_ranks(ms: float, world: int) -> float:

@@ -46,7 +46,8 @@ int pm_router_args_ok(uint32_t n_expert, uint32_t k_used, uint32_t n_tok, uint32
 __device__ static const uint16_t pm_kgrid_layer[256] = PM_IQ2XXS_KGRID_INIT;
 
 #define PM_TC_N 64u  /* tokens per tensor-core tile (MMA N) */
-#define PM_TC_MIN 128u /* experts with at least this many tokens take the tensor-core path */
+#define PM_TC_MIN 192u /* experts with at least this many tokens take the tensor-core path: below it the
+                        * once-per-call expand costs more than the dp4a units it replaces */
 #define PM_TC_G 4u                   /* tiles per MMA group */
 #define PM_TC_IMG 16384u             /* one 128 x 64 fp16 operand image */
 #define PM_TC_BIMG (PM_TC_N * 128u)  /* one 64-token x 64 fp16 image */

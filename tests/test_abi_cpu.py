@@ -88,8 +88,8 @@ def test_row_bytes_match_block_layouts(L):
 
 
 def test_workspace_tensor_core_images(L):
-    """Calls of >= 128 tokens carry the tensor-core operand images: the
-    expanded weights of the experts that can reach 128 tokens (fp16 hi + lo,
+    """Calls of >= 192 tokens carry the tensor-core operand images: the
+    expanded weights of the experts that can reach 192 tokens (fp16 hi + lo,
     4 B per weight of gate, up) and the token images; the weight-image region
     is bounded (more experts run in waves)."""
     from pulsar_b200 import LayerDesc
@@ -97,9 +97,9 @@ def test_workspace_tensor_core_images(L):
     d.n_embd, d.n_ff, d.n_expert, d.n_used, d.quant, d.router_mode = 2880, 2880, 32, 4, 12, 1
     d.row_bytes_gu = d.row_bytes_down = 90 * 17
     d.gate = d.up = d.down = d.router_w = 1
-    below, at = L.pulsar_moe_layer_workspace(ctypes.byref(d), 127), L.pulsar_moe_layer_workspace(ctypes.byref(d), 128)
+    below, at = L.pulsar_moe_layer_workspace(ctypes.byref(d), 191), L.pulsar_moe_layer_workspace(ctypes.byref(d), 192)
     per_expert = 2 * 23 * 45 * 2 * 16384  # gate + up, 23 row blocks x 45 K chunks, hi + lo images
-    assert at - below >= 4 * per_expert   # 128 x 4 / 128 = 4 experts can reach the threshold
+    assert at - below >= 4 * per_expert   # 192 x 4 / 192 = 4 experts can reach the threshold
     assert L.pulsar_moe_layer_workspace(ctypes.byref(d), 2048) >= 32 * per_expert
     e = LayerDesc()  # C5 shapes: 256 IQ2_XXS experts of H 7168, F 2048: 30 GB if every expert were expanded at once
     e.n_embd, e.n_ff, e.n_expert, e.n_used, e.quant, e.router_mode = 7168, 2048, 256, 8, 1, 0

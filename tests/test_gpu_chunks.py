@@ -8,7 +8,7 @@ from helpers import HostLayer, rel_l2
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-TC_MIN = 128  # experts with at least this many tokens take the tensor-core path (moe_layer.cu PM_TC_MIN)
+TC_MIN = 192  # experts with at least this many tokens take the tensor-core path (moe_layer.cu PM_TC_MIN)
 
 
 @pytest.mark.parametrize("T", [8, 9, 16, 17])
