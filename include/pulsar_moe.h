@@ -169,6 +169,11 @@ typedef struct pulsar_moe_layer_desc {
     uint32_t expert_lo, expert_hi; /* experts computed here: [lo, hi); hi = 0 -> all */
     uint64_t shared_row_bytes_gu, shared_row_bytes_down;
     const void *shared_gate, *shared_up, *shared_down;
+    /* limit of each device wait on a copy or MMA stage, in SM cycles; 0 =
+     * the default (2^31, about one second).  A wait that runs out sets bit 0
+     * of the call's error word, the kernel drains what it has in flight and
+     * returns; the output of that call is then invalid. */
+    uint64_t wait_cycles;
 } pulsar_moe_layer_desc;
 
 /* pulsar_rms_norm on an explicit stream (cudaStream_t, NULL = per-thread default) */
@@ -181,8 +186,10 @@ size_t pulsar_moe_layer_workspace(const pulsar_moe_layer_desc *d, uint32_t max_t
 /* out[t] = (residual ? residual[t] : 0) + moe(x[t]) for n_tok tokens.
  * x, out, residual f32 [n_tok][n_embd] (out may alias residual).  ws is
  * caller device memory of pulsar_moe_layer_workspace bytes; it carries
- * state between the layer's kernels only, so one ws serves any number of
- * sequential calls on one stream.  stream: cudaStream_t or NULL. */
+ * state between the layer's kernels only (the call's first kernel clears
+ * its control words), so one ws serves any number of sequential calls on
+ * one stream, of any n_tok and descriptor that fit it.  stream:
+ * cudaStream_t or NULL. */
 int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
                      uint32_t n_tok, void *ws, size_t ws_bytes, void *stream);
 
@@ -192,15 +199,18 @@ int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x,
  * the reference.  The workspace is a fixed 32 MiB array inside the library,
  * held by every GPU that loads it until the process exits; a call whose
  * workspace (pulsar_moe_layer_workspace) exceeds 32 MiB returns 0 with a
- * message.  The first call on a device resolves the array's address on that
- * device, so make that first call before any stream capture.  Every call
- * shares the one array: calls that overlap on the GPU (other streams,
- * other threads) race and must be serialised by the caller.  Allocates
- * nothing. */
+ * message.  Every call looks up the array's address on the current device;
+ * the first call on a device also loads the library's module there, so make
+ * that first call before any stream capture.  Every call shares the one
+ * array: calls that overlap on the GPU (other streams, other threads) race
+ * and must be serialised by the caller.  The call's error word is read with
+ * pulsar_moe_layer_ws_view(d, n_tok, NULL, &view).  Allocates nothing. */
 int pulsar_moe_layer_noalloc(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
                              uint32_t n_tok, void *stream);
 
-/* device pointers into a layer workspace after a call, for inspection */
+/* device pointers into a layer workspace after a call, for inspection.
+ * ws NULL describes the built-in array of pulsar_moe_layer_noalloc on the
+ * current device (so its callers can read the call's error word). */
 typedef struct pulsar_moe_ws_view {
     float *logits;        /* [n_tok][E] */
     int32_t *selected;    /* [n_tok][n_slot] (routed slots, then shared ids E + s) */
@@ -215,6 +225,11 @@ typedef struct pulsar_moe_ws_view {
     float *partial;                             /* [n_tok * n_slot][H] down rows before the combine */
     uint32_t *tc_tile;                          /* tensor-core tiles: (item, first token) pairs of u32 */
     uint32_t n_slot, f_max;
+    uint8_t *tc_img;        /* expanded tensor-core weight images of the last pass's last wave */
+    uint8_t *tc_lo;         /* per image pair: 1 if its lo image was written */
+    uint64_t tc_slot_bytes; /* bytes of one expert's images in tc_img */
+    uint32_t tc_slots;      /* experts per wave */
+    uint32_t max_tc;        /* tensor-core tile capacity */
 } pulsar_moe_ws_view;
 /* pulsar_moe_layer that also records events[0..5] (cudaEvent_t, NULL
  * entries skipped) around its kernels: before the router, after the

@@ -53,6 +53,7 @@ class LayerDesc(ctypes.Structure):
         ("expert_lo", ctypes.c_uint32), ("expert_hi", ctypes.c_uint32),
         ("shared_row_bytes_gu", ctypes.c_uint64), ("shared_row_bytes_down", ctypes.c_uint64),
         ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p), ("shared_down", ctypes.c_void_p),
+        ("wait_cycles", ctypes.c_uint64),
     ]
 
 
@@ -62,8 +63,9 @@ class WsView(ctypes.Structure):
                 ("err", ctypes.c_void_p), ("n_items", ctypes.c_void_p), ("item_expert", ctypes.c_void_p),
                 ("item_start", ctypes.c_void_p), ("pairs", ctypes.c_void_p), ("work_item", ctypes.c_void_p),
                 ("work_t0", ctypes.c_void_p), ("partial", ctypes.c_void_p), ("tc_tile", ctypes.c_void_p),
-                ("n_slot", ctypes.c_uint32),
-                ("f_max", ctypes.c_uint32)]
+                ("n_slot", ctypes.c_uint32), ("f_max", ctypes.c_uint32),
+                ("tc_img", ctypes.c_void_p), ("tc_lo", ctypes.c_void_p), ("tc_slot_bytes", ctypes.c_uint64),
+                ("tc_slots", ctypes.c_uint32), ("max_tc", ctypes.c_uint32)]
 
 
 # (name, argtypes) of every C entry point, in header order

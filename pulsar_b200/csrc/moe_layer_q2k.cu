@@ -1,0 +1,6 @@
+/* moe_layer_q2k.cu - the fused layer's expert passes (stream-K dp4a and
+ * tensor-core tiles) for routed experts in Q2_K, with each shared-expert
+ * format; see pm_layer.cuh. */
+#include "pm_layer.cuh"
+
+PM_LAYER_FOR_QR(pm_layer_q2k, PM_QUANT_Q2_K)

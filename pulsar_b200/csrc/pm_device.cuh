@@ -74,12 +74,16 @@ __device__ __forceinline__ bool pm_mbar_try(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-/* bounded wait for phase `parity`; false (and err |= TIMEOUT) on timeout */
-__device__ __forceinline__ bool pm_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err) {
+/* bounded wait for phase `parity`; false (and err |= TIMEOUT) after
+ * `budget` SM cycles.  Callers may shorten the budget of ring waits (a
+ * layer descriptor's wait_cycles); waits that drain copies or MMAs still
+ * in flight before a kernel exits always keep the full default budget. */
+__device__ __forceinline__ bool pm_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
+                                             long long budget = PM_WAIT_CYCLES) {
     if (pm_mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!pm_mbar_try(bar, parity)) {
-        if (clock64() - t0 > PM_WAIT_CYCLES) {
+        if (clock64() - t0 > budget) {
             if (err) atomicOr(err, PM_ERR_TIMEOUT);
             return false;
         }
@@ -101,11 +105,12 @@ __device__ __forceinline__ bool pm_mbar_try_sleep(uint64_t *bar, uint32_t parity
 }
 
 /* bounded wait with suspension; false (and err |= TIMEOUT) on timeout */
-__device__ __forceinline__ bool pm_mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t *err) {
-    if (pm_mbar_try_sleep(bar, parity)) return true;
+__device__ __forceinline__ bool pm_mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t *err,
+                                                   long long budget = PM_WAIT_CYCLES) {
+    if (budget < PM_WAIT_CYCLES ? pm_mbar_try(bar, parity) : pm_mbar_try_sleep(bar, parity)) return true;
     const long long t0 = clock64();
     while (!pm_mbar_try_sleep(bar, parity)) {
-        if (clock64() - t0 > PM_WAIT_CYCLES) {
+        if (clock64() - t0 > budget) {
             if (err) atomicOr(err, PM_ERR_TIMEOUT);
             return false;
         }

@@ -146,7 +146,8 @@ template <int TPB, int EPW>
 __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, const float *__restrict__ w,
                                                              const float *__restrict__ x,
                                                              const float *__restrict__ lbias, uint32_t n_expert,
-                                                             uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq) {
+                                                             uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq,
+                                                             uint32_t *ctl) {
     constexpr int G = EPW == 1 ? 8 : 2;
     extern __shared__ float4 xs[]; /* [TPB][32 nj]: rows padded with zeros to whole 128-wide chunks */
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
@@ -167,6 +168,8 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
             wv[q][ee] = (uint32_t)q < nj && ((uint32_t)q + 1u < nj || tail)
                             ? __ldg((const float4 *)(wr[ee] + 128u * q + 4u * lane))
                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    /* the first kernel of a layer call clears the call's control words */
+    if (ctl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 2) ctl[threadIdx.x] = 0u;
     const uint32_t h4 = 32u * nj, r4 = in_dim / 4u;
     for (uint32_t i = threadIdx.x; i < nt * h4; i += blockDim.x)
         xs[i] = i % h4 < r4 ? __ldg((const float4 *)(x + (uint64_t)(t0 + i / h4) * in_dim) + i % h4)
@@ -245,18 +248,18 @@ __global__ void __launch_bounds__(256) pm_router_tile_kernel(float *logits, cons
 
 template <int TPB, int EPW>
 static int pm_launch_router_tile(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
-                                 uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq, cudaStream_t st) {
+                                 uint32_t in_dim, uint32_t n_tok, pm_block_q8K *xq, uint32_t *ctl, cudaStream_t st) {
     static uint64_t done = 0;
     const uint32_t smem = TPB * ((in_dim + 127u) / 128u) * 512u;
     if (!pm_smem_attr(pm_router_tile_kernel<TPB, EPW>, smem, &done)) return 0;
     dim3 grid((n_expert + 8u * EPW - 1u) / (8u * EPW), (n_tok + TPB - 1) / TPB);
-    pm_router_tile_kernel<TPB, EPW><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq);
+    pm_router_tile_kernel<TPB, EPW><<<grid, 256, smem, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok, xq, ctl);
     return pm_ok(cudaGetLastError(), "router logits launch");
 }
 
 /* logits (and, with xq, the q8_K rows of x) on stream st */
 int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
-                               uint32_t in_dim, uint32_t n_tok, void *xq, cudaStream_t st) {
+                               uint32_t in_dim, uint32_t n_tok, void *xq, uint32_t *ctl, cudaStream_t st) {
     if (in_dim % 4u == 0 && in_dim <= 25600u) {
         /* tokens per tile: no more than the batch, x tile (rows padded to 128) within 200 KB */
         const uint32_t row = ((in_dim + 127u) / 128u) * 512u;
@@ -264,13 +267,14 @@ int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, co
         while (tpb > 1 && tpb * row > 200u * 1024u) tpb >>= 1;
         pm_block_q8K *q = (pm_block_q8K *)xq;
         if (tpb == 4 && n_tok >= 16) /* enough token tiles: 4 experts per warp */
-            return pm_launch_router_tile<4, 4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+            return pm_launch_router_tile<4, 4>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, ctl, st);
         switch (tpb) {
-        case 4: return pm_launch_router_tile<4, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
-        case 2: return pm_launch_router_tile<2, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
-        default: return pm_launch_router_tile<1, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, st);
+        case 4: return pm_launch_router_tile<4, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, ctl, st);
+        case 2: return pm_launch_router_tile<2, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, ctl, st);
+        default: return pm_launch_router_tile<1, 1>(logits, w, x, lbias, n_expert, in_dim, n_tok, q, ctl, st);
         }
     }
+    if (ctl && !pm_ok(cudaMemsetAsync(ctl, 0, 8, st), "layer control words")) return 0;
     dim3 grid((n_expert + 3u) / 4u, (n_tok + PM_RT_TOK - 1) / PM_RT_TOK);
     pm_router_logits_kernel<<<grid, 128, 0, st>>>(logits, w, x, lbias, n_expert, in_dim, n_tok);
     if (!pm_ok(cudaGetLastError(), "router logits launch")) return 0;
@@ -279,7 +283,7 @@ int pm_launch_router_logits_q8(float *logits, const float *w, const float *x, co
 
 int pm_launch_router_logits(float *logits, const float *w, const float *x, const float *lbias, uint32_t n_expert,
                             uint32_t in_dim, uint32_t n_tok, cudaStream_t st) {
-    return pm_launch_router_logits_q8(logits, w, x, lbias, n_expert, in_dim, n_tok, nullptr, st);
+    return pm_launch_router_logits_q8(logits, w, x, lbias, n_expert, in_dim, n_tok, nullptr, nullptr, st);
 }
 
 /* cu:6526 pulsar_matmul_f32: out[t][r] = W[r] . x[t], here in the fixed
