@@ -1,14 +1,20 @@
-"""MoE-layer tokens/s on B200: BASELINE config 2.
+"""MoE-layer tokens/s on B200 for the BASELINE configurations.
 
-Workload: the shared-expert MoE stack of config 2 - 40 layers of hidden
-2048, 256 routed experts (sigmoid top-8, Zipf(1.1) selection bias) plus one
-always-on shared expert, expert intermediate 512, all Q4_K.  Weights are
-seeded f32 N(0, 0.02) generated on the device and encoded with the GPU Q4_K
-encoder (byte-identical to crates/quant quantize_row_q4_k); hidden rows are
-fresh seeded N(0, 1) per step.  A step is one decode batch of T tokens
-through the 40-layer stack (layer l+1 reads layer l's output: the residual
-add is fused into the combine).  The stack's expert bytes read per step
-(hundreds of MB to GB) exceed the 126 MB L2, so no flush is needed.
+Default workload (--workload c4-decode): BASELINE configs[3], the largest
+configuration that fits one GPU - a stack of 94 MoE layers of hidden 4096,
+128 routed experts (softmax top-8, Zipf(1.2) logit bias), expert
+intermediate 1536, Q2_K experts (74.5 GB), router weights Q8_0 used as their
+exact f32 dequant.  Weights are seeded f32 N(0, 0.02) generated on the
+device and encoded with the GPU block encoders (byte-identical to
+crates/quant); hidden rows are fresh seeded N(0, 1) per step.  A step is one
+decode batch of T tokens through the whole stack (layer l+1 reads layer l's
+output: x + moe(rms_norm(x)), the residual add fused into the layer's
+combine).  The stack's expert bytes read per step exceed the 126 MB L2, so
+no flush is needed.  Decode batches 1, 32 and 256; the headline is T = 32.
+
+Other workloads: c2-decode (configs[1], 40 layers, T 1/8/64), c1-decode
+(configs[0]: one layer, T = 1, four weight copies rotated so L2 cannot hold
+them), c3-prefill (configs[2], one layer at T = 2048 on the tensor cores).
 
 value     tokens/s with inputs resident in HBM: K replays of a captured CUDA
           graph of the step, CUDA events on the launching stream, max over ranks.
@@ -17,14 +23,17 @@ e2e       the same through the public API each step: pinned host x -> device,
 roofline  the dominant kernel (the stream-K gate/up pass, pm_layer_sk_kernel
           <.., 2, 0>): algorithmic bytes per launch (distinct routed experts x
           gate+up bytes + shared gate+up + q8_K activations) / its CUDA-event
-          duration, vs the measured HBM copy bandwidth; traffic from ncu.
+          duration on the launching stream, vs the measured HBM copy bandwidth.
 cpu_baseline  the C restatement of the reference CPU expert lane (oracle/,
-          all host threads) on a bounded sample of the same stack.
+          all host threads) on a bounded sample of the same workload.
 
 N > 1 (torchrun): expert parallel, weak scaling.  Each rank owns its own T
 tokens and E/N experts; per layer the ranks all-gather the hidden rows,
 compute their experts for every token and reduce-scatter the outputs back to
-the token owners (NCCL).  --impl reference times the CPU lane alone.
+the token owners (NCCL).
+
+--impl reference times the reference's CPU expert lane (the oracle port)
+alone, on rank 0, with weights built by the oracle's own encoders.
 """
 from __future__ import annotations
 
@@ -33,6 +42,7 @@ import datetime
 import faulthandler
 import json
 import os
+import platform
 import subprocess
 import sys
 import threading
@@ -45,15 +55,20 @@ faulthandler.enable()
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-CFG = dict(name="C2", n_embd=2048, n_ff=512, n_expert=256, n_used=8, layers=40, zipf=1.1, batches=(1, 8, 64))
 METRIC = "MoE-layer tokens/s and % of HBM/tensor roofline at 1/2/4/8 B200"
-# DRAM bytes (read + write) per gate/up launch over the launch's algorithmic bytes, from one
-# ncu capture of this workload (profiles/pm_layer_sk_kernel_c2_b64.md: 228.4 + 13.2 MB
-# against 221.2 MB); the reported traffic scales it to this run's launch.
-TRAFFIC_RATIO = (228.40 + 13.16) / 221.2
-TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of pm_layer_sk_kernel gate/up (config 2, "
-                "batch 64) / algorithmic bytes, times this run's algorithmic bytes per launch")
 UNIT = "tokens/s"
+WORKLOADS = {
+    "c4-decode": dict(cfg="C4", layers=94, batches=(1, 32, 256), batch=32, copies=1,
+                      label="C4 Q2_K expert stack, decode (BASELINE configs[3])"),
+    "c2-decode": dict(cfg="C2", layers=40, batches=(1, 8, 64), batch=64, copies=1,
+                      label="C2 shared-expert MoE stack, decode (BASELINE configs[1])"),
+    "c1-decode": dict(cfg="C1", layers=1, batches=(1,), batch=1, copies=4,
+                      label="C1 single MoE layer, decode T=1 (BASELINE configs[0])"),
+}
+# DRAM bytes (read + write) per gate/up launch over the launch's algorithmic bytes, from one
+# ncu capture per workload (committed summaries under profiles/); the reported traffic scales
+# it to this run's launch.  None where no capture of that workload exists.
+TRAFFIC_RATIO = {"c2-decode": (228.40 + 13.16) / 221.2}
 
 
 def log(*a):
@@ -113,20 +128,55 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def measured_peak_hbm():
+def measured_peak(key: str, fallback: float):
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        return float(json.load(open(p))["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(json.load(open(p))[key]), "measured"
+    return fallback, "fallback"
 
 
-def build_stack(layers: int, lo: int, hi: int, dev):
-    from pulsar_b200 import QUANT_Q4_K, LayerSpec, make_layer
-    spec = LayerSpec(n_embd=CFG["n_embd"], n_ff=CFG["n_ff"], n_expert=CFG["n_expert"], n_used=CFG["n_used"],
-                     quant=QUANT_Q4_K, router_mode=0, zipf_s=CFG["zipf"], zipf_kind="select",
-                     shared_quant=QUANT_Q4_K, shared_n_ff=CFG["n_ff"])
+def cpu_info():
+    model = platform.processor() or ""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    n = os.cpu_count() or 1
+    return model, n
+
+
+def spec_of(wl: dict):
+    from pulsar_b200.configs import CONFIGS
+    return CONFIGS[wl["cfg"]]["spec"]
+
+
+def config_dict(wl: dict, spec, T: int, world: int):
+    q = {0: "Q2_K", 1: "IQ2_XXS", 2: "Q4_K", 10: "Q8_0", 12: "MXFP4"}
+    router = ("sigmoid" if spec.router_mode == 0 else "softmax") + f" top-{spec.n_used}"
+    if spec.zipf_s:
+        router += f", Zipf({spec.zipf_s}) {'selection' if spec.zipf_kind == 'select' else 'logit'} bias"
+    if spec.router_q8_0:
+        router += ", router weights Q8_0 (exact f32 dequant)"
+    c = {"workload": wl["label"], "layers": wl["layers"], "n_embd": spec.n_embd, "n_expert": spec.n_expert,
+         "n_used": spec.n_used, "n_shared": 1 if spec.shared_quant is not None else 0, "n_ff": spec.n_ff,
+         "quant": q[spec.quant], "router": router, "batch_per_rank": T, "global_batch": T * world,
+         "parallelism": f"ep{world}" if world > 1 else "single",
+         "l2": "per-step expert bytes exceed the 126 MB L2 (no flush)"}
+    if wl["copies"] > 1:
+        c["l2"] = (f"{wl['copies']} weight copies of the layer rotated step by step "
+                   f"({wl['copies']} x the layer's bytes > 4 x the 126 MB L2; no flush)")
+    return c
+
+
+def build_stack(wl: dict, lo: int, hi: int, dev):
+    from pulsar_b200 import make_layer
+    spec = spec_of(wl)
     stack = []
-    for l in range(layers):
+    n = wl["layers"] * wl["copies"]
+    for l in range(n):
         L = make_layer(spec, seed=2000 + l, device=dev)
         L.expert_lo, L.expert_hi = lo, hi
         stack.append(L)
@@ -135,44 +185,49 @@ def build_stack(layers: int, lo: int, hi: int, dev):
 
 
 class Runner:
-    """Static buffers and the captured CUDA graph of one decode step."""
+    """Static buffers and the captured CUDA graph of one step.  A step runs
+    `per_step` passes of T tokens; each pass is x + moe(rms_norm(x)) through
+    `layers` consecutive layers of the stack (copies > 1: pass i uses weight
+    copy i, so one replay is `copies` decode steps on different weights)."""
 
-    def __init__(self, stack, T: int, world: int, group=None):
-        self.stack, self.T, self.world, self.group = stack, T, world, group
-        H = CFG["n_embd"]
+    def __init__(self, stack, wl, T: int, world: int, group=None):
+        self.stack, self.wl, self.T, self.world, self.group = stack, wl, T, world, group
+        self.copies = wl["copies"]
+        H = stack[0].spec.n_embd
         dev = torch.device("cuda")
         self.Tg = T * world  # tokens each rank computes its experts for
-        self.x = torch.zeros((T, H), dtype=torch.float32, device=dev)
+        self.x = torch.zeros((self.copies, T, H), dtype=torch.float32, device=dev)
         self.h = [torch.zeros((self.Tg, H), dtype=torch.float32, device=dev) for _ in range(2)]
         self.part = torch.zeros((self.Tg, H), dtype=torch.float32, device=dev)
         self.rs = torch.zeros((T, H), dtype=torch.float32, device=dev)
         self.r = [torch.zeros((T, H), dtype=torch.float32, device=dev) for _ in range(2)]
         self.ws = torch.zeros(max(L.workspace_bytes(self.Tg) for L in stack), dtype=torch.uint8, device=dev)
-        self.cur = torch.zeros((T, H), dtype=torch.float32, device=dev)
+        self.cur = torch.zeros((self.copies, T, H), dtype=torch.float32, device=dev)
         self.xn = torch.zeros((self.Tg, H), dtype=torch.float32, device=dev)
         self.graph = None
         self.stream = torch.cuda.Stream()
 
     def step_body(self):
-        """x -> per layer: x + moe(rms_norm(x)) -> cur (this rank's rows)"""
         from pulsar_b200 import ops
-        cur = self.x
-        for L in self.stack:
-            if self.world == 1:
-                nxt = self.h[0] if cur is not self.h[0] else self.h[1]
-                ops.rms_norm(self.xn, cur)
-                L.forward(self.xn, nxt, self.ws, residual=cur)
-                cur = nxt
-            else:
-                import torch.distributed as dist
-                dist.all_gather_into_tensor(self.h[0], cur, group=self.group)
-                ops.rms_norm(self.xn, self.h[0])
-                L.forward(self.xn, self.part, self.ws)
-                dist.reduce_scatter_tensor(self.rs, self.part, group=self.group)
-                nxt = self.r[0] if cur is not self.r[0] else self.r[1]
-                torch.add(self.rs, cur, out=nxt)
-                cur = nxt
-        self.cur.copy_(cur)
+        nl = self.wl["layers"]
+        for c in range(self.copies):
+            cur = self.x[c]
+            for L in self.stack[c * nl:(c + 1) * nl]:
+                if self.world == 1:
+                    nxt = self.h[0] if cur is not self.h[0] else self.h[1]
+                    ops.rms_norm(self.xn, cur)
+                    L.forward(self.xn, nxt, self.ws, residual=cur)
+                    cur = nxt
+                else:
+                    import torch.distributed as dist
+                    dist.all_gather_into_tensor(self.h[0], cur, group=self.group)
+                    ops.rms_norm(self.xn, self.h[0])
+                    L.forward(self.xn, self.part, self.ws)
+                    dist.reduce_scatter_tensor(self.rs, self.part, group=self.group)
+                    nxt = self.r[0] if cur is not self.r[0] else self.r[1]
+                    torch.add(self.rs, cur, out=nxt)
+                    cur = nxt
+            self.cur[c].copy_(cur)
 
     def capture(self):
         with torch.cuda.stream(self.stream):
@@ -191,13 +246,13 @@ class Runner:
             self.graph.replay()
 
 
-def launches_per_layer(T: int) -> int:
+def launches_per_layer(T: int, tc_fmt: bool = True) -> int:
     """kernels one layer step launches for a layer call over T tokens (all ranks' tokens under
     expert parallelism): rms_norm, router (+ q8_K of x), selection, gate/up, down, combine, and
     when an expert can reach 192 tokens the tensor-core passes - per pass (gate/up, down) the
-    token-image pack plus one expand + one gemm (the workloads here fit one expert wave) - and
-    the tensor-core mid kernel"""
-    return 6 + (7 if T >= 192 else 0)
+    token-image pack plus one expand + one gemm (these workloads fit one expert wave) - and the
+    tensor-core mid kernel"""
+    return 6 + (7 if T >= 192 and tc_fmt else 0)
 
 
 def max_over_ranks(ms: float, world: int) -> float:
@@ -261,89 +316,212 @@ def profile_stages(runner: Runner, x_dev):
     experts each layer touched (read from the workspace)."""
     import ctypes
 
-    from pulsar_b200 import lib
+    from pulsar_b200 import lib, ops, row_bytes
     from pulsar_b200._lib import check, ptr
-    from pulsar_b200 import ops
     st = runner.stream
     stage_ms = np.zeros(5)
     gu_bytes = layer_bytes = 0.0
-    H, F = CFG["n_embd"], CFG["n_ff"]
+    spec = runner.stack[0].spec
+    H, F = spec.n_embd, spec.n_ff
     runner.x.copy_(x_dev)
     torch.cuda.synchronize()
-    cur = runner.x
-    for L in runner.stack:
-        nxt = runner.h[0] if cur is not runner.h[0] else runner.h[1]
-        with torch.cuda.stream(st):
-            ops.rms_norm(runner.xn, cur)
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-        for e in evs:
-            e.record(st)  # creates the event handle
-        torch.cuda.synchronize()
-        arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs])
-        check(lib().pulsar_moe_layer_profiled(ctypes.byref(L.desc()), ptr(nxt), ptr(runner.xn), ptr(cur), runner.T,
-                                              ptr(runner.ws), runner.ws.numel(), st.cuda_stream, arr),
-              "moe_layer_profiled")
-        torch.cuda.synchronize()
-        for i in range(5):
-            stage_ms[i] += evs[i].elapsed_time(evs[i + 1])
-        v = L.ws_view(runner.ws, runner.T)
-        n_routed = int(runner.ws.view(torch.int32)[(v.n_items - runner.ws.data_ptr()) // 4 + 1].item())
-        act = runner.T * ((H + 255) // 256) * 292
-        gu_bytes += (n_routed + 1) * 2 * F * L.rb_gu + act
-        layer_bytes += ((n_routed + 1) * L.weight_bytes_per_expert() + L.router_w.numel() * 4
-                        + runner.T * H * 8)
-        cur = nxt
-    n = len(runner.stack)
-    return stage_ms / n, gu_bytes / n, layer_bytes / n
+    n_calls, tiles = 0, 0
+    for c in range(runner.copies):
+        cur = runner.x[c]
+        nl = runner.wl["layers"]
+        for L in runner.stack[c * nl:(c + 1) * nl]:
+            nxt = runner.h[0] if cur is not runner.h[0] else runner.h[1]
+            with torch.cuda.stream(st):
+                ops.rms_norm(runner.xn, cur)
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            for e in evs:
+                e.record(st)  # creates the event handle
+            torch.cuda.synchronize()
+            arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in evs])
+            check(lib().pulsar_moe_layer_profiled(ctypes.byref(L.desc()), ptr(nxt), ptr(runner.xn), ptr(cur),
+                                                  runner.T, ptr(runner.ws), runner.ws.numel(), st.cuda_stream, arr),
+                  "moe_layer_profiled")
+            torch.cuda.synchronize()
+            for i in range(5):
+                stage_ms[i] += evs[i].elapsed_time(evs[i + 1])
+            v = L.ws_view(runner.ws, runner.T)
+            base = (v.n_items - runner.ws.data_ptr()) // 4
+            n = runner.ws.view(torch.int32)[base:base + 6].cpu().tolist()
+            n_routed, tiles = int(n[1]), tiles + int(n[4])
+            ns = 1 if spec.shared_quant is not None else 0
+            act = runner.T * ((H + 255) // 256) * 292
+            sh_gu = 2 * spec.shared_n_ff * row_bytes(spec.shared_quant, H) if ns else 0
+            gu_bytes += n_routed * 2 * F * L.rb_gu + sh_gu + act
+            layer_bytes += (n_routed * L.weight_bytes_per_expert() + L.shared_bytes() + L.router_w.numel() * 4
+                            + runner.T * H * 8)
+            cur = nxt
+            n_calls += 1
+    return stage_ms / n_calls, gu_bytes / n_calls, layer_bytes / n_calls, tiles / n_calls
 
 
-def cpu_baseline(stack, T: int, x0: np.ndarray, threads: int, budget_s: float = 15.0):
-    """The oracle lane (C restatement of the reference CPU expert lane) over
-    the first layers of the same stack on all host threads, extrapolated to
-    the 40-layer step.  Returns (tokens/s, layers sampled)."""
-    import oracle as orc
-    H, E, F, k = CFG["n_embd"], CFG["n_expert"], CFG["n_ff"], CFG["n_used"]
-    t_total, done = 0.0, 0
-    x = x0.astype(np.float32).copy()
-    for L in stack:
-        gate, up, down = (t.cpu().numpy() for t in (L.gate, L.up, L.down))
-        sg, su, sd = (t.cpu().numpy() for t in (L.shared_gate, L.shared_up, L.shared_down))
-        rw = L.router_w.cpu().numpy()
-        sb = L.router_select_b.cpu().numpy()
-        rg, rd = L.rb_gu, L.rb_down
-        if not np.isfinite(x).all():
-            raise RuntimeError(f"cpu baseline: non-finite hidden rows entering layer {done}")
-        t0 = time.perf_counter()
+# ---------------------------------------------------------------- CPU lane
+
+class RefStack:
+    """The workload's stack for the CPU lane, built with the oracle's own
+    encoders (no product code): `distinct` expert weight sets encoded on the
+    host and tiled over the E expert slots of one layer (the lane reads each
+    slot from its own address, as it would distinct experts: the slab is far
+    larger than any CPU cache), and per layer its own router weights and
+    Zipf bias, so routing differs layer by layer.  Layer l of the stack uses
+    the shared slab with router l."""
+
+    def __init__(self, wl: dict, n_router_layers: int, distinct: int = 8, seed: int = 90_000):
+        import oracle as orc
+        spec = spec_of(wl)
+        self.spec = spec
+        s = spec
+        H, F, E = s.n_embd, s.n_ff, s.n_expert
+        rng = np.random.default_rng(seed)
+        q = s.quant
+        qw = np.ones(H, np.float32) if q == 1 else None
+        qwf = np.ones(F, np.float32) if q == 1 else None
+        self.rb_gu, self.rb_dn = orc.row_bytes(q, H), orc.row_bytes(q, F)
+        from concurrent.futures import ThreadPoolExecutor
+
+        def enc(rows, n, qq, ww):
+            x = rng.normal(0, s.weight_std, (rows, n)).astype(np.float32)
+            parts = np.array_split(np.arange(rows), min(rows, os.cpu_count() or 1))
+            with ThreadPoolExecutor(len(parts)) as ex:  # the oracle encoders release the GIL (ctypes)
+                out = list(ex.map(lambda ix: orc.quantize(qq, x[ix[0]:ix[-1] + 1], ww), parts))
+            return np.concatenate(out, axis=0).reshape(-1)
+        d = min(distinct, E)
+        g = [enc(F, H, q, qw) for _ in range(d)]
+        u = [enc(F, H, q, qw) for _ in range(d)]
+        dn = [enc(H, F, q, qwf) for _ in range(d)]
+        self.gate = np.stack([g[e % d] for e in range(E)])
+        self.up = np.stack([u[e % d] for e in range(E)])
+        self.down = np.stack([dn[e % d] for e in range(E)])
+        self.shared = None
+        if s.shared_quant is not None:
+            sq, Fs = s.shared_quant, s.shared_n_ff
+            self.shared = dict(quant=sq, F=Fs, rb_gu=orc.row_bytes(sq, H), rb_dn=orc.row_bytes(sq, Fs),
+                               gate=enc(Fs, H, sq, None), up=enc(Fs, H, sq, None), down=enc(H, Fs, sq, None))
+        self.routers = []
+        for l in range(n_router_layers):
+            w = rng.normal(0, s.weight_std, (E, H)).astype(np.float32)
+            if s.router_q8_0:
+                w = np.stack([orc.dequant(10, r, H) for r in orc.quantize(10, w)])
+            lb = sb = None
+            if s.zipf_s:
+                rank = rng.permutation(E).astype(np.float64) + 1.0
+                if s.zipf_kind == "select":
+                    sb = (rank ** -s.zipf_s).astype(np.float32)
+                else:
+                    lb = (-s.zipf_s * np.log(rank)).astype(np.float32)
+            self.routers.append((w, lb, sb))
+
+    def layer(self, l, x, threads):
+        """x + moe(rms_norm(x)) through layer l on the CPU lane"""
+        import oracle as orc
+        s = self.spec
+        H, k = s.n_embd, s.n_used
+        w_r, lb, sb = self.routers[l % len(self.routers)]
         xn = (x / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6)).astype(np.float32)
-        lg = orc.router_logits(rw, xn)
-        sel, w = orc.router_select(lg, sb, k, 1.0, 0)
-        slots, ws = [], np.zeros((T, k + 1), np.float32)
+        lg = orc.router_logits(w_r, xn, lb)
+        sel, w = orc.router_select(lg, sb, k, s.weight_scale, s.router_mode, n_group=s.n_group,
+                                   topk_group=s.topk_group)
+        T = x.shape[0]
+        ns = 1 if self.shared is not None else 0
+        slots, ws = [], np.zeros((T, k + ns), np.float32)
         for t in range(T):
             row = []
-            for s in range(k):
-                e = int(sel[t, s])
-                ws[t, s] = w[t, s]
-                row.append(dict(gate=gate[e * F * rg:(e + 1) * F * rg], up=up[e * F * rg:(e + 1) * F * rg],
-                                down=down[e * H * rd:(e + 1) * H * rd]))
-            ws[t, k] = 1.0
-            row.append(dict(gate=sg, up=su, down=sd))
+            for j in range(k):
+                e = int(sel[t, j])
+                ws[t, j] = w[t, j]
+                row.append(dict(gate=self.gate[e], up=self.up[e], down=self.down[e]))
+            if ns:
+                ws[t, k] = 1.0
+                row.append(dict(gate=self.shared["gate"], up=self.shared["up"], down=self.shared["down"]))
             slots.append(row)
-        out = orc.moe_ffn(xn, slots, ws, H, k, (F, 2, rg, rd), (F, 2, rg, rd), n_threads=threads)
-        x = (x + out).astype(np.float32)
-        t_total += time.perf_counter() - t0
-        done += 1
-        if t_total > budget_s:
+        sh = None
+        if ns:
+            sh = (self.shared["F"], self.shared["quant"], self.shared["rb_gu"], self.shared["rb_dn"])
+        out = orc.moe_ffn(xn, slots, ws, H, k, (s.n_ff, s.quant, self.rb_gu, self.rb_dn), sh, act_op=s.act_op,
+                          n_threads=threads)
+        return (x + out).astype(np.float32)
+
+
+def cpu_lane_sample(ref: RefStack, wl: dict, T: int, x0: np.ndarray, threads: int, budget_s: float):
+    """Run the CPU lane through consecutive layers of the stack until the
+    budget is spent (at least one layer).  Returns (seconds, layers run)."""
+    x = x0.astype(np.float32).copy()
+    t0 = time.perf_counter()
+    nl = 0
+    while True:
+        x = ref.layer(nl, x, threads)
+        nl += 1
+        if nl >= wl["layers"] * wl["copies"] or time.perf_counter() - t0 >= budget_s:
             break
-    step_s = t_total / done * CFG["layers"]
-    return T / step_s, done
+    return time.perf_counter() - t0, nl
 
 
-def measured_peak_tensor():
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
-        return float(json.load(open(p))["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
-    return 1590.0, "fallback"
+def reference_arm(args, wl, T, world, rank):
+    """--impl reference: the reference's CPU expert lane (the oracle port of
+    crates/engine cpu_tier::Lane) on all host threads, rank 0 only.  A step is
+    a bounded sample: T tokens through as many consecutive layers of the
+    stack as fit the per-step budget; value = tokens/s of the whole stack
+    (T / (per-layer time x layers)), ms_per_step = the sample's measured time."""
+    if rank != 0:
+        return
+    import oracle as orc
+    orc.build()
+    spec = spec_of(wl)
+    model, ncpu = cpu_info()
+    threads = ncpu
+    t0 = time.time()
+    ref = RefStack(wl, n_router_layers=8)
+    log(f"[reference] oracle-encoded stack in {time.time() - t0:.1f}s")
+    n_layers = wl["layers"] * wl["copies"]
+    per_tok_layer, samples, layers_run = [], [], []
+    rng = np.random.default_rng(10_000)
+    budget = float(os.environ.get("PULSAR_REF_STEP_S", "3.0"))
+    for i in range(args.warmup + args.steps):
+        x0 = rng.normal(0, 1, (T, spec.n_embd)).astype(np.float32)
+        sec, nl = cpu_lane_sample(ref, wl, T, x0, threads, budget if i >= args.warmup else 0.0)
+        if i >= args.warmup:
+            samples.append(sec)
+            layers_run.append(nl)
+            per_tok_layer.append(sec / nl)
+    layer_s = float(np.sum(samples) / np.sum(layers_run))
+    val = T * wl["copies"] / (layer_s * n_layers)
+    ms = float(np.mean(samples)) * 1e3
+    nl_mean = float(np.mean(layers_run))
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "higher_is_better": True,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "dtype": "int8 dots, f32", "data": "synthetic (seeded)", "config": config_dict(wl, spec, T, 1),
+        "scaling": "weak", "vs_baseline": None,
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port", "cpu": model,
+                         "sample": f"each step: {T} tokens through {nl_mean:.1f} of the {n_layers} layers "
+                                   f"(measured {ms:.0f} ms); value = T / (per-layer time x {n_layers})"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
 
+
+def cpu_baseline_leg(wl, T, x0, budget_s=15.0):
+    """cpu_baseline of the GPU line: the same CPU lane as the reference arm,
+    at the reference default thread count (cores / 2 - 2, crates/engine/src/
+    lib.rs:1893-1896) and on all host threads."""
+    model, ncpu = cpu_info()
+    ref = RefStack(wl, n_router_layers=8)
+    n_layers = wl["layers"] * wl["copies"]
+    res = {}
+    for threads in sorted({max(1, ncpu // 2 - 2), ncpu}):
+        sec, nl = cpu_lane_sample(ref, wl, T, x0, threads, budget_s / 2)
+        res[threads] = T * wl["copies"] / (sec / nl * n_layers)
+    best = max(res, key=res.get)
+    return {"value": res[best], "unit": UNIT, "cores": best, "kind": "port", "cpu": model,
+            "by_threads": {str(k): v for k, v in res.items()},
+            "sample": f"oracle CPU lane (C restatement of crates/engine cpu_tier::Lane), batch {T}, "
+                      f"oracle-encoded weights, consecutive layers for ~{budget_s / 2:.0f} s per thread "
+                      f"count, per-layer time x {n_layers} layers"}
+
+
+# ------------------------------------------------------------- C3 prefill
 
 def prefill_c3(args):
     """C3 prefill: one layer of H 2880, 32 MXFP4 experts (softmax top-4, F 2880,
@@ -410,7 +588,7 @@ def prefill_c3(args):
     n = ws.view(torch.int32)[(v.n_items - ws.data_ptr()) // 4:(v.n_items - ws.data_ptr()) // 4 + 6].cpu().tolist()
     flops = 2.0 * T * k * 3 * H * F + 2.0 * T * E * H
     issued = 2 * 2.0 * T * k * 3 * H * F  # wh xh + wh xl: MXFP4 weights are exact in fp16 (zero lo images)
-    peak, peak_kind = measured_peak_tensor()
+    peak, peak_kind = measured_peak("bf16_tflops", 1590.0)
     ach = flops / (ms / 1e3) / 1e12
     cfg = {"workload": "C3 prefill, one layer (BASELINE configs[2] shapes)", "n_embd": H, "n_ff": F,
            "n_expert": E, "n_used": k, "quant": "MXFP4", "router": "softmax top-4, router + expert biases",
@@ -425,68 +603,43 @@ def prefill_c3(args):
                 "d2h_bytes_per_step": T * H * 4},
         "gpu_launches": (launches_per_layer(T) - 1) * args.steps, "clocks": clk.summary(),
         "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                     "peak_kind": peak_kind, "traffic": None, "algorithmic_flops_per_step": flops,
+                     "peak_kind": peak_kind + " (cuBLAS bf16 burst)", "traffic": None,
+                     "algorithmic_flops_per_step": flops,
                      "issued_mma_flops_per_step": issued, "issued_tflops": issued / (ms / 1e3) / 1e12,
                      "scope": "whole layer step (router, selection, tensor-core tiles, mid, combine)"},
         "tc_tiles": n[4], "tc_splits": n[5], "cpu_baseline": None}), flush=True)
 
+
+# -------------------------------------------------------------------- main
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=64, help="decode batch per rank of the headline value")
+    ap.add_argument("--workload", default="c4-decode", choices=sorted(WORKLOADS) + ["c3-prefill"])
+    ap.add_argument("--batch", type=int, default=0, help="decode batch per rank of the headline value "
+                                                         "(0 = the workload's default)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--layers", type=int, default=CFG["layers"])
+    ap.add_argument("--layers", type=int, default=0, help="override the stack depth (diagnostics only)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel roofline leg")
-    ap.add_argument("--all-batches", action="store_true", help="also time decode batches 1 and 8")
-    ap.add_argument("--workload", default="c2-decode", choices=["c2-decode", "c3-prefill"],
-                    help="c3-prefill: one C3 layer at T 2048 on the tensor-core path (a secondary line)")
+    ap.add_argument("--all-batches", action="store_true", help="also time the workload's other decode batches")
     args = ap.parse_args()
     if args.workload == "c3-prefill":
         return prefill_c3(args)
-    CFG["layers"] = args.layers
+    wl = dict(WORKLOADS[args.workload])
+    if args.layers:
+        wl["layers"] = args.layers
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    T = args.batch
-    config = {"workload": "C2 shared-expert MoE stack, decode (BASELINE configs[1])", "layers": CFG["layers"],
-              "n_embd": CFG["n_embd"], "n_expert": CFG["n_expert"], "n_used": CFG["n_used"], "n_shared": 1,
-              "n_ff": CFG["n_ff"], "quant": "Q4_K", "router": "sigmoid top-8, Zipf(1.1) selection bias",
-              "batch_per_rank": T, "global_batch": T * world,
-              "parallelism": f"ep{world}" if world > 1 else "single",
-              "l2": "per-step expert bytes exceed the 126 MB L2 (no flush)"}
+    T = args.batch or wl["batch"]
+    spec = spec_of(wl)
+    config = config_dict(wl, spec, T, world)
 
     if args.impl == "reference":
-        if rank != 0:
-            return
-        import oracle as orc
-        orc.build()
-        if not torch.cuda.is_available():
-            print(json.dumps({"impl": "reference", "unavailable": "the seeded weights are built on the GPU box"}))
-            return
-        dev = torch.device("cuda", local)
-        torch.cuda.set_device(dev)
-        threads = os.cpu_count() or 1
-        stack = build_stack(min(CFG["layers"], 4), 0, 0, dev)
-        vals, nl = [], 0
-        for i in range(args.warmup + args.steps):
-            x0 = np.random.default_rng(10_000 + i).normal(0, 1, (T, CFG["n_embd"])).astype(np.float32)
-            v, nl = cpu_baseline(stack, T, x0, threads, budget_s=2.0)
-            if i >= args.warmup:
-                vals.append(v)
-        val = float(np.mean(vals))
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "higher_is_better": True,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": T / val * 1e3,
-            "dtype": "int8 dots, f32", "data": "synthetic (seeded)", "config": config, "scaling": "weak",
-            "vs_baseline": None,
-            "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"oracle CPU lane on {nl} of {CFG['layers']} layers per step, extrapolated"},
-            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
-        return
+        return reference_arm(args, wl, T, world, rank)
 
     import pulsar_b200
     pulsar_b200.lib()
@@ -497,11 +650,11 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
         group = dist.group.WORLD
-    E = CFG["n_expert"]
+    E, H = spec.n_expert, spec.n_embd
     lo, hi = (rank * E // world, (rank + 1) * E // world) if world > 1 else (0, 0)
     t0 = time.time()
-    stack = build_stack(CFG["layers"], lo, hi, dev)
-    log(f"[rank {rank}] built {CFG['layers']} layers in {time.time() - t0:.1f}s "
+    stack = build_stack(wl, lo, hi, dev)
+    log(f"[rank {rank}] built {len(stack)} layers in {time.time() - t0:.1f}s "
         f"({sum(L.gate.numel() + L.up.numel() + L.down.numel() for L in stack) / 1e9:.1f} GB)")
 
     def inputs(Tb, n):
@@ -509,67 +662,73 @@ def main():
         xs = []
         for i in range(n):
             g.manual_seed(1_000_000 * (rank + 1) + 7919 * Tb + i)
-            xs.append(torch.randn((Tb, CFG["n_embd"]), generator=g, device=dev))
+            xs.append(torch.randn((wl["copies"], Tb, H), generator=g, device=dev))
         return xs
 
     results, head = {}, None
-    batches = sorted(set([T] + (list(CFG["batches"]) if args.all_batches else [])))
+    batches = sorted(set([T] + (list(wl["batches"]) if args.all_batches else [])))
+    tok_per_step = lambda Tb: Tb * world * wl["copies"]  # noqa: E731
     for Tb in batches:
-        runner = Runner(stack, Tb, world, group)
+        runner = Runner(stack, wl, Tb, world, group)
         runner.capture()
-        xs = inputs(Tb, min(args.steps + args.warmup, 32))
+        xs = inputs(Tb, min(args.steps + args.warmup, 16))
         with ClockSampler(local) as clk:
             ms = timed(runner, xs, args.steps, args.warmup, world)
         clocks = clk.summary()
         xs_host = [x.cpu().pin_memory() for x in xs]
         e2e_ms, h2d, d2h = timed_e2e(runner, xs_host, args.steps, args.warmup, world)
-        tok = Tb * world
+        tok = tok_per_step(Tb)
         results[Tb] = {"tokens_per_s": tok / (ms / 1e3), "ms_per_step": ms,
                        "e2e_tokens_per_s": tok / (e2e_ms / 1e3), "e2e_ms_per_step": e2e_ms}
         if Tb == T:
             head = (runner, xs, ms, e2e_ms, h2d, d2h, clocks)
+        else:
+            del runner
         log(f"[rank {rank}] T={Tb}: {ms:.3f} ms/step, {tok / (ms / 1e3):.0f} tok/s, e2e {e2e_ms:.3f} ms")
 
     runner, xs, ms, e2e_ms, h2d, d2h, clocks = head
     line = None
     if rank == 0:
         roof = None
+        n_layer_calls = wl["layers"] * wl["copies"]
         if world == 1 and not args.no_profile:
-            peak, peak_kind = measured_peak_hbm()
-            st_ms, gu_bytes, layer_bytes = profile_stages(runner, xs[0])
+            peak, peak_kind = measured_peak("hbm_gbs", 6650.0)
+            st_ms, gu_bytes, layer_bytes, tiles = profile_stages(runner, xs[0])
             gu_ms = float(st_ms[3])
             ach = gu_bytes / (gu_ms / 1e3) / 1e9
             layer_ms = float(st_ms.sum())
+            graph_layer_ms = ms / n_layer_calls
+            ratio = TRAFFIC_RATIO.get(args.workload)
             roof = {"bound": "hbm", "kernel": "pm_layer_sk_kernel gate/up (dp4a stream-K: gate + up + glu -> mid)",
-                    "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_kind": peak_kind,
-                    "traffic": TRAFFIC_RATIO * gu_bytes, "traffic_note": TRAFFIC_NOTE,
-                    "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms,
-                    "stage_ms": dict(zip(["router_logits+q8k_x", "(fused)", "select_csr", "gate_up", "down_combine"],
-                                         map(float, st_ms))),
+                    "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                    "peak_kind": peak_kind + " (STREAM-style copy)",
+                    "traffic": ratio * gu_bytes if ratio else None,
+                    "traffic_note": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the gate/up launch over "
+                                     "its algorithmic bytes, times this run's algorithmic bytes per launch")
+                    if ratio else "no ncu capture of this workload",
+                    "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms, "tc_tiles_per_layer": tiles,
+                    "stage_ms": dict(zip(["router_logits+q8k_x", "(fused)", "select_csr", "gate_up",
+                                          "down_combine"], map(float, st_ms))),
                     "layer": {"algorithmic_bytes": layer_bytes, "eager_ms": layer_ms,
                               "eager_gbs": layer_bytes / (layer_ms / 1e3) / 1e9,
-                              "graph_ms": ms / CFG["layers"],
-                              "graph_gbs": layer_bytes / (ms / CFG["layers"] / 1e3) / 1e9,
-                              "graph_frac": layer_bytes / (ms / CFG["layers"] / 1e3) / 1e9 / peak}}
+                              "graph_ms": graph_layer_ms,
+                              "graph_gbs": layer_bytes / (graph_layer_ms / 1e3) / 1e9,
+                              "graph_frac": layer_bytes / (graph_layer_ms / 1e3) / 1e9 / peak}}
             log(f"[rank 0] roofline {json.dumps(roof)}")
         cpu = None
         if world == 1 and not args.no_cpu:
             import oracle as orc
             orc.build()
-            threads = os.cpu_count() or 1
-            v, nl = cpu_baseline(stack, T, xs[0].cpu().numpy(), threads)
-            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"oracle CPU lane (C restatement of crates/engine cpu_tier::Lane) on {nl} of "
-                             f"{CFG['layers']} layers, batch {T}, extrapolated to the 40-layer step"}
-        tok = T * world
+            cpu = cpu_baseline_leg(wl, T, xs[0][0].cpu().numpy())
+        tok = tok_per_step(T)
         line = {"metric": METRIC, "value": tok / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8 dp4a dots, f32 accumulate", "data": "synthetic (seeded)",
                 "config": config,
                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
-                "gpu_launches": launches_per_layer(T * world) * CFG["layers"] * args.steps, "clocks": clocks, "roofline": roof,
-                "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
+                "gpu_launches": launches_per_layer(T * world) * n_layer_calls * args.steps, "clocks": clocks,
+                "roofline": roof, "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
     if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -21,7 +21,7 @@ CONFIGS = {
     "C3": dict(spec=LayerSpec(n_embd=2880, n_ff=2880, n_expert=32, n_used=4, quant=QUANT_MXFP4, router_mode=1,
                               act_op=2, biases=True), layers=1, batches=(1, 2048)),
     "C4": dict(spec=LayerSpec(n_embd=4096, n_ff=1536, n_expert=128, n_used=8, quant=QUANT_Q2_K, router_mode=1,
-                              zipf_s=1.2, zipf_kind="logit"), layers=94, batches=(1, 32, 256)),
+                              zipf_s=1.2, zipf_kind="logit", router_q8_0=True), layers=94, batches=(1, 32, 256)),
     "C5": dict(spec=LayerSpec(n_embd=7168, n_ff=2048, n_expert=256, n_used=8, quant=QUANT_IQ2_XXS, router_mode=0,
                               n_group=8, topk_group=4, zipf_s=1.1, zipf_kind="select", shared_quant=QUANT_Q8_0,
                               shared_n_ff=2048), layers=61, batches=(4096, 64)),

@@ -40,6 +40,7 @@ class LayerSpec:
     shared_quant: int | None = None
     shared_n_ff: int = 0
     biases: bool = False          # per-expert gate/up/down biases + router logit bias
+    router_q8_0: bool = False     # router weights stored as Q8_0 and used as their exact f32 dequant
     weight_std: float = 0.02
     bias_std: float = 0.01
 
@@ -163,6 +164,21 @@ def _quantized(rows: int, n: int, quant: int, std: float, gen: torch.Generator, 
     return out
 
 
+def q8_0_roundtrip(w: torch.Tensor) -> torch.Tensor:
+    """rows of f32 -> Q8_0 blocks (GPU encoder, crates/quant q8_0) -> their f32
+    dequant d * q, exact in f32: the engine stores the router as Q8_0 and
+    uploads it dequantized (crates/engine/src/lib.rs:2884-2921)"""
+    from ._lib import QUANT_Q8_0
+    rows, n = w.shape
+    rb = row_bytes(QUANT_Q8_0, n)
+    q = torch.empty(rows * rb, dtype=torch.uint8, device=w.device)
+    quantize_rows(q, w, QUANT_Q8_0)
+    blk = q.view(rows, n // 32, 34)
+    d = blk[:, :, 0:2].contiguous().view(torch.float16).to(torch.float32)
+    v = blk[:, :, 2:].contiguous().view(torch.int8).to(torch.float32)
+    return (d * v).reshape(rows, n).contiguous()
+
+
 def make_layer(spec: LayerSpec, seed: int, device="cuda") -> MoeLayer:
     """Seeded synthetic layer: every tensor from its own generator stream."""
     dev = torch.device(device)
@@ -177,6 +193,8 @@ def make_layer(spec: LayerSpec, seed: int, device="cuda") -> MoeLayer:
     up = _quantized(s.n_expert * s.n_ff, s.n_embd, s.quant, s.weight_std, gen(2), dev, qw=qw)
     down = _quantized(s.n_expert * s.n_embd, s.n_ff, s.quant, s.weight_std, gen(3), dev, qw=qw_f)
     router_w = torch.randn((s.n_expert, s.n_embd), generator=gen(4), device=dev) * s.weight_std
+    if s.router_q8_0:
+        router_w = q8_0_roundtrip(router_w.contiguous())
     layer = MoeLayer(spec=s, gate=gate, up=up, down=down, router_w=router_w.contiguous())
     if s.zipf_s > 0:
         b = zipf_bias(s.n_expert, s.zipf_s, s.zipf_kind, seed).to(dev)

@@ -130,3 +130,104 @@ class HostLayer:
         if self.shared is not None:
             L.shared_gate, L.shared_up, L.shared_down = (up_(self.shared[n]) for n in ("gate", "up", "down"))
         return L
+
+
+class DeviceMirror:
+    """The oracle's view of a layer built on the device (make_layer: GPU
+    block encoders, byte-identical to the crates/quant encoders): router
+    weights, biases and the slabs of the experts a batch selects are copied
+    to the host on demand, so true-size layers (GBs of experts) are checked
+    against the oracle without encoding them on the CPU."""
+
+    def __init__(self, layer):
+        s = layer.spec
+        self.dl, self.spec = layer, s
+        self.H, self.F, self.E, self.k, self.quant = s.n_embd, s.n_ff, s.n_expert, s.n_used, s.quant
+        self.router_mode, self.act_op = s.router_mode, s.act_op
+        self.n_group, self.topk_group, self.weight_scale = s.n_group, s.topk_group, s.weight_scale
+        self.rb_gu, self.rb_dn = layer.rb_gu, layer.rb_down
+
+        def h(t):
+            return None if t is None else t.detach().cpu().numpy()
+
+        self.router_w = h(layer.router_w)
+        self.logit_b, self.select_b = h(layer.router_logit_b), h(layer.router_select_b)
+        self.gate_b, self.up_b, self.down_b = h(layer.gate_b), h(layer.up_b), h(layer.down_b)
+        self.shared = None
+        if s.shared_quant is not None:
+            sq, Fs = s.shared_quant, s.shared_n_ff
+            self.shared = dict(quant=sq, F=Fs, rb_gu=orc.row_bytes(sq, self.H), rb_dn=orc.row_bytes(sq, Fs))
+            for n, t, rows, rb in (("gate", layer.shared_gate, Fs, self.shared["rb_gu"]),
+                                   ("up", layer.shared_up, Fs, self.shared["rb_gu"]),
+                                   ("down", layer.shared_down, self.H, self.shared["rb_dn"])):
+                self.shared[n] = t[:rows * rb].cpu().numpy()
+        self._exp = {}
+
+    def expert(self, e: int):
+        if e not in self._exp:
+            g, u, d = self.dl.expert_rows(e)
+            self._exp[e] = tuple(t.cpu().numpy() for t in (g, u, d))
+        return self._exp[e]
+
+    def oracle_route(self, x):
+        lg = orc.router_logits(self.router_w, x, self.logit_b)
+        sel, w = orc.router_select(lg, self.select_b, self.k, self.weight_scale, self.router_mode,
+                                   n_group=self.n_group, topk_group=self.topk_group)
+        return lg, sel, w
+
+    def oracle_ffn(self, x, sel, w, with_shared=True):
+        T = x.shape[0]
+        ns = 1 if (self.shared is not None and with_shared) else 0
+        slots, ws = [], np.zeros((T, self.k + ns), np.float32)
+        for t in range(T):
+            row = []
+            for s in range(self.k):
+                e = int(sel[t, s])
+                ws[t, s] = w[t, s]
+                g, u, d = self.expert(e)
+                dd = dict(gate=g, up=u, down=d)
+                if self.gate_b is not None:
+                    dd.update(gate_b=self.gate_b[e], up_b=self.up_b[e], down_b=self.down_b[e])
+                row.append(dd)
+            if ns:
+                ws[t, self.k] = 1.0
+                row.append(dict(gate=self.shared["gate"], up=self.shared["up"], down=self.shared["down"]))
+            slots.append(row)
+        sh = None
+        if ns:
+            s = self.shared
+            sh = (s["F"], s["quant"], s["rb_gu"], s["rb_dn"])
+        return orc.moe_ffn(x, slots, ws, self.H, self.k, (self.F, self.quant, self.rb_gu, self.rb_dn), sh,
+                           act_op=self.act_op)
+
+
+def reader(ws):
+    """rd(device pointer, n, dtype): n elements of a workspace region, copied to the host"""
+    base = ws.data_ptr()
+
+    def rd(p, n, dt):
+        nb = n * np.dtype(dt).itemsize
+        return ws[p - base:p - base + nb].cpu().numpy().view(dt)
+    return rd
+
+
+def tc_images(rd, v):
+    """The items (CSR expert entries) of the tensor-core experts of the last
+    layer call, in ordinal order: image slot o of the last wave holds the
+    last pass's (down) images of items[o].  Ordinals are dense over the
+    tiles' items in tile order (the first tile of an item has t0 0).
+    rd(pointer, n, dtype) reads device memory."""
+    n = rd(v.n_items, 7, np.uint32)
+    tiles = rd(v.tc_tile, 2 * int(n[4]), np.uint32).reshape(-1, 2)
+    items = [int(it) for it, t0 in tiles if t0 == 0]
+    return items
+
+
+def sw128_unswizzle(img: np.ndarray) -> np.ndarray:
+    """128 x 64 fp16 K-major tile in the 128-byte swizzle -> [128][64] fp16"""
+    b = img.reshape(16, 8, 8, 16)  # atom, row in atom, 16-byte chunk position, bytes
+    out = np.zeros((128, 64), np.float16)
+    for r in range(128):
+        for j in range(8):
+            out[r, 8 * j:8 * j + 8] = b[r >> 3, r & 7, j ^ (r & 7)].view(np.float16)
+    return out

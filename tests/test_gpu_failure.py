@@ -1,0 +1,68 @@
+"""Failure detection and workspace reuse of pulsar_moe_layer, without a GPU
+fault.
+
+- Every device wait of the layer kernels is bounded.  A descriptor's
+  wait_cycles shortens the limit of the copy-ring waits; at 1 cycle almost
+  every wait runs out, so the kernels take their failure path (record the
+  timeout in the call's error word, drain the copies still in flight with
+  the full limit, return).  The test checks the error word, then that the
+  next call with the default limit starts from a clear error word and gives
+  the right result: the context stays usable.
+- One workspace serves calls of different batch sizes and descriptors: the
+  call's first kernel clears the control words (selection counter, error
+  word), so stale bytes from earlier calls - here a workspace filled with
+  0xA5 - never leak into a later call.
+"""
+import numpy as np
+import pytest
+
+from helpers import HostLayer, reader, rel_l2
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def test_wait_limit_reports_timeout_and_recovers(oracle):
+    L = HostLayer(H=2048, F=512, E=64, k=8, quant=2, seed=41, router_mode=0, zipf=(1.1, "select"), shared=(2, 512))
+    T = 64
+    x = np.random.default_rng(8).normal(0, 1, (T, L.H)).astype(np.float32)
+    _, sel, w = L.oracle_route(x)
+    ref = L.oracle_ffn(x, sel, w)
+    dl = L.to_device()
+    ws = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
+    xd = torch.from_numpy(x).cuda()
+    rd = reader(ws)
+    dl.desc().wait_cycles = 1
+    dl.forward(xd, out, ws)
+    torch.cuda.synchronize()
+    v = dl.ws_view(ws, T)
+    assert rd(v.err, 1, np.uint32)[0] == 1, "no wait ran out at a 1-cycle limit"
+    dl.desc().wait_cycles = 0
+    dl.forward(xd, out, ws)
+    torch.cuda.synchronize()
+    assert rd(v.err, 1, np.uint32)[0] == 0
+    assert rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+def test_workspace_reused_across_sizes_and_descriptors(oracle):
+    A = HostLayer(H=512, F=512, E=8, k=2, quant=2, seed=42, router_mode=0)
+    B = HostLayer(H=512, F=512, E=32, k=8, quant=0, seed=43, router_mode=1, zipf=(1.2, "logit"), shared=(2, 256))
+    da, db = A.to_device(), B.to_device()
+    calls = [(A, da, 512), (A, da, 1), (B, db, 9), (A, da, 300), (B, db, 1)]
+    nbytes = max(d.workspace_bytes(T) for _, d, T in calls)
+    ws = torch.full((nbytes,), 0xA5, dtype=torch.uint8, device="cuda")
+    rd = reader(ws)
+    for i, (H, d, T) in enumerate(calls):
+        x = np.random.default_rng(50 + i).normal(0, 1, (T, H.H)).astype(np.float32)
+        _, sel, w = H.oracle_route(x)
+        ref = H.oracle_ffn(x, sel, w)
+        out = torch.zeros((T, H.H), dtype=torch.float32, device="cuda")
+        d.forward(torch.from_numpy(x).cuda(), out, ws)
+        torch.cuda.synchronize()
+        v = d.ws_view(ws, T)
+        assert rd(v.err, 1, np.uint32)[0] == 0, i
+        err = rel_l2(out.cpu().numpy(), ref)
+        assert err < TOL, (i, T, err)

@@ -67,3 +67,53 @@ def test_tensor_core_c3_structure(oracle):
     n = _ws(wst.cpu().numpy(), wst.data_ptr(), v.n_items, 6, np.uint32)
     assert n[4] > 0, "no tensor-core tiles at this batch"
     assert rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+IMG_CASES = [2, 0, 1, 10, 12]  # Q4_K, Q2_K, IQ2_XXS, Q8_0, MXFP4
+
+
+@pytest.mark.parametrize("quant", IMG_CASES, ids=[f"q{q}" for q in IMG_CASES])
+def test_tensor_core_weight_images(oracle, quant):
+    """The dequantized weights the tensor cores multiply: every down-pass
+    image pair (fp16 hi + lo, 128 rows x 64 K) of every tensor-core expert
+    against the oracle's f32 dequant of the same blocks.  hi + lo equals the
+    f32 weight to |w - (hi + lo)| <= 2^-22 |w| + 2^-25 (hi = fp16(w), lo =
+    fp16(w - hi); the 2^-25 term is half the fp16 subnormal spacing of lo);
+    MXFP4 weights are exact in fp16: hi == w and no lo image is written."""
+    from helpers import reader, sw128_unswizzle, tc_images
+    T = 512  # about 256 tokens per expert: every expert on the tensor-core path
+    L = HostLayer(H=512, F=512, E=4, k=2, quant=quant, seed=31, router_mode=0)
+    x = np.random.default_rng(6).normal(0, 1, (T, L.H)).astype(np.float32)
+    dl = L.to_device()
+    wst = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
+    dl.forward(torch.from_numpy(x).cuda(), out, wst)
+    torch.cuda.synchronize()
+    v = dl.ws_view(wst, T)
+    rd = reader(wst)
+    items = tc_images(rd, v)
+    assert items and len(items) <= v.tc_slots
+    item_expert = rd(v.item_expert, max(items) + 1, np.uint32)
+    H, F = L.H, L.F
+    nch, pairs_per_slot = F // 64, v.tc_slot_bytes // (2 * 16384)
+    worst = 0.0
+    for o, item in enumerate(items):
+        e = int(item_expert[item])
+        down = L.down[e]
+        deq = np.stack([oracle.dequant(quant, down[r * L.rb_dn:(r + 1) * L.rb_dn], F) for r in range(H)])
+        for rt in range(H // 128):
+            for c in range(nch):
+                pi = rt * nch + c
+                pair = rd(v.tc_img + o * v.tc_slot_bytes + pi * 2 * 16384, 2 * 16384, np.uint8)
+                hi = sw128_unswizzle(pair[:16384]).astype(np.float32)
+                has_lo = rd(v.tc_lo + o * pairs_per_slot + pi, 1, np.uint8)[0]
+                lo = sw128_unswizzle(pair[16384:]).astype(np.float32) if has_lo else np.zeros_like(hi)
+                wv = deq[128 * rt:128 * rt + 128, 64 * c:64 * c + 64]
+                if quant == 12:
+                    assert not has_lo and np.array_equal(hi, wv), (e, rt, c)
+                    continue
+                d = np.abs(wv.astype(np.float64) - (hi.astype(np.float64) + lo))
+                bound = np.abs(wv.astype(np.float64)) * 2.0 ** -22 + 2.0 ** -25
+                worst = max(worst, float(np.max(d / bound)))
+                assert np.all(d <= bound), (e, rt, c, float(np.max(d)))
+    print(f"quant {quant}: {len(items)} experts, worst |w - (hi + lo)| / bound {worst:.3f}")
