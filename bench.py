@@ -27,10 +27,13 @@ roofline  the dominant kernel (the stream-K gate/up pass, pm_layer_sk_kernel
 cpu_baseline  the C restatement of the reference CPU expert lane (oracle/,
           all host threads) on a bounded sample of the same workload.
 
-N > 1 (torchrun): expert parallel, weak scaling.  Each rank owns its own T
-tokens and E/N experts; per layer the ranks all-gather the hidden rows,
-compute their experts for every token and reduce-scatter the outputs back to
-the token owners (NCCL).
+N > 1 (torchrun): expert parallel, weak scaling, through the library's
+pulsar_moe_layer_ep.  Each rank owns its own T tokens and E/N expert slots
+(experts placed in snake order over their Zipf popularity); per layer every
+rank routes its own tokens, the q8_K rows / ids / weights are all-gathered,
+each rank runs its experts for every token that chose them (and the shared
+expert for its own tokens), and the sums are reduce-scattered back to the
+token owners - NCCL collectives on the layer's stream, inside the graph.
 
 --impl reference times the reference's CPU expert lane (the oracle port)
 alone, on rank 0, with weights built by the oracle's own encoders.
@@ -171,14 +174,23 @@ def config_dict(wl: dict, spec, T: int, world: int):
     return c
 
 
-def build_stack(wl: dict, lo: int, hi: int, dev):
+def build_stack(wl: dict, world: int, rank: int, dev):
+    """the workload's layers on this rank: all experts at N = 1; under
+    expert parallelism only this rank's expert slots, with the experts
+    placed in snake order over their Zipf popularity"""
     from pulsar_b200 import make_layer
+    from pulsar_b200.ep import shard, snake_order, zipf_popularity
     spec = spec_of(wl)
     stack = []
     n = wl["layers"] * wl["copies"]
     for l in range(n):
-        L = make_layer(spec, seed=2000 + l, device=dev)
-        L.expert_lo, L.expert_hi = lo, hi
+        seed = 2000 + l
+        if world == 1:
+            L = make_layer(spec, seed=seed, device=dev)
+        else:
+            lo, hi = shard(spec.n_expert, world, rank)
+            order = snake_order(zipf_popularity(spec.n_expert, spec.zipf_s or 1.0, seed), world)
+            L = make_layer(spec, seed=seed, device=dev, lo=lo, hi=hi, order=order)
         stack.append(L)
     torch.cuda.synchronize()
     return stack
@@ -190,20 +202,17 @@ class Runner:
     `layers` consecutive layers of the stack (copies > 1: pass i uses weight
     copy i, so one replay is `copies` decode steps on different weights)."""
 
-    def __init__(self, stack, wl, T: int, world: int, group=None):
-        self.stack, self.wl, self.T, self.world, self.group = stack, wl, T, world, group
+    def __init__(self, stack, wl, T: int, world: int, comm=None):
+        self.stack, self.wl, self.T, self.world, self.comm = stack, wl, T, world, comm
         self.copies = wl["copies"]
         H = stack[0].spec.n_embd
         dev = torch.device("cuda")
-        self.Tg = T * world  # tokens each rank computes its experts for
         self.x = torch.zeros((self.copies, T, H), dtype=torch.float32, device=dev)
-        self.h = [torch.zeros((self.Tg, H), dtype=torch.float32, device=dev) for _ in range(2)]
-        self.part = torch.zeros((self.Tg, H), dtype=torch.float32, device=dev)
-        self.rs = torch.zeros((T, H), dtype=torch.float32, device=dev)
-        self.r = [torch.zeros((T, H), dtype=torch.float32, device=dev) for _ in range(2)]
-        self.ws = torch.zeros(max(L.workspace_bytes(self.Tg) for L in stack), dtype=torch.uint8, device=dev)
+        self.h = [torch.zeros((T, H), dtype=torch.float32, device=dev) for _ in range(2)]
+        nbytes = max((L.workspace_bytes(T) if world == 1 else L.ep_workspace_bytes(world, T)) for L in stack)
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         self.cur = torch.zeros((self.copies, T, H), dtype=torch.float32, device=dev)
-        self.xn = torch.zeros((self.Tg, H), dtype=torch.float32, device=dev)
+        self.xn = torch.zeros((T, H), dtype=torch.float32, device=dev)
         self.graph = None
         self.stream = torch.cuda.Stream()
 
@@ -213,20 +222,13 @@ class Runner:
         for c in range(self.copies):
             cur = self.x[c]
             for L in self.stack[c * nl:(c + 1) * nl]:
+                nxt = self.h[0] if cur is not self.h[0] else self.h[1]
+                ops.rms_norm(self.xn, cur)
                 if self.world == 1:
-                    nxt = self.h[0] if cur is not self.h[0] else self.h[1]
-                    ops.rms_norm(self.xn, cur)
                     L.forward(self.xn, nxt, self.ws, residual=cur)
-                    cur = nxt
-                else:
-                    import torch.distributed as dist
-                    dist.all_gather_into_tensor(self.h[0], cur, group=self.group)
-                    ops.rms_norm(self.xn, self.h[0])
-                    L.forward(self.xn, self.part, self.ws)
-                    dist.reduce_scatter_tensor(self.rs, self.part, group=self.group)
-                    nxt = self.r[0] if cur is not self.r[0] else self.r[1]
-                    torch.add(self.rs, cur, out=nxt)
-                    cur = nxt
+                else:  # pulsar_moe_layer_ep: route own tokens, NCCL dispatch / combine inside the call
+                    L.forward_ep(self.comm, self.xn, nxt, self.ws, residual=cur)
+                cur = nxt
             self.cur[c].copy_(cur)
 
     def capture(self):
@@ -246,13 +248,14 @@ class Runner:
             self.graph.replay()
 
 
-def launches_per_layer(T: int, tc_fmt: bool = True) -> int:
-    """kernels one layer step launches for a layer call over T tokens (all ranks' tokens under
-    expert parallelism): rms_norm, router (+ q8_K of x), selection, gate/up, down, combine, and
-    when an expert can reach 192 tokens the tensor-core passes - per pass (gate/up, down) the
+def launches_per_layer(T: int, world: int = 1, tc_fmt: bool = True) -> int:
+    """this library's kernels one layer step launches for a layer call over T tokens per rank:
+    rms_norm, router (+ q8_K of x), selection (two launches under expert parallelism: top-k, then
+    the CSR after the dispatch), gate/up, down, combine, and when an expert can reach 192 tokens
+    (counted over every rank's tokens) the tensor-core passes - per pass (gate/up, down) the
     token-image pack plus one expand + one gemm (these workloads fit one expert wave) - and the
-    tensor-core mid kernel"""
-    return 6 + (7 if T >= 192 and tc_fmt else 0)
+    tensor-core mid kernel.  NCCL's own kernels are not counted."""
+    return 6 + (1 if world > 1 else 0) + (7 if T * world >= 192 and tc_fmt else 0)
 
 
 def max_over_ranks(ms: float, world: int) -> float:
@@ -645,15 +648,16 @@ def main():
     pulsar_b200.lib()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    group = None
+    comm = None
     if world > 1:
         import torch.distributed as dist
+
+        from pulsar_b200.ep import EpComm
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-        group = dist.group.WORLD
-    E, H = spec.n_expert, spec.n_embd
-    lo, hi = (rank * E // world, (rank + 1) * E // world) if world > 1 else (0, 0)
+        comm = EpComm(rank, world, device=dev)
+    H = spec.n_embd
     t0 = time.time()
-    stack = build_stack(wl, lo, hi, dev)
+    stack = build_stack(wl, world, rank, dev)
     log(f"[rank {rank}] built {len(stack)} layers in {time.time() - t0:.1f}s "
         f"({sum(L.gate.numel() + L.up.numel() + L.down.numel() for L in stack) / 1e9:.1f} GB)")
 
@@ -669,7 +673,7 @@ def main():
     batches = sorted(set([T] + (list(wl["batches"]) if args.all_batches else [])))
     tok_per_step = lambda Tb: Tb * world * wl["copies"]  # noqa: E731
     for Tb in batches:
-        runner = Runner(stack, wl, Tb, world, group)
+        runner = Runner(stack, wl, Tb, world, comm)
         runner.capture()
         xs = inputs(Tb, min(args.steps + args.warmup, 16))
         with ClockSampler(local) as clk:
@@ -721,13 +725,15 @@ def main():
             orc.build()
             cpu = cpu_baseline_leg(wl, T, xs[0][0].cpu().numpy())
         tok = tok_per_step(T)
+        if world > 1:
+            config["placement"] = "experts in snake order over Zipf popularity, E/N contiguous slots per rank"
         line = {"metric": METRIC, "value": tok / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8 dp4a dots, f32 accumulate", "data": "synthetic (seeded)",
                 "config": config,
                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
-                "gpu_launches": launches_per_layer(T * world) * n_layer_calls * args.steps, "clocks": clocks,
+                "gpu_launches": launches_per_layer(T, world) * n_layer_calls * args.steps, "clocks": clocks,
                 "roofline": roof, "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
     if line is not None:
         print(json.dumps(line), flush=True)

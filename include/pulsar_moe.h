@@ -208,6 +208,34 @@ int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x,
 int pulsar_moe_layer_noalloc(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
                              uint32_t n_tok, void *stream);
 
+/* Expert parallel over `world` GPUs, one process (or thread) per GPU, one
+ * call per rank with the same descriptor shapes and n_tok (north star:
+ * experts sharded over the box, NCCL dispatch / combine over NVLink; the
+ * reference's tier launches crates/engine/src/lib.rs:8395-8450 and their
+ * gather :8620-8638 do the same job across its CPU / GPU / NVMe tiers).
+ * d->expert_lo, expert_hi name this rank's experts (the ranks' ranges
+ * partition [0, n_expert)); its routed slabs need hold only those.  Each
+ * rank routes its own n_tok tokens, the (q8_K rows, expert ids, route
+ * weights) of every rank's tokens are all-gathered, every rank runs its
+ * experts for all tokens that chose them plus its shared expert for its own
+ * tokens, and the per-token sums are reduce-scattered back to the token
+ * owners: out[t] = residual[t] + moe(x[t]) for this rank's tokens.
+ * nccl_comm: an ncclComm_t of the world (pulsar_ep_comm_init, or the
+ * caller's own, from the same NCCL library); all collectives run on
+ * `stream`, so the call stays capturable into a CUDA graph.  world 1 is a
+ * plain pulsar_moe_layer call.  Workspace: pulsar_moe_layer_ep_workspace;
+ * pulsar_moe_layer_ws_view describes it for n_tok * world tokens. */
+size_t pulsar_moe_layer_ep_workspace(const pulsar_moe_layer_desc *d, uint32_t world, uint32_t max_tok);
+int pulsar_moe_layer_ep(const pulsar_moe_layer_desc *d, void *nccl_comm, uint32_t rank, uint32_t world,
+                        float *out, const float *x, const float *residual, uint32_t n_tok, void *ws, size_t ws_bytes,
+                        void *stream);
+/* NCCL communicator helpers for pulsar_moe_layer_ep: rank 0 makes the
+ * 128-byte id, the caller hands it to every rank, each rank (with its GPU
+ * current) creates its communicator */
+int pulsar_ep_unique_id(void *id);
+int pulsar_ep_comm_init(void **comm, const void *id, uint32_t world, uint32_t rank);
+int pulsar_ep_comm_destroy(void *comm);
+
 /* device pointers into a layer workspace after a call, for inspection.
  * ws NULL describes the built-in array of pulsar_moe_layer_noalloc on the
  * current device (so its callers can read the call's error word). */

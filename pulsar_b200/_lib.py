@@ -116,6 +116,14 @@ def lib() -> ctypes.CDLL:
             fn.restype = ctypes.c_int
         L.pulsar_moe_layer_workspace.argtypes = [ctypes.POINTER(LayerDesc), _U32]
         L.pulsar_moe_layer_workspace.restype = ctypes.c_size_t
+        L.pulsar_moe_layer_ep_workspace.argtypes = [ctypes.POINTER(LayerDesc), _U32, _U32]
+        L.pulsar_moe_layer_ep_workspace.restype = ctypes.c_size_t
+        L.pulsar_moe_layer_ep.argtypes = [ctypes.POINTER(LayerDesc), _P, _U32, _U32, _P, _P, _P, _U32, _P,
+                                          ctypes.c_size_t, _P]
+        L.pulsar_moe_layer_ep.restype = ctypes.c_int
+        L.pulsar_ep_unique_id.argtypes = [_P]
+        L.pulsar_ep_comm_init.argtypes = [ctypes.POINTER(ctypes.c_void_p), _P, _U32, _U32]
+        L.pulsar_ep_comm_destroy.argtypes = [_P]
         L.pulsar_row_bytes.argtypes = [_U32, _U32]
         L.pulsar_row_bytes.restype = _U64
         L.pulsar_b200_abi_error.argtypes = []

@@ -29,6 +29,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <nccl.h>
+
 #include "pm_layer.cuh"
 
 int pm_launch_q8k(void *out, const float *x, uint32_t in_dim, uint32_t n_rows, cudaStream_t st);
@@ -60,7 +62,7 @@ static bool pm_tc_on_s(const pulsar_moe_layer_desc *d) {
     return d->n_shared && pm_tc_fmt(d->shared_quant) && d->n_embd % 64 == 0 && d->shared_n_ff % 64 == 0;
 }
 
-static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
+static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T, bool ep = false) {
     pm_layout L;
     L.T = T;
     L.E = d->n_expert;
@@ -138,6 +140,10 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T) {
     /* control words: [0] selection arrival counter, [1] error word; both
      * cleared by the first kernel of every call */
     L.ctl = o, o = pm_al(o + 8);
+    /* expert parallel: per-token sums over this rank's experts, before the
+     * combine (last, so every other region sits where a single-GPU call of
+     * the same T has it) */
+    L.epo = o, o = pm_al(o + (ep ? (size_t)T * L.H * 4 : 0));
     L.total = o;
     return L;
 }
@@ -167,26 +173,29 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
     __shared__ uint32_t is_last;
     __shared__ uint4 wsum[PM_SEL_WARPS], carry;
     const uint32_t lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
-    const uint32_t token = blockIdx.x * PM_SEL_WARPS + wid;
-    if (token < a.T) {
-        float *score = (float *)sm + (size_t)wid * 2 * (a.E > 256u ? a.E : 256u);
-        if (a.E <= 256u && a.k <= 32u && a.mode <= 1u && (a.n_group <= 1u || a.topk_group >= a.n_group))
-            pm_select_fast(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, score,
-                           score + 256, a.n_slot);
-        else
-            pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0, a.n_group,
-                            a.topk_group, score, score + a.E, a.n_slot);
-        if (lane < a.S) { /* shared experts: always-on slots k.., ids E + s, weight 1 */
-            a.sel[token * a.n_slot + a.k + lane] = (int32_t)(a.E + lane);
-            a.w[token * a.n_slot + a.k + lane] = 1.0f;
+    if (a.phase != 2u) {
+        const uint32_t token = a.sel_t0 + blockIdx.x * PM_SEL_WARPS + wid;
+        if (token < a.sel_t0 + a.sel_nt) {
+            float *score = (float *)sm + (size_t)wid * 2 * (a.E > 256u ? a.E : 256u);
+            if (a.E <= 256u && a.k <= 32u && a.mode <= 1u && (a.n_group <= 1u || a.topk_group >= a.n_group))
+                pm_select_fast(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, score,
+                               score + 256, a.n_slot);
+            else
+                pm_select_token(a.sel, a.w, a.logits, a.router_sel_b, a.E, a.k, a.scale, token, a.mode, 0,
+                                a.n_group, a.topk_group, score, score + a.E, a.n_slot);
+            if (lane < a.S) { /* shared experts: always-on slots k.., ids E + s, weight 1 */
+                a.sel[token * a.n_slot + a.k + lane] = (int32_t)(a.E + lane);
+                a.w[token * a.n_slot + a.k + lane] = 1.0f;
+            }
         }
+        if (a.phase == 1u) return;
+        __threadfence(); /* every thread publishes its own selection writes */
+        __syncthreads();
+        if (threadIdx.x == 0) is_last = atomicAdd(a.sel_done, 1u) == gridDim.x - 1u;
+        __syncthreads();
+        if (!is_last) return;
+        __threadfence();
     }
-    __threadfence(); /* every thread publishes its own selection writes */
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(a.sel_done, 1u) == gridDim.x - 1u;
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
 
     /* ---- the last CTA: CSR by expert over routed pairs in [lo, hi) ---- */
     const uint32_t n_routed = a.T * a.k;
@@ -304,22 +313,23 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
             __syncwarp();
         }
     }
-    /* shared experts (computed on the shard that owns expert 0): one item
-     * each over all tokens, appended after the routed items */
-    const uint32_t n_sh = a.lo == 0 ? a.S : 0u;
-    const bool sh_tc = a.tc_s && a.T >= PM_TC_MIN; /* shared experts on the tensor-core path */
-    const uint32_t sh_chunks = sh_tc ? 0u : (a.T + PM_TT - 1) / PM_TT, sh_cost = PM_SK_CR * sh_chunks + a.T;
-    const uint32_t sh_tiles = sh_tc ? (a.T + PM_TC_N - 1) / PM_TC_N : 0u;
+    /* shared experts: one item each over the tokens [sh_t0, sh_t0 + sh_nt)
+     * they serve here, appended after the routed items */
+    const uint32_t n_sh = a.sh_nt ? a.S : 0u, snt = a.sh_nt;
+    const bool sh_tc = a.tc_s && snt >= PM_TC_MIN; /* shared experts on the tensor-core path */
+    const uint32_t sh_chunks = sh_tc ? 0u : (snt + PM_TT - 1) / PM_TT;
+    const uint32_t sh_cost = sh_tc ? 0u : PM_SK_CR * sh_chunks + snt;
+    const uint32_t sh_tiles = sh_tc ? (snt + PM_TC_N - 1) / PM_TC_N : 0u;
     for (uint32_t s = 0; s < n_sh; s++) {
-        const uint32_t item = tot_items + s, base = tot_pairs + s * a.T, w0 = tot_work + s * sh_chunks;
+        const uint32_t item = tot_items + s, base = tot_pairs + s * snt, w0 = tot_work + s * sh_chunks;
         const uint32_t c0 = tot_cost + s * sh_cost;
         if (threadIdx.x == 0) {
             a.item_expert[item] = a.E + s;
             a.item_start[item] = base;
         }
-        for (uint32_t t = threadIdx.x; t < a.T; t += blockDim.x) a.pairs[base + t] = t * a.n_slot + a.k + s;
+        for (uint32_t t = threadIdx.x; t < snt; t += blockDim.x) a.pairs[base + t] = (a.sh_t0 + t) * a.n_slot + a.k + s;
         for (uint32_t j = threadIdx.x; j < sh_chunks; j += blockDim.x) {
-            const uint32_t nt = a.T - j * PM_TT < PM_TT ? a.T - j * PM_TT : PM_TT;
+            const uint32_t nt = snt - j * PM_TT < PM_TT ? snt - j * PM_TT : PM_TT;
             a.work_item[w0 + j] = item;
             a.work_t0[w0 + j] = j * PM_TT;
             a.wd[w0 + j] = make_uint4(a.E + s, base + j * PM_TT, nt, 0u);
@@ -372,7 +382,7 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
         const uint32_t cps = (a.H / 64u + ks - 1) / ks;
         ks = (a.H / 64u + cps - 1) / cps;
         a.n_items[6] = n_ti;
-        a.item_start[tot_items + n_sh] = tot_pairs + n_sh * a.T;
+        a.item_start[tot_items + n_sh] = tot_pairs + n_sh * snt;
         a.n_items[0] = tot_items + n_sh;
         a.n_items[1] = tot_items;
         a.n_items[2] = tot_work + n_sh * sh_chunks;
@@ -460,10 +470,10 @@ __global__ void pm_layer_combine_kernel(const __grid_constant__ pm_layer_args a)
             if (a.down_b) b += a.w[t * a.n_slot + s] * a.down_b[(uint64_t)e * a.H + r];
         }
     }
-    if (a.lo == 0)
+    if (t - a.sh_t0 < a.sh_nt) /* unsigned: t >= sh_t0 and t < sh_t0 + sh_nt */
         for (uint32_t s = a.k; s < a.n_slot; s++) v += a.partial[(uint64_t)(t * a.n_slot + s) * a.H + r];
     if (b != 0.0f) v += b;
-    if (a.residual) v += a.residual[gid];
+    if (a.residual && t - a.res_t0 < a.res_nt) v += a.residual[(uint64_t)(t - a.res_t0) * a.H + r];
     a.out[gid] = v;
 }
 
@@ -551,15 +561,20 @@ static int pm_layer_dispatch(uint32_t qr, uint32_t qs, const pm_layer_args &a, c
     }
 }
 
-static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
-                             uint32_t n_tok, void *ws, size_t ws_bytes, void *stream, void *const *ev) {
-    if (!pm_desc_ok(d) || !out || !x || !ws || n_tok == 0) return 0;
-    if (!pm_router_args_ok(d->n_expert, d->n_used, n_tok, d->router_mode, 0, d->n_group, d->topk_group)) return 0;
-    const pm_layout L = pm_make_layout(d, n_tok);
-    if (L.total > ws_bytes) return 0;
-    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
-    uint8_t *b = (uint8_t *)ws;
-    pm_layer_args a;
+/* expert-parallel context of a call (world 1 = a plain single-GPU call) */
+struct pm_ep {
+    ncclComm_t comm;
+    uint32_t rank, world;
+};
+
+static int pm_nccl_ok(ncclResult_t r, const char *what) {
+    if (r == ncclSuccess) return 1;
+    fprintf(stderr, "pulsar-b200: %s: %s\n", what, ncclGetErrorString(r));
+    return 0;
+}
+
+/* the argument block of a call over T tokens in workspace ws */
+static void pm_fill_args(pm_layer_args &a, const pulsar_moe_layer_desc *d, const pm_layout &L, uint8_t *b) {
     memset(&a, 0, sizeof(a));
     a.T = L.T, a.E = L.E, a.k = L.k, a.S = L.S, a.n_slot = L.n_slot, a.H = L.H, a.Fr = L.Fr, a.Fs = L.Fs;
     a.Fmax = L.Fmax, a.hb = L.hb, a.fb = L.fb, a.max_items = L.max_items;
@@ -609,25 +624,95 @@ static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const f
     a.wait = d->wait_cycles ? (long long)(d->wait_cycles < (uint64_t)PM_WAIT_CYCLES ? d->wait_cycles
                                                                                   : (uint64_t)PM_WAIT_CYCLES)
                             : PM_WAIT_CYCLES;
-    a.out = out;
-    a.residual = residual;
+    /* single GPU: every token is this call's, the shared expert serves all
+     * of them (on the shard that owns expert 0 when the experts are split) */
+    a.sel_t0 = 0, a.sel_nt = L.T;
+    a.sh_t0 = 0, a.sh_nt = a.lo == 0 ? L.T : 0u;
+    a.res_t0 = 0, a.res_nt = L.T;
+    a.phase = 0;
+}
 
-    /* 1, 2: logits and q8_K(x) */
-    pm_ev(ev, 0, st);
-    if (!pm_launch_router_logits_q8(a.logits, d->router_w, x, d->router_logit_b, L.E, L.H, L.T, a.xq, a.sel_done, st))
-        return 0;
-    pm_ev(ev, 1, st);
-    pm_ev(ev, 2, st); /* q8_K of x is written by the router kernel */
-    /* 3: select + CSR */
+static int pm_select_launch(const pm_layer_args &a, const pm_layout &L, uint32_t grid, cudaStream_t st) {
     const uint32_t n_routed = L.T * L.k;
     const uint32_t per_warp = 2u * (L.E > 256u ? L.E : 256u) * 4u; /* scores + probabilities */
     const uint32_t smem_sel = PM_SEL_WARPS * per_warp + (n_routed <= PM_SEL_STAGE ? 2u * n_routed : 0u);
     static uint64_t done_sel = 0;
     if (!pm_smem_attr(pm_layer_select_kernel, smem_sel, &done_sel)) return 0;
-    pm_layer_select_kernel<<<(L.T + PM_SEL_WARPS - 1) / PM_SEL_WARPS, PM_SEL_WARPS * 32u, smem_sel, st>>>(a);
-    if (!pm_ok(cudaGetLastError(), "moe layer select launch")) return 0;
+    pm_layer_select_kernel<<<grid, PM_SEL_WARPS * 32u, smem_sel, st>>>(a);
+    return pm_ok(cudaGetLastError(), "moe layer select launch");
+}
+
+/* One layer call.  ep.world > 1: this rank's n_tok tokens are routed here,
+ * the (q8_K rows, ids, weights) of every rank's tokens are all-gathered,
+ * this rank's experts [lo, hi) run for every token that chose them and its
+ * shared expert for its own tokens, and the per-token sums are
+ * reduce-scattered back to the token owners. */
+static int pm_moe_layer_run(const pulsar_moe_layer_desc *d, const pm_ep &ep, float *out, const float *x,
+                            const float *residual, uint32_t n_tok, void *ws, size_t ws_bytes, void *stream,
+                            void *const *ev) {
+    if (!pm_desc_ok(d) || !out || !x || !ws || n_tok == 0) return 0;
+    if (ep.world > 1 && (!d->expert_hi || ep.rank >= ep.world || (uint64_t)n_tok * ep.world > 0xffffffffull))
+        return 0;
+    if (!pm_router_args_ok(d->n_expert, d->n_used, n_tok * ep.world, d->router_mode, 0, d->n_group, d->topk_group))
+        return 0;
+    const pm_layout L = pm_make_layout(d, n_tok * ep.world, ep.world > 1);
+    if (L.total > ws_bytes) return 0;
+    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
+    uint8_t *b = (uint8_t *)ws;
+    pm_layer_args a;
+    pm_fill_args(a, d, L, b);
+    const uint32_t t0 = ep.rank * n_tok; /* this rank's tokens in the gathered order */
+    if (ep.world > 1) {
+        a.sel_t0 = t0, a.sel_nt = n_tok;
+        a.sh_t0 = t0, a.sh_nt = d->n_shared ? n_tok : 0u;
+        a.res_t0 = t0, a.res_nt = residual ? n_tok : 0u;
+        a.out = (float *)(b + L.epo);
+    } else {
+        a.out = out;
+    }
+    a.residual = residual;
+
+    /* 1, 2: logits and q8_K(x) of this call's own tokens */
+    pm_ev(ev, 0, st);
+    if (!pm_launch_router_logits_q8(a.logits + (uint64_t)t0 * L.E, d->router_w, x, d->router_logit_b, L.E, L.H,
+                                    n_tok, a.xq + (uint64_t)t0 * L.hb, a.sel_done, st))
+        return 0;
+    pm_ev(ev, 1, st);
+    pm_ev(ev, 2, st); /* q8_K of x is written by the router kernel */
+    /* 3: select + CSR */
+    const uint32_t sel_grid = (n_tok + PM_SEL_WARPS - 1) / PM_SEL_WARPS;
+    if (ep.world == 1) {
+        if (!pm_select_launch(a, L, sel_grid, st)) return 0;
+    } else {
+        a.phase = 1;
+        if (!pm_select_launch(a, L, sel_grid, st)) return 0;
+        /* dispatch: every rank's q8_K rows, ids and weights (in place) */
+        const size_t xq_b = (size_t)n_tok * L.hb * PM_Q8_K_BYTES, nsl = (size_t)n_tok * L.n_slot;
+        if (!pm_nccl_ok(ncclGroupStart(), "ep dispatch") ||
+            !pm_nccl_ok(ncclAllGather((uint8_t *)a.xq + (size_t)ep.rank * xq_b, a.xq, xq_b, ncclUint8, ep.comm, st),
+                        "ep dispatch q8_K rows") ||
+            !pm_nccl_ok(ncclAllGather(a.sel + (size_t)ep.rank * nsl, a.sel, nsl, ncclInt32, ep.comm, st),
+                        "ep dispatch ids") ||
+            !pm_nccl_ok(ncclAllGather(a.w + (size_t)ep.rank * nsl, a.w, nsl, ncclFloat32, ep.comm, st),
+                        "ep dispatch weights") ||
+            !pm_nccl_ok(ncclGroupEnd(), "ep dispatch"))
+            return 0;
+        a.phase = 2;
+        if (!pm_select_launch(a, L, 1, st)) return 0;
+    }
     pm_ev(ev, 3, st);
-    return pm_layer_dispatch(d->quant, d->n_shared ? d->shared_quant : d->quant, a, L, st, ev);
+    if (!pm_layer_dispatch(d->quant, d->n_shared ? d->shared_quant : d->quant, a, L, st, ev)) return 0;
+    if (ep.world > 1) /* combine: this rank's tokens summed over every rank's experts */
+        if (!pm_nccl_ok(ncclReduceScatter(a.out, out, (size_t)n_tok * L.H, ncclFloat32, ncclSum, ep.comm, st),
+                        "ep combine"))
+            return 0;
+    return 1;
+}
+
+static int pm_moe_layer_impl(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
+                             uint32_t n_tok, void *ws, size_t ws_bytes, void *stream, void *const *ev) {
+    const pm_ep one = {nullptr, 0u, 1u};
+    return pm_moe_layer_run(d, one, out, x, residual, n_tok, ws, ws_bytes, stream, ev);
 }
 
 extern "C" int pulsar_moe_layer(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
@@ -682,3 +767,41 @@ extern "C" int pulsar_moe_layer_noalloc(const pulsar_moe_layer_desc *d, float *o
     return pm_moe_layer_impl(d, out, x, residual, n_tok, ws, PM_NOALLOC_SCRATCH_BYTES, stream, nullptr);
 }
 
+
+/* ============================================ expert parallel (NCCL) */
+
+extern "C" size_t pulsar_moe_layer_ep_workspace(const pulsar_moe_layer_desc *d, uint32_t world, uint32_t max_tok) {
+    if (!pm_desc_ok(d) || max_tok == 0 || world == 0 || (uint64_t)max_tok * world > 0xffffffffull) return 0;
+    return pm_make_layout(d, max_tok * world, world > 1).total;
+}
+
+extern "C" int pulsar_moe_layer_ep(const pulsar_moe_layer_desc *d, void *nccl_comm, uint32_t rank, uint32_t world,
+                                   float *out, const float *x, const float *residual, uint32_t n_tok, void *ws,
+                                   size_t ws_bytes, void *stream) {
+    if (world == 0 || (world > 1 && !nccl_comm)) return 0;
+    const pm_ep ep = {(ncclComm_t)nccl_comm, rank, world};
+    return pm_moe_layer_run(d, ep, out, x, residual, n_tok, ws, ws_bytes, stream, nullptr);
+}
+
+extern "C" int pulsar_ep_unique_id(void *id) {
+    if (!id) return 0;
+    ncclUniqueId u;
+    if (!pm_nccl_ok(ncclGetUniqueId(&u), "ep unique id")) return 0;
+    memcpy(id, &u, sizeof(u));
+    return 1;
+}
+
+extern "C" int pulsar_ep_comm_init(void **comm, const void *id, uint32_t world, uint32_t rank) {
+    if (!comm || !id || world == 0 || rank >= world) return 0;
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    ncclComm_t c = nullptr;
+    if (!pm_nccl_ok(ncclCommInitRank(&c, (int)world, u, (int)rank), "ep communicator")) return 0;
+    *comm = (void *)c;
+    return 1;
+}
+
+extern "C" int pulsar_ep_comm_destroy(void *comm) {
+    if (!comm) return 0;
+    return pm_nccl_ok(ncclCommDestroy((ncclComm_t)comm), "ep communicator destroy");
+}

@@ -83,7 +83,7 @@ struct pm_layout {
     uint64_t tc_slot_bytes;
     size_t tc_ord, tc_first, tcb, tcx, tclo;
     size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, tc_tile, pairs, mid,
-        midq, tcp, partial, ctl, total;
+        midq, tcp, partial, epo, ctl, total;
 };
 
 
@@ -122,6 +122,12 @@ struct pm_layer_args {
     float *partial; /* [T * n_slot][H] down outputs before the combine */
     uint32_t *sel_done, *err;
     long long wait; /* budget of ring / accumulator waits in SM cycles */
+    /* token ranges (expert parallel: the T tokens are every rank's, gathered)
+     *  sel_t0, sel_nt  tokens whose top-k this call computes (selection phase)
+     *  sh_t0, sh_nt    tokens the shared expert serves here
+     *  res_t0, res_nt  tokens whose residual rows this call adds
+     * phase: 0 selection then CSR in one launch, 1 selection only, 2 CSR only */
+    uint32_t sel_t0, sel_nt, sh_t0, sh_nt, res_t0, res_nt, phase;
     /* io */
     float *out;
     const float *residual;

@@ -62,6 +62,7 @@ class MoeLayer:
     shared_down: torch.Tensor | None = None
     expert_lo: int = 0
     expert_hi: int = 0
+    slab_lo: int = 0              # first expert held in the routed slabs (shards hold [slab_lo, expert_hi))
     _desc: LayerDesc | None = field(default=None, repr=False)
 
     # ---------------------------------------------------------- geometry
@@ -96,7 +97,11 @@ class MoeLayer:
         d.row_bytes_gu, d.row_bytes_down = self.rb_gu, self.rb_down
         d.expert_stride_gu = s.n_ff * self.rb_gu
         d.expert_stride_down = s.n_embd * self.rb_down
-        d.gate, d.up, d.down = ptr(self.gate), ptr(self.up), ptr(self.down)
+        # slab e sits at base + e * stride: a shard's base is its first slab less slab_lo strides
+        # (never dereferenced for experts outside the shard)
+        d.gate = ptr(self.gate) - self.slab_lo * d.expert_stride_gu
+        d.up = ptr(self.up) - self.slab_lo * d.expert_stride_gu
+        d.down = ptr(self.down) - self.slab_lo * d.expert_stride_down
         d.gate_b, d.up_b, d.down_b = ptr(self.gate_b), ptr(self.up_b), ptr(self.down_b)
         d.router_w = ptr(self.router_w)
         d.router_logit_b, d.router_select_b = ptr(self.router_logit_b), ptr(self.router_select_b)
@@ -124,6 +129,23 @@ class MoeLayer:
                                      ws.numel(), st.cuda_stream), "moe_layer")
         return out
 
+    def ep_workspace_bytes(self, world: int, max_tok: int) -> int:
+        n = int(lib().pulsar_moe_layer_ep_workspace(ctypes.byref(self.desc()), world, max_tok))
+        if n == 0:
+            raise ValueError("layer descriptor rejected by pulsar_moe_layer_ep_workspace")
+        return n
+
+    def forward_ep(self, comm, x: torch.Tensor, out: torch.Tensor, ws: torch.Tensor,
+                   residual: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """expert-parallel layer (pulsar_moe_layer_ep): x, out, residual hold
+        this rank's tokens; comm is an ep.EpComm"""
+        T = x.shape[0]
+        st = torch.cuda.current_stream() if stream is None else stream
+        check(lib().pulsar_moe_layer_ep(ctypes.byref(self.desc()), comm.handle, comm.rank, comm.world, ptr(out),
+                                        ptr(x), ptr(residual), T, ptr(ws), ws.numel(), st.cuda_stream),
+              "moe_layer_ep")
+        return out
+
     def ws_view(self, ws: torch.Tensor, n_tok: int) -> WsView:
         v = WsView()
         check(lib().pulsar_moe_layer_ws_view(ctypes.byref(self.desc()), n_tok, ptr(ws), ctypes.byref(v)), "ws_view")
@@ -132,6 +154,7 @@ class MoeLayer:
     def expert_rows(self, e: int):
         """(gate, up, down) byte views of expert e (device tensors)."""
         s = self.spec
+        e -= self.slab_lo
         g = self.gate[e * s.n_ff * self.rb_gu:(e + 1) * s.n_ff * self.rb_gu]
         u = self.up[e * s.n_ff * self.rb_gu:(e + 1) * s.n_ff * self.rb_gu]
         d = self.down[e * s.n_embd * self.rb_down:(e + 1) * s.n_embd * self.rb_down]
@@ -179,34 +202,69 @@ def q8_0_roundtrip(w: torch.Tensor) -> torch.Tensor:
     return (d * v).reshape(rows, n).contiguous()
 
 
-def make_layer(spec: LayerSpec, seed: int, device="cuda") -> MoeLayer:
-    """Seeded synthetic layer: every tensor from its own generator stream."""
+def _expert_slabs(spec: LayerSpec, seed: int, lo: int, hi: int, dev, order=None):
+    """gate, up, down slabs of expert slots [lo, hi): slot p holds logical
+    expert order[p] (identity without order), whose matrix m comes from its
+    own generator stream, so a shard holds the same bytes as the full layer
+    does for those experts."""
+    s = spec
+    qw = torch.ones(s.n_embd, device=dev) if s.quant == 1 else None
+    qw_f = torch.ones(s.n_ff, device=dev) if s.quant == 1 else None
+    out = []
+    for m, (rows, n, q) in enumerate(((s.n_ff, s.n_embd, qw), (s.n_ff, s.n_embd, qw), (s.n_embd, s.n_ff, qw_f))):
+        rb = row_bytes(s.quant, n)
+        slab = torch.empty((hi - lo) * rows * rb + SLAB_SLACK, dtype=torch.uint8, device=dev)
+        slab[(hi - lo) * rows * rb:].zero_()
+        for e in range(lo, hi):
+            le = int(order[e]) if order is not None else e
+            g = torch.Generator(device=dev).manual_seed(seed * 1_000_003 + 7 * le + m)
+            x = torch.randn((rows, n), generator=g, device=dev, dtype=torch.float32) * s.weight_std
+            o = (e - lo) * rows * rb
+            quantize_rows(slab[o:o + rows * rb], x, s.quant, qw=q)
+        out.append(slab)
+    return out
+
+
+def make_layer(spec: LayerSpec, seed: int, device="cuda", lo: int = 0, hi: int = 0, order=None) -> MoeLayer:
+    """Seeded synthetic layer: every tensor from its own generator stream.
+    lo, hi (hi 0 = all): build the routed slabs of experts [lo, hi) only -
+    an expert-parallel shard; the layer then computes those experts only.
+    order: expert placement - slot p holds logical expert order[p] (router
+    rows, biases and slabs permuted alike, so the layer computes the same
+    function; ep.snake_order balances popular experts over the shards)."""
     dev = torch.device(device)
     s = spec
+    hi = hi or s.n_expert
 
     def gen(k: int) -> torch.Generator:
         return torch.Generator(device=dev).manual_seed(seed * 1000 + k)
 
-    qw = torch.ones(s.n_embd, device=dev) if s.quant == 1 else None
-    qw_f = torch.ones(s.n_ff, device=dev) if s.quant == 1 else None
-    gate = _quantized(s.n_expert * s.n_ff, s.n_embd, s.quant, s.weight_std, gen(1), dev, qw=qw)
-    up = _quantized(s.n_expert * s.n_ff, s.n_embd, s.quant, s.weight_std, gen(2), dev, qw=qw)
-    down = _quantized(s.n_expert * s.n_embd, s.n_ff, s.quant, s.weight_std, gen(3), dev, qw=qw_f)
+    gate, up, down = _expert_slabs(s, seed, lo, hi, dev, order)
     router_w = torch.randn((s.n_expert, s.n_embd), generator=gen(4), device=dev) * s.weight_std
     if s.router_q8_0:
         router_w = q8_0_roundtrip(router_w.contiguous())
-    layer = MoeLayer(spec=s, gate=gate, up=up, down=down, router_w=router_w.contiguous())
+    perm = None if order is None else torch.as_tensor(list(order), dtype=torch.long, device=dev)
+    if perm is not None:
+        router_w = router_w[perm]
+    layer = MoeLayer(spec=s, gate=gate, up=up, down=down, router_w=router_w.contiguous(), slab_lo=lo)
+    if (lo, hi) != (0, s.n_expert):
+        layer.expert_lo, layer.expert_hi = lo, hi
     if s.zipf_s > 0:
         b = zipf_bias(s.n_expert, s.zipf_s, s.zipf_kind, seed).to(dev)
+        if perm is not None:
+            b = b[perm].contiguous()
         if s.zipf_kind == "select":
             layer.router_select_b = b
         else:
             layer.router_logit_b = b
     if s.biases:
-        layer.gate_b = (torch.randn((s.n_expert, s.n_ff), generator=gen(5), device=dev) * s.bias_std).contiguous()
-        layer.up_b = (torch.randn((s.n_expert, s.n_ff), generator=gen(6), device=dev) * s.bias_std).contiguous()
-        layer.down_b = (torch.randn((s.n_expert, s.n_embd), generator=gen(7), device=dev) * s.bias_std).contiguous()
-        rb = torch.randn((s.n_expert,), generator=gen(8), device=dev) * s.bias_std
+        def bias(shape, k):
+            t = torch.randn(shape, generator=gen(k), device=dev) * s.bias_std
+            return (t if perm is None else t[perm]).contiguous()
+        layer.gate_b = bias((s.n_expert, s.n_ff), 5)
+        layer.up_b = bias((s.n_expert, s.n_ff), 6)
+        layer.down_b = bias((s.n_expert, s.n_embd), 7)
+        rb = bias((s.n_expert,), 8)
         layer.router_logit_b = rb if layer.router_logit_b is None else (layer.router_logit_b + rb).contiguous()
     if s.shared_quant is not None:
         sq = s.shared_quant

@@ -12,6 +12,11 @@ Checked per case:
   - expert-FFN output within rel L2 1e-3 and the reference selftest bound
     max|d| <= 1e-3 max(|ref|, 1) (cu:6318-6319), on every token up to 256
     tokens and on a seeded subset of 48 tokens for the prefill batches.
+    Where experts ran on the tensor-core tiles (fp32 accumulation in the
+    MMA order) the max bound is the reference's own grouped/tensor-core
+    selftest bound 5e-3 max(|ref|, 1) (cu:6389): a different f32 summation
+    order moves a few mid values across a q8_K rounding boundary, and one
+    such step moves every output row of the token by ~5e-4.
 C3 at 2048 tokens also checks the dequantized weights of the tensor-core
 path: the MXFP4 weight images hold the oracle's f32 dequant exactly, with
 no lo part.
@@ -77,7 +82,8 @@ def test_config_true_shape(oracle, name, T):
     err = rel_l2(d, ref)
     print(f"{name} T={T}: rel_l2 {err:.3e}")
     assert err < TOL, (name, T, err)
-    assert ref_close(d, ref)
+    tiles = int(rd(v.n_items, 5, np.uint32)[4])
+    assert ref_close(d, ref, rel=5e-3 if tiles else 1e-3), (name, T, tiles)
     if name == "C3" and T == 2048:
         check_mxfp4_images(M, rd, v)
 
