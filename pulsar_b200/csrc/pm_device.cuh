@@ -107,15 +107,16 @@ __device__ __forceinline__ bool pm_mbar_try_sleep(uint64_t *bar, uint32_t parity
 /* bounded wait with suspension; false (and err |= TIMEOUT) on timeout */
 __device__ __forceinline__ bool pm_mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t *err,
                                                    long long budget = PM_WAIT_CYCLES) {
-    if (budget < PM_WAIT_CYCLES ? pm_mbar_try(bar, parity) : pm_mbar_try_sleep(bar, parity)) return true;
+    /* a shortened budget polls without suspending, so it is checked at once */
+    const bool poll = budget < PM_WAIT_CYCLES;
     const long long t0 = clock64();
-    while (!pm_mbar_try_sleep(bar, parity)) {
+    for (;;) {
+        if (poll ? pm_mbar_try(bar, parity) : pm_mbar_try_sleep(bar, parity)) return true;
         if (clock64() - t0 > budget) {
             if (err) atomicOr(err, PM_ERR_TIMEOUT);
             return false;
         }
     }
-    return true;
 }
 
 /* order this thread's generic-proxy shared accesses before later

@@ -466,6 +466,8 @@ __device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, uint32_t lpr, c
                                             uint32_t rows, uint32_t row_g) {
     if (lpr == 16u)
         pm_rows_nt<Q, NMAT, 16, EPI>(jb, w0, w1, rows, row_g);
+    else if (lpr == 32u)
+        pm_rows_nt<Q, NMAT, 32, EPI>(jb, w0, w1, rows, row_g);
     else
         pm_rows_nt<Q, NMAT, 4, EPI>(jb, w0, w1, rows, row_g);
 }
@@ -516,8 +518,9 @@ struct pm_skind {
     uint64_t rb;      /* row bytes */
     uint32_t n_units; /* 32-value units per row */
     uint32_t npair;
-    uint32_t lpr;     /* lanes per row: 16 or 4 */
+    uint32_t lpr;     /* lanes per row: 4, 16 or 32 */
     uint32_t rw;      /* rows per stage */
+    uint32_t direct;  /* 1: rows too large for the per-warp rings, read straight from global memory */
 };
 
 /* shared-memory layout of one stream-K launch (computed on the host) */

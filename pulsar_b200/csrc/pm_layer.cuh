@@ -318,7 +318,19 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
         pm_it_norm<EPI>(it, a, tab, sl, P);
         return it;
     };
+    /* stages of "direct" kinds (rows too large for the ring) are read from
+     * global memory by the consumer: the issue walk steps over them */
+    auto skip_direct = [&](pm_it &it) {
+        while (it.k < sl.n_seg) {
+            const uint32_t kind = it.k < PM_SK_MAXSEG ? tab[it.k].kind : pm_seg_get<EPI>(a, tab, sl, it.k).kind;
+            if (!P.k[kind].direct) break;
+            const uint32_t end = it.g0 + it.nst, W = (uint32_t)pm_sk_warps(NMAT);
+            it.g += (end - it.g + W - 1) / W * W;
+            pm_it_norm<EPI>(it, a, tab, sl, P);
+        }
+    };
     pm_it iti = it_init(), itc = iti;
+    skip_direct(iti);
     uint32_t ni = 0, ci = 0;
     auto issue = [&](uint32_t slot) { /* lane 0: the stage iti points at */
         const uint8_t *src[NMAT];
@@ -343,6 +355,7 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
         ni++;
         iti.g += (uint32_t)pm_sk_warps(NMAT);
         pm_it_norm<EPI>(iti, a, tab, sl, P);
+        skip_direct(iti);
     }
 
     /* ---- segments: swap the token tile, then consume this warp's stages ---- */
@@ -382,6 +395,20 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
         jb.b1 = s.b1;
         jb.wts = a.w;
         const uint32_t bytes_row = (uint32_t)kd.rb;
+        if (kd.direct) { /* rows straight from global memory, no ring stage */
+            while (itc.k == k) {
+                const uint8_t *src[NMAT];
+                uint32_t r, rows;
+                pm_stage_src<NMAT>(s, kd, itc, src, r, rows);
+                if (s.kind == 0)
+                    pm_rows_any<QR, NMAT, EPI>(jb, kd.lpr, src[0], NMAT == 2 ? src[1] : nullptr, rows, r);
+                else
+                    pm_rows_any<QS, NMAT, EPI>(jb, kd.lpr, src[0], NMAT == 2 ? src[1] : nullptr, rows, r);
+                itc.g += (uint32_t)pm_sk_warps(NMAT);
+                pm_it_norm<EPI>(itc, a, tab, sl, P);
+            }
+            continue;
+        }
         while (itc.k == k) {
             const uint32_t slot = ci % P.S;
             if (!pm_mbar_wait_sleep(bars + slot, (ci / P.S) & 1u, a.err, a.wait)) {
@@ -407,6 +434,7 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
                 ni++;
                 iti.g += (uint32_t)pm_sk_warps(NMAT);
                 pm_it_norm<EPI>(iti, a, tab, sl, P);
+                skip_direct(iti);
             }
             ci++;
             itc.g += (uint32_t)pm_sk_warps(NMAT);
@@ -857,18 +885,24 @@ __global__ void __launch_bounds__(192, 1) pm_tc_gemm_kernel(const __grid_constan
 /* geometry of one matrix kind: 16 lanes per row when a row has at least
  * 32 unit pairs (2+ pairs per lane), else 4; a stage holds whole passes
  * of the warp (32 / lpr rows) */
+/* rows per stage: whole passes of the warp (rpp rows each), ~9 KB stages
+ * where one CTA holds the SM (fewer stage hand-offs per row), ~4.5 KB
+ * otherwise */
+static uint32_t pm_kind_rw(uint32_t nmat, uint64_t rb, uint32_t rpp) {
+    const uint32_t target = pm_sk_minb((int)nmat) == 1 && pm_sk_warps((int)nmat) <= 8 ? 9216u : 4608u;
+    uint64_t passes = target / (nmat * rb * rpp);
+    if (passes < 1) passes = 1;
+    return (uint32_t)(rpp * passes);
+}
+
 static pm_skind pm_kind_for(uint32_t nmat, uint64_t rb, uint32_t n) {
     pm_skind k;
     k.rb = rb;
     k.n_units = (n + 31u) / 32u;
     k.npair = (k.n_units + 1u) / 2u;
     k.lpr = k.npair >= 32u ? 16u : 4u;
-    const uint32_t rpp = 32u / k.lpr;
-    /* ~9 KB stages where one CTA holds the SM (fewer stage hand-offs per row), ~4.5 KB otherwise */
-    const uint32_t target = pm_sk_minb((int)nmat) == 1 && pm_sk_warps((int)nmat) <= 8 ? 9216u : 4608u;
-    uint64_t passes = target / (nmat * rb * rpp);
-    if (passes < 1) passes = 1;
-    k.rw = (uint32_t)(rpp * passes);
+    k.rw = pm_kind_rw(nmat, rb, 32u / k.lpr);
+    k.direct = 0;
     return k;
 }
 
@@ -878,8 +912,8 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
     pm_skp P;
     P.k[0] = r;
     P.k[1] = s;
-    const uint32_t st0 = pm_stage_bytes(nmat, r.rb, r.rw), st1 = pm_stage_bytes(nmat, s.rb, s.rw);
-    P.stage = ((st0 > st1 ? st0 : st1) + 15u) & ~15u;
+    const uint32_t W = (uint32_t)pm_sk_warps((int)nmat);
+    const uint32_t budget = pm_sk_minb(nmat) == 1 ? 200u * 1024u : 110u * 1024u;
     P.P = r.npair > s.npair ? r.npair : s.npair;
     const uint32_t nb0 = (r.n_units + 7u) / 8u, nb1 = (s.n_units + 7u) / 8u;
     P.NB = nb0 > nb1 ? nb0 : nb1;
@@ -889,9 +923,25 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
     P.off_acts = (off + 15u) & ~15u;
     off = P.off_acts + pm_acts_bytes(P.P, P.NB);
     P.off_bar = (off + 15u) & ~15u;
-    const uint32_t W = (uint32_t)pm_sk_warps((int)nmat);
     P.off_ring = (P.off_bar + W * 8u * 8u + 127u) & ~127u;
-    const uint32_t budget = pm_sk_minb(nmat) == 1 ? 200u * 1024u : 110u * 1024u;
+    /* a kind whose two-deep rings do not fit next to the token tile takes a
+     * whole warp per row (one row per stage); if that still does not fit,
+     * it reads its rows from global memory (e.g. Q8_0 rows of 7168 values) */
+    P.stage = 16u;
+    for (int i = 0; i < 2; i++) {
+        pm_skind &k = P.k[i];
+        auto fits = [&](const pm_skind &kk) {
+            const uint32_t sti = (pm_stage_bytes(nmat, kk.rb, kk.rw) + 15u) & ~15u;
+            return (uint64_t)P.off_ring + (uint64_t)W * 2u * sti <= budget;
+        };
+        if (!fits(k) && k.lpr == 16u) {
+            k.lpr = 32u;
+            k.rw = pm_kind_rw(nmat, k.rb, 1u);
+        }
+        k.direct = fits(k) ? 0u : 1u;
+        const uint32_t sti = (pm_stage_bytes(nmat, k.rb, k.rw) + 15u) & ~15u;
+        if (!k.direct && sti > P.stage) P.stage = sti;
+    }
     uint32_t S = budget > P.off_ring ? (budget - P.off_ring) / (W * P.stage) : 2u;
     P.S = S < 2 ? 2 : (S > 8 ? 8 : S);
     P.smem = P.off_ring + W * P.S * P.stage;

@@ -50,7 +50,7 @@ def test_noalloc_matches_workspace_layer_and_oracle():
     layers = {"shared": (shared, shared.to_device()), "plain": (plain, plain.to_device())}
     stream = torch.cuda.current_stream().cuda_stream
     # (layer, tokens): repeated calls, a large one (more of the array written) between small ones
-    calls = [("shared", 11), ("shared", 11), ("plain", 3), ("shared", 200), ("plain", 1), ("shared", 5)]
+    calls = [("shared", 11), ("shared", 11), ("plain", 3), ("shared", 64), ("plain", 1), ("shared", 5)]
     for i, (name, T) in enumerate(calls):
         H, dl = layers[name]
         rng = np.random.default_rng(100 + i)
