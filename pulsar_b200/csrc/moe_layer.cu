@@ -467,7 +467,7 @@ __global__ void pm_layer_combine_kernel(const __grid_constant__ pm_layer_args a)
         const uint32_t e = (uint32_t)a.sel[t * a.n_slot + s];
         if (e >= a.lo && e < a.hi) {
             v += a.partial[(uint64_t)(t * a.n_slot + s) * a.H + r];
-            if (a.down_b) b += a.w[t * a.n_slot + s] * a.down_b[(uint64_t)e * a.H + r];
+            if (a.down_b) b = __fadd_rn(b, __fmul_rn(a.w[t * a.n_slot + s], a.down_b[(uint64_t)e * a.H + r]));
         }
     }
     if (t - a.sh_t0 < a.sh_nt) /* unsigned: t >= sh_t0 and t < sh_t0 + sh_nt */

@@ -74,15 +74,29 @@ __device__ __forceinline__ bool pm_mbar_try(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+/* non-blocking test of phase `parity` (never suspends the thread) */
+__device__ __forceinline__ bool pm_mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(pm_smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 /* bounded wait for phase `parity`; false (and err |= TIMEOUT) after
  * `budget` SM cycles.  Callers may shorten the budget of ring waits (a
  * layer descriptor's wait_cycles); waits that drain copies or MMAs still
  * in flight before a kernel exits always keep the full default budget. */
 __device__ __forceinline__ bool pm_mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
                                              long long budget = PM_WAIT_CYCLES) {
-    if (pm_mbar_try(bar, parity)) return true;
+    const bool poll = budget < PM_WAIT_CYCLES; /* a shortened budget never suspends the thread */
+    if (poll ? pm_mbar_test(bar, parity) : pm_mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
-    while (!pm_mbar_try(bar, parity)) {
+    while (!(poll ? pm_mbar_test(bar, parity) : pm_mbar_try(bar, parity))) {
         if (clock64() - t0 > budget) {
             if (err) atomicOr(err, PM_ERR_TIMEOUT);
             return false;
@@ -111,7 +125,7 @@ __device__ __forceinline__ bool pm_mbar_wait_sleep(uint64_t *bar, uint32_t parit
     const bool poll = budget < PM_WAIT_CYCLES;
     const long long t0 = clock64();
     for (;;) {
-        if (poll ? pm_mbar_try(bar, parity) : pm_mbar_try_sleep(bar, parity)) return true;
+        if (poll ? pm_mbar_test(bar, parity) : pm_mbar_try_sleep(bar, parity)) return true;
         if (clock64() - t0 > budget) {
             if (err) atomicOr(err, PM_ERR_TIMEOUT);
             return false;
@@ -334,25 +348,32 @@ __device__ __forceinline__ float pm_warp_sum(float v) {
     return v;
 }
 
-/* glu (cu:124-162 pulsar_glu; elib:2134 glu): 0 silu, 1 gelu-tanh,
+/* e^x rounded to binary32 from the binary64 exponential (correctly rounded
+ * but for rare double-rounding cases), so the glu matches the CPU lane's
+ * f32 expf (glibc, within 0.502 ulp) bit for bit in all but rare inputs */
+__device__ __forceinline__ float pm_exp_f32(float x) { return (float)exp((double)x); }
+
+/* crates/engine/src/lib.rs:2134-2159 glu (cu:124 pulsar_glu) in the CPU
+ * lane's f32 operation order, without contraction: 0 silu, 1 gelu tanh,
  * 2 swiglu_oai, 3 clamped silu, 4 SiTU-GLU */
 __device__ __forceinline__ float pm_glu(float g, float u, uint32_t op) {
     if (op == 2u) {
         g = fminf(g, 7.0f);
         u = fminf(fmaxf(u, -7.0f), 7.0f);
-        return g / (1.0f + expf(-1.702f * g)) * (u + 1.0f);
+        const float e = pm_exp_f32(__fmul_rn(-1.702f, g));
+        return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), __fadd_rn(u, 1.0f));
     }
     if (op == 3u) {
         g = fminf(g, 10.0f);
         u = fminf(fmaxf(u, -10.0f), 10.0f);
-        return g / (1.0f + expf(-g)) * u;
+        return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, pm_exp_f32(-g))), u);
     }
     if (op == 4u) {
-        const float a = 4.0f * tanhf(g / 4.0f) / (1.0f + expf(-g));
+        const float a = 4.0f * tanhf(g / 4.0f) / (1.0f + pm_exp_f32(-g));
         return a * (25.0f * tanhf(u / 25.0f));
     }
     if (op == 1u) return 0.5f * g * (1.0f + tanhf(0.7978846f * (g + 0.044715f * g * g * g))) * u;
-    return g / (1.0f + expf(-g)) * u;
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, pm_exp_f32(-g))), u);
 }
 
 /* One warp quantizes one 256-value q8_K block exactly like the CPU lane

@@ -329,34 +329,6 @@ __device__ __forceinline__ float pm_pair_dot(const pm_wp &w, const uint4 &A, con
     }
 }
 
-/* ------------------------------------------------------ reduce-scatter */
-
-/* Halving exchange across the LPR lanes of a row: at each step a lane
- * keeps one half of its values (chosen by one lane-index bit) and adds
- * the partner's copy of that half.  idx returns the original index of
- * v[0]; afterwards a lane holds max(V / LPR, 1) consecutive totals. */
-template <int V, int LPR, int S = 0>
-struct pm_rs {
-    static __device__ __forceinline__ void run(float *v, uint32_t lane, int &idx) {
-        constexpr int Vc = V >> S, H = Vc / 2, O = LPR >> (S + 1);
-        if constexpr (Vc > 1 && O >= 1) {
-            const bool bit = (lane & (uint32_t)O) != 0;
-#pragma unroll
-            for (int i = 0; i < H; i++) {
-                const float send = bit ? v[i] : v[i + H];
-                const float keep = bit ? v[i + H] : v[i];
-                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
-            }
-            if (bit) idx += H;
-            pm_rs<V, LPR, S + 1>::run(v, lane, idx);
-        } else if constexpr (Vc == 1) {
-            /* one value left: finish the sum over the remaining lane bits */
-#pragma unroll
-            for (int o = O; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-        }
-    }
-};
-
 /* ------------------------------------------------------ one stage */
 
 /* what stays fixed over a segment (one work unit's rows); the stage's row
@@ -370,78 +342,200 @@ struct pm_rowjob {
     float *out;
     const float *b0, *b1; /* gate / up bias rows of the expert (or null) */
     const float *wts;     /* route weight per pair */
+    float *terms;         /* this warp's [PM_TERM_V][PM_TERM_P] super-block terms */
 };
 
-/* EPI 0: gate/up -> mid = glu(g + bg, u + bu) * w;  EPI 1: down -> partial */
+#define PM_TERM_V 16u /* NMAT * tokens */
+#define PM_TERM_P 33u /* 32 lanes + 1 (bank skew) */
+
+/* one unit pair's integer (or per-32-block float) contribution to the
+ * super-block accumulators of one token, in the CPU lane's arithmetic:
+ *   Q4_K   ia += 16 (sc0 S0 + sc1 S1)     ib += m0 B0 + m1 B1
+ *   Q2_K   ia += sum sc16 S16              ib += sum m16 B16
+ *   IQ2    ia += ls0 S0 + ls1 S1
+ *   MXFP4  fa += d0 S0 (+ d1 S1)           (block order, no contraction)
+ *   Q8_0   fa += d0 S0 (+ d1 S1), blocks whose integer sum is 0 skipped */
+template <int Q>
+__device__ __forceinline__ void pm_pair_acc(const pm_wp &w, const uint4 &A, const uint4 &B, const uint4 &C,
+                                            const uint4 &D, const int4 &bs, bool two, int32_t &ia, int32_t &ib,
+                                            float &fa) {
+    int c0, c1;
+    if constexpr (Q == PM_QUANT_Q4_K) {
+        c0 = pm_dp4a_us(w.w0[0], (int)A.x, 0);
+        c1 = pm_dp4a_us(w.w1[0], (int)C.x, 0);
+        c0 = pm_dp4a_us(w.w0[1], (int)A.y, c0);
+        c1 = pm_dp4a_us(w.w1[1], (int)C.y, c1);
+        c0 = pm_dp4a_us(w.w0[2], (int)A.z, c0);
+        c1 = pm_dp4a_us(w.w1[2], (int)C.z, c1);
+        c0 = pm_dp4a_us(w.w0[3], (int)A.w, c0);
+        c1 = pm_dp4a_us(w.w1[3], (int)C.w, c1);
+        c0 = pm_dp4a_us(w.w0[4], (int)B.x, c0);
+        c1 = pm_dp4a_us(w.w1[4], (int)D.x, c1);
+        c0 = pm_dp4a_us(w.w0[5], (int)B.y, c0);
+        c1 = pm_dp4a_us(w.w1[5], (int)D.y, c1);
+        c0 = pm_dp4a_us(w.w0[6], (int)B.z, c0);
+        c1 = pm_dp4a_us(w.w1[6], (int)D.z, c1);
+        c0 = pm_dp4a_us(w.w0[7], (int)B.w, c0);
+        c1 = pm_dp4a_us(w.w1[7], (int)D.w, c1);
+    } else {
+        c0 = __dp4a((int)w.w0[0], (int)A.x, 0);
+        c1 = __dp4a((int)w.w1[0], (int)C.x, 0);
+        c0 = __dp4a((int)w.w0[1], (int)A.y, c0);
+        c1 = __dp4a((int)w.w1[1], (int)C.y, c1);
+        c0 = __dp4a((int)w.w0[2], (int)A.z, c0);
+        c1 = __dp4a((int)w.w1[2], (int)C.z, c1);
+        c0 = __dp4a((int)w.w0[3], (int)A.w, c0);
+        c1 = __dp4a((int)w.w1[3], (int)C.w, c1);
+        c0 = __dp4a((int)w.w0[4], (int)B.x, c0);
+        c1 = __dp4a((int)w.w1[4], (int)D.x, c1);
+        c0 = __dp4a((int)w.w0[5], (int)B.y, c0);
+        c1 = __dp4a((int)w.w1[5], (int)D.y, c1);
+        c0 = __dp4a((int)w.w0[6], (int)B.z, c0);
+        c1 = __dp4a((int)w.w1[6], (int)D.z, c1);
+        c0 = __dp4a((int)w.w0[7], (int)B.w, c0);
+        c1 = __dp4a((int)w.w1[7], (int)D.w, c1);
+    }
+    if constexpr (Q == PM_QUANT_Q4_K) {
+        ia += w.i0 * c0 + w.i1 * c1;
+        ib += w.m0 * (bs.x + bs.y) + w.m1 * (bs.z + bs.w);
+    } else if constexpr (Q == PM_QUANT_Q2_K) {
+        ia += c0 + c1;
+        ib += w.m0 * bs.x + w.m1 * bs.y + w.m2 * bs.z + w.m3 * bs.w;
+    } else if constexpr (Q == PM_QUANT_IQ2_XXS) {
+        ia += w.i0 * c0 + w.i1 * c1;
+    } else if constexpr (Q == PM_QUANT_MXFP4) {
+        fa = __fadd_rn(fa, __fmul_rn(w.d, (float)c0));
+        if (two) fa = __fadd_rn(fa, __fmul_rn(w.dm, (float)c1));
+    } else {
+        if (c0 != 0) fa = __fadd_rn(fa, __fmul_rn(w.d, (float)c0));
+        if (two && c1 != 0) fa = __fadd_rn(fa, __fmul_rn(w.dm, (float)c1));
+    }
+}
+
+/* the super-block's term of the row's dot for one token, exactly as the
+ * CPU lane forms it (cpu_dot.rs:250-279 q4_K, :732-767 q2_K, :92-122
+ * iq2_xxs; MXFP4 cu:2053 / Q8_0 cu:2174 as the oracle restates them): the
+ * same f32 operations in the same order, no fused multiply-add */
+template <int Q>
+__device__ __forceinline__ float pm_sb_term(float d, float dm, float yd, int32_t ia, int32_t ib, float fa) {
+    if constexpr (Q == PM_QUANT_Q4_K) /* xd yd isum - xmin yd msum (d holds xd / 16, ia 16 isum) */
+        return __fsub_rn(__fmul_rn(__fmul_rn(d * 16.0f, yd), (float)(ia >> 4)), __fmul_rn(__fmul_rn(dm, yd), (float)ib));
+    else if constexpr (Q == PM_QUANT_Q2_K) /* yd xd isum - yd xmin summs */
+        return __fsub_rn(__fmul_rn(__fmul_rn(yd, d), (float)ia), __fmul_rn(__fmul_rn(yd, dm), (float)ib));
+    else if constexpr (Q == PM_QUANT_IQ2_XXS) /* (0.125 xd) yd bsum (d holds 0.125 xd) */
+        return __fmul_rn(__fmul_rn(d, yd), (float)ia);
+    else /* yd sum over the blocks */
+        return __fmul_rn(yd, fa);
+}
+
+/* A stage's rows, each dot formed exactly as the CPU lane forms it.  LPR
+ * lanes share a row; lane l of a row takes super-blocks l, l + LPR, ...
+ * (its 4 unit pairs in order), so every super-block's integer sums are
+ * exact in one lane and its f32 term is the CPU lane's.  The terms then
+ * meet in shared memory, round by round (LPR super-blocks per round), and
+ * one lane per (row, token) adds them in super-block order - the CPU
+ * lane's sequential `total +=`.  EPI 0: gate/up -> mid = glu(g + bg,
+ * u + bu) * w;  EPI 1: down -> partial. */
 template <int Q, int NMAT, int NT, int LPR, int EPI>
 __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, const uint8_t *w1, uint32_t rows,
                                      uint32_t row_g) {
     constexpr int RPP = 32 / LPR;
-    constexpr int NTP = NT <= 1 ? 1 : (NT <= 2 ? 2 : (NT <= 4 ? 4 : 8));
-    constexpr int V = NMAT * NTP;
-    constexpr int K = V >= LPR ? V / LPR : 1;
+    constexpr int V = NMAT * NT;
     const uint32_t lane = threadIdx.x & 31u, sub = lane / LPR, sl = lane % LPR;
     const pm_acts &ac = jb.acts;
     const uint32_t P = ac.P;
+    const uint32_t nsb = (jb.npair + 3u) / 4u, rounds = (nsb + LPR - 1u) / LPR;
+    float *tm = jb.terms;
+    constexpr uint32_t JOBS = (uint32_t)(RPP * NT); /* (row of the pass, token) */
     for (uint32_t j0 = 0; j0 < rows; j0 += RPP) {
         const uint32_t j = j0 + sub;
         const bool rv = j < rows;
-        float v[V];
+        float acc[NMAT][(JOBS + 31) / 32];
 #pragma unroll
-        for (int i = 0; i < V; i++) v[i] = 0.0f;
-        if (rv) {
-            for (uint32_t p = sl; p < jb.npair; p += LPR) {
-                const bool two = 2u * p + 1u < jb.n_units;
-                pm_wp W[NMAT];
+        for (int m = 0; m < NMAT; m++)
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) pm_decode_pair<Q>((m == 0 ? w0 : w1) + (size_t)j * jb.rb, p, two, jb.grid, W[m]);
-                const uint32_t blk = p >> 2;
+            for (int q = 0; q < (int)((JOBS + 31) / 32); q++) acc[m][q] = 0.0f;
+        for (uint32_t rd = 0; rd < rounds; rd++) {
+            const uint32_t sb = rd * LPR + sl;
+            float term[V];
+#pragma unroll
+            for (int i = 0; i < V; i++) term[i] = 0.0f;
+            if (rv && sb < nsb) {
+                int32_t ia[V], ib[V];
+                float fa[V];
+#pragma unroll
+                for (int i = 0; i < V; i++) ia[i] = ib[i] = 0, fa[i] = 0.0f;
+                float dd[NMAT], dmm[NMAT];
+#pragma unroll 1
+                for (uint32_t p = 4u * sb; p < 4u * sb + 4u && p < jb.npair; p++) {
+                    const bool two = 2u * p + 1u < jb.n_units;
+                    pm_wp W[NMAT];
+#pragma unroll
+                    for (int m = 0; m < NMAT; m++) {
+                        pm_decode_pair<Q>((m == 0 ? w0 : w1) + (size_t)j * jb.rb, p, two, jb.grid, W[m]);
+                        dd[m] = W[m].d, dmm[m] = W[m].dm;
+                    }
+#pragma unroll
+                    for (int t = 0; t < NT; t++) {
+                        const uint4 A = ac.x[(0 * PM_TT + t) * P + p];
+                        const uint4 B = ac.x[(1 * PM_TT + t) * P + p];
+                        const uint4 C = ac.x[(2 * PM_TT + t) * P + p];
+                        const uint4 D = ac.x[(3 * PM_TT + t) * P + p];
+                        int4 bs = make_int4(0, 0, 0, 0);
+                        if constexpr (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bs = ac.bs[t * P + p];
+#pragma unroll
+                        for (int m = 0; m < NMAT; m++)
+                            pm_pair_acc<Q>(W[m], A, B, C, D, bs, two, ia[m * NT + t], ib[m * NT + t], fa[m * NT + t]);
+                        /* keep at most two tokens' activations live */
+                        if ((t & 1) == 1) asm volatile("" ::: "memory");
+                    }
+                }
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
-                    const uint4 A = ac.x[(0 * PM_TT + t) * P + p];
-                    const uint4 B = ac.x[(1 * PM_TT + t) * P + p];
-                    const uint4 C = ac.x[(2 * PM_TT + t) * P + p];
-                    const uint4 D = ac.x[(3 * PM_TT + t) * P + p];
-                    int4 bs = make_int4(0, 0, 0, 0);
-                    if constexpr (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bs = ac.bs[t * P + p];
-                    const float yd = ac.d[t * ac.NB + blk];
+                    const float yd = ac.d[t * ac.NB + sb];
 #pragma unroll
                     for (int m = 0; m < NMAT; m++)
-                        v[m * NTP + t] = fmaf(yd, pm_pair_dot<Q>(W[m], A, B, C, D, bs), v[m * NTP + t]);
-                    /* keep at most two tokens' activations live (no spills at NT = 8) */
-                    if ((t & 1) == 1) asm volatile("" ::: "memory");
+                        term[m * NT + t] = pm_sb_term<Q>(dd[m], dmm[m], yd, ia[m * NT + t], ib[m * NT + t],
+                                                         fa[m * NT + t]);
                 }
             }
-        }
-        int idx = 0;
-        pm_rs<V, LPR>::run(v, lane, idx);
-        /* lanes that hold a distinct total (the rest hold copies) */
-        const bool owner = V >= LPR || (sl & (uint32_t)(LPR / V - 1)) == 0;
-        if constexpr (NMAT == 2) {
-            /* the first exchange split gate | up: the partner lane holds up */
-            float u[K];
+            /* this round's terms: [v][lane] (skewed rows: conflict-free) */
 #pragma unroll
-            for (int i = 0; i < K; i++) u[i] = __shfl_xor_sync(0xffffffffu, v[i], LPR / 2);
-            if (rv && owner && idx < NTP) {
+            for (int i = 0; i < V; i++) tm[i * PM_TERM_P + lane] = term[i];
+            __syncwarp();
+            /* job lanes add the round's LPR terms in super-block order */
 #pragma unroll
-                for (int i = 0; i < K; i++) {
-                    const uint32_t t = (uint32_t)(idx + i);
-                    if (t < jb.nt) {
-                        const uint32_t row = row_g + j, pr = jb.tokpair[t];
-                        float g = v[i], up = u[i];
-                        if (jb.b0) g += jb.b0[row];
-                        if (jb.b1) up += jb.b1[row];
-                        jb.out[(size_t)pr * jb.ostride + row] = pm_glu(g, up, jb.act) * jb.wts[pr];
+            for (int q = 0; q < (int)((JOBS + 31) / 32); q++) {
+                const uint32_t jobi = lane + 32u * q;
+                if (jobi < JOBS) {
+                    const uint32_t jr = jobi / NT, jt = jobi % NT;
+                    const uint32_t nlim = nsb - rd * LPR < LPR ? nsb - rd * LPR : LPR;
+#pragma unroll
+                    for (int m = 0; m < NMAT; m++) {
+                        float a = acc[m][q];
+                        for (uint32_t l = 0; l < nlim; l++)
+                            a = __fadd_rn(a, tm[(m * NT + jt) * PM_TERM_P + jr * LPR + l]);
+                        acc[m][q] = a;
                     }
                 }
             }
-        } else {
-            if (rv && owner) {
+            __syncwarp();
+        }
+        /* outputs: one lane per (row, token) */
 #pragma unroll
-                for (int i = 0; i < K; i++) {
-                    const uint32_t t = (uint32_t)(idx + i);
-                    if (t < jb.nt) jb.out[(size_t)jb.tokpair[t] * jb.ostride + row_g + j] = v[i];
-                }
+        for (int q = 0; q < (int)((JOBS + 31) / 32); q++) {
+            const uint32_t jobi = lane + 32u * q;
+            if (jobi >= JOBS) continue;
+            const uint32_t jr = jobi / NT, jt = jobi % NT, jj = j0 + jr;
+            if (jj >= rows || jt >= jb.nt) continue;
+            const uint32_t row = row_g + jj, pr = jb.tokpair[jt];
+            if constexpr (NMAT == 2) {
+                float g = acc[0][q], up = acc[1][q];
+                if (jb.b0) g = __fadd_rn(g, jb.b0[row]);
+                if (jb.b1) up = __fadd_rn(up, jb.b1[row]);
+                jb.out[(size_t)pr * jb.ostride + row] = __fmul_rn(pm_glu(g, up, jb.act), jb.wts[pr]);
+            } else {
+                jb.out[(size_t)pr * jb.ostride + row] = acc[0][q];
             }
         }
     }
@@ -464,12 +558,13 @@ __device__ __forceinline__ void pm_rows_nt(const pm_rowjob &jb, const uint8_t *w
 template <int Q, int NMAT, int EPI>
 __device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, uint32_t lpr, const uint8_t *w0, const uint8_t *w1,
                                             uint32_t rows, uint32_t row_g) {
-    if (lpr == 16u)
-        pm_rows_nt<Q, NMAT, 16, EPI>(jb, w0, w1, rows, row_g);
-    else if (lpr == 32u)
-        pm_rows_nt<Q, NMAT, 32, EPI>(jb, w0, w1, rows, row_g);
-    else
-        pm_rows_nt<Q, NMAT, 4, EPI>(jb, w0, w1, rows, row_g);
+    switch (lpr) {
+    case 2: pm_rows_nt<Q, NMAT, 2, EPI>(jb, w0, w1, rows, row_g); break;
+    case 4: pm_rows_nt<Q, NMAT, 4, EPI>(jb, w0, w1, rows, row_g); break;
+    case 8: pm_rows_nt<Q, NMAT, 8, EPI>(jb, w0, w1, rows, row_g); break;
+    case 16: pm_rows_nt<Q, NMAT, 16, EPI>(jb, w0, w1, rows, row_g); break;
+    default: pm_rows_nt<Q, NMAT, 32, EPI>(jb, w0, w1, rows, row_g); break;
+    }
 }
 
 /* ------------------------------------------------------ stage copies */
@@ -518,7 +613,7 @@ struct pm_skind {
     uint64_t rb;      /* row bytes */
     uint32_t n_units; /* 32-value units per row */
     uint32_t npair;
-    uint32_t lpr;     /* lanes per row: 4, 16 or 32 */
+    uint32_t lpr;     /* lanes per row: 2, 4, 8, 16 or 32 (super-block slots) */
     uint32_t rw;      /* rows per stage */
     uint32_t direct;  /* 1: rows too large for the per-warp rings, read straight from global memory */
 };
@@ -529,7 +624,7 @@ struct pm_skp {
     uint32_t S;      /* ring stages per warp */
     uint32_t stage;  /* bytes per stage */
     uint32_t P, NB;  /* activation tile geometry (max over kinds) */
-    uint32_t off_bar, off_seg, off_acts, off_ring, smem;
+    uint32_t off_bar, off_seg, off_acts, off_terms, off_ring, smem;
 };
 
 /* one segment of a CTA's slice: rows [r0, r1) of one work unit */

@@ -394,6 +394,7 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
         jb.b0 = s.b0;
         jb.b1 = s.b1;
         jb.wts = a.w;
+        jb.terms = (float *)(smem + P.off_terms) + warp * (PM_TERM_V * PM_TERM_P);
         const uint32_t bytes_row = (uint32_t)kd.rb;
         if (kd.direct) { /* rows straight from global memory, no ring stage */
             while (itc.k == k) {
@@ -900,14 +901,19 @@ static pm_skind pm_kind_for(uint32_t nmat, uint64_t rb, uint32_t n) {
     k.rb = rb;
     k.n_units = (n + 31u) / 32u;
     k.npair = (k.n_units + 1u) / 2u;
-    k.lpr = k.npair >= 32u ? 16u : 4u;
+    /* lanes per row: the super-block slots of a row (a power of two up to
+     * 16, at least 2) */
+    const uint32_t nsb = (k.npair + 3u) / 4u;
+    k.lpr = 2u;
+    while (k.lpr * 2u <= nsb && k.lpr < 16u) k.lpr *= 2u;
     k.rw = pm_kind_rw(nmat, rb, 32u / k.lpr);
     k.direct = 0;
     return k;
 }
 
-/* shared-memory layout: IQ2 grid | segment table | token tile | mbarriers
- * | per-warp rings; ring depth from a ~110 KB budget (two CTAs per SM) */
+/* shared-memory layout: IQ2 grid | segment table | token tile | per-warp
+ * super-block terms | mbarriers | per-warp rings; ring depth from the
+ * budget of the CTAs per SM the kernel is built for */
 static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bool grid) {
     pm_skp P;
     P.k[0] = r;
@@ -922,6 +928,8 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
     off += PM_SK_MAXSEG * (uint32_t)sizeof(pm_segi);
     P.off_acts = (off + 15u) & ~15u;
     off = P.off_acts + pm_acts_bytes(P.P, P.NB);
+    P.off_terms = (off + 15u) & ~15u;
+    off = P.off_terms + W * PM_TERM_V * PM_TERM_P * 4u;
     P.off_bar = (off + 15u) & ~15u;
     P.off_ring = (P.off_bar + W * 8u * 8u + 127u) & ~127u;
     /* a kind whose two-deep rings do not fit next to the token tile takes a
@@ -934,7 +942,7 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
             const uint32_t sti = (pm_stage_bytes(nmat, kk.rb, kk.rw) + 15u) & ~15u;
             return (uint64_t)P.off_ring + (uint64_t)W * 2u * sti <= budget;
         };
-        if (!fits(k) && k.lpr == 16u) {
+        if (!fits(k) && k.lpr < 32u) {
             k.lpr = 32u;
             k.rw = pm_kind_rw(nmat, k.rb, 1u);
         }

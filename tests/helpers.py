@@ -175,7 +175,7 @@ class DeviceMirror:
                                    n_group=self.n_group, topk_group=self.topk_group)
         return lg, sel, w
 
-    def oracle_ffn(self, x, sel, w, with_shared=True):
+    def oracle_ffn(self, x, sel, w, with_shared=True, return_mid=False):
         T = x.shape[0]
         ns = 1 if (self.shared is not None and with_shared) else 0
         slots, ws = [], np.zeros((T, self.k + ns), np.float32)
@@ -198,7 +198,7 @@ class DeviceMirror:
             s = self.shared
             sh = (s["F"], s["quant"], s["rb_gu"], s["rb_dn"])
         return orc.moe_ffn(x, slots, ws, self.H, self.k, (self.F, self.quant, self.rb_gu, self.rb_dn), sh,
-                           act_op=self.act_op)
+                           act_op=self.act_op, return_mid=return_mid)
 
 
 def reader(ws):

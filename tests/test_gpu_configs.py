@@ -17,6 +17,11 @@ Checked per case:
     selftest bound 5e-3 max(|ref|, 1) (cu:6389): a different f32 summation
     order moves a few mid values across a q8_K rounding boundary, and one
     such step moves every output row of the token by ~5e-4.
+On the dp4a path (no tensor-core tiles) every dot is formed in the CPU
+lane's order, so the mid rows (glu * route weight) match the oracle's bit
+for bit; the test allows a handful of 1-ulp differences per million values,
+from the rare inputs where the CPU's f32 expf and the binary64 exponential
+rounded to f32 differ.
 C3 at 2048 tokens also checks the dequantized weights of the tensor-core
 path: the MXFP4 weight images hold the oracle's f32 dequant exactly, with
 no lo part.
@@ -77,13 +82,25 @@ def test_config_true_shape(oracle, name, T):
     xq_ref = oracle.quantize_q8k(x).reshape(-1)
     assert np.array_equal(rd(v.xq, xq_ref.size, np.uint8), xq_ref), "q8_K of x"
     idx = np.arange(T) if T <= 256 else np.sort(rng.choice(T, SUBSET, replace=False))
-    ref = M.oracle_ffn(x[idx], sel[idx], w[idx])
+    ref, ref_mid = M.oracle_ffn(x[idx], sel[idx], w[idx], return_mid=True)
     d = got[idx] - resid[idx]
     err = rel_l2(d, ref)
     print(f"{name} T={T}: rel_l2 {err:.3e}")
     assert err < TOL, (name, T, err)
     tiles = int(rd(v.n_items, 5, np.uint32)[4])
     assert ref_close(d, ref, rel=5e-3 if tiles else 1e-3), (name, T, tiles)
+    if not tiles:  # dp4a path: mid rows in the CPU lane's arithmetic
+        ns, fm = v.n_slot, v.f_max
+        mid = rd(v.mid, T * ns * fm, np.float32).reshape(T, ns, fm)[idx]
+        diff = 0
+        for s in range(ns):
+            F = M.F if s < M.k else M.shared["F"]
+            a, b = mid[:, s, :F], ref_mid[:, s, :F]
+            diff += int(np.count_nonzero(a.view(np.uint32) != b.view(np.uint32)))
+            assert np.all(np.abs(a.astype(np.float64) - b) <= np.abs(b) * 2.0 ** -23 + 1e-38), (name, T, s)
+        total = len(idx) * ns * M.F
+        print(f"{name} T={T}: mid bits differ in {diff} of {total}")
+        assert diff <= max(2, total // 100_000), (name, T, diff)
     if name == "C3" and T == 2048:
         check_mxfp4_images(M, rd, v)
 

@@ -25,7 +25,7 @@ TOL = 1e-3
 
 
 def test_wait_limit_reports_timeout_and_recovers(oracle):
-    L = HostLayer(H=2048, F=512, E=64, k=8, quant=2, seed=41, router_mode=0, zipf=(1.1, "select"), shared=(2, 512))
+    L = HostLayer(H=1024, F=512, E=32, k=8, quant=2, seed=41, router_mode=0, zipf=(1.1, "select"), shared=(2, 512))
     T = 64
     x = np.random.default_rng(8).normal(0, 1, (T, L.H)).astype(np.float32)
     _, sel, w = L.oracle_route(x)
