@@ -276,6 +276,14 @@ int pulsar_quantize_rows(void *out, const void *x, const void *qw, uint32_t quan
                          void *stream);
 uint64_t pulsar_row_bytes(uint32_t quant, uint32_t n);
 
+/* Failure-detection check of the kernels' bounded device wait: one thread
+ * waits on an mbarrier phase that nothing completes, with a limit of
+ * `cycles` SM cycles (1 .. 2^31); the wait runs out, the kernel records the
+ * timeout and returns.  Returns the error word (1 = timeout recorded, the
+ * expected result), 0xffffffff on a launch error.  Synchronous; allocates
+ * 4 bytes of device memory for the word. */
+uint32_t pulsar_wait_selftest(uint64_t cycles);
+
 /* reads and clears the error word of the Part-1 kernels (synchronous) */
 uint32_t pulsar_b200_abi_error(void);
 

@@ -66,8 +66,13 @@ struct pm_acts {
     uint4 *x;
     int4 *bs;
     float *d;
-    uint32_t P, NB;
+    uint32_t P, NB; /* P: pair slots per token, a multiple of 4 */
 };
+
+/* slot of unit pair p in a token's planes: pair j of super-block b sits at
+ * j * (P / 4) + b, so the lanes of a row, which take consecutive
+ * super-blocks, read consecutive 16-byte slots (no bank conflicts) */
+__host__ __device__ __forceinline__ uint32_t pm_pslot(uint32_t p, uint32_t P) { return (p & 3u) * (P >> 2) + (p >> 2); }
 
 __host__ __device__ __forceinline__ uint32_t pm_acts_bytes(uint32_t P, uint32_t NB) {
     return PM_TT * (P * 80u + NB * 4u) + 64u;
@@ -93,13 +98,13 @@ __device__ __forceinline__ void pm_acts_stage_q8(const pm_acts &a, uint32_t nt, 
         const uint32_t u = wd >> 3, k = wd & 7u;
         const int32_t v = __ldcg((const int32_t *)((const uint8_t *)(rows[t] + (u >> 3)) + 4 + 32 * (u & 7u)) + k);
         const uint32_t plane = 2u * (u & 1u) + (k >> 2);
-        ((int32_t *)(a.x + (plane * PM_TT + t) * a.P + (u >> 1)))[k & 3u] = v;
+        ((int32_t *)(a.x + (plane * PM_TT + t) * a.P + pm_pslot(u >> 1, a.P)))[k & 3u] = v;
     }
     for (uint32_t i = threadIdx.x; i < nt * n_units; i += blockDim.x) {
         const uint32_t t = i / n_units, u = i % n_units;
         const pm_block_q8K *blk = rows[t] + (u >> 3);
         const uint32_t w = (uint32_t)__ldcg((const int32_t *)((const uint8_t *)blk + 260 + 4 * (u & 7u)));
-        int32_t *dst = (int32_t *)(a.bs + t * a.P + (u >> 1)) + 2u * (u & 1u);
+        int32_t *dst = (int32_t *)(a.bs + t * a.P + pm_pslot(u >> 1, a.P)) + 2u * (u & 1u);
         dst[0] = (int32_t)(int16_t)(w & 0xffffu);
         dst[1] = (int32_t)(int16_t)(w >> 16);
         if ((u & 7u) == 0) a.d[t * a.NB + (u >> 3)] = __ldcg(&blk->d);
@@ -145,11 +150,11 @@ __device__ __forceinline__ void pm_acts_stage_f32(const pm_acts &a, uint32_t nt,
         if (u < n_units) {
             const uint32_t q = lane & 3u; /* quarter of the unit */
             const uint32_t plane = 2u * (u & 1u) + (q >> 1);
-            uint32_t *dst = (uint32_t *)(a.x + (plane * PM_TT + t) * a.P + (u >> 1)) + 2u * (q & 1u);
+            uint32_t *dst = (uint32_t *)(a.x + (plane * PM_TT + t) * a.P + pm_pslot(u >> 1, a.P)) + 2u * (q & 1u);
             dst[0] = qv[0] | (qv[1] << 8) | (qv[2] << 16) | (qv[3] << 24);
             dst[1] = qv[4] | (qv[5] << 8) | (qv[6] << 16) | (qv[7] << 24);
             if (q == 0) {
-                int32_t *bd = (int32_t *)(a.bs + t * a.P + (u >> 1)) + 2u * (u & 1u);
+                int32_t *bd = (int32_t *)(a.bs + t * a.P + pm_pslot(u >> 1, a.P)) + 2u * (u & 1u);
                 bd[0] = s;
                 bd[1] = s_hi;
             }
@@ -457,15 +462,15 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, con
             for (int q = 0; q < (int)((JOBS + 31) / 32); q++) acc[m][q] = 0.0f;
         for (uint32_t rd = 0; rd < rounds; rd++) {
             const uint32_t sb = rd * LPR + sl;
-            float term[V];
+            const bool live = rv && sb < nsb;
+            int32_t ia[V], ib[V];
+            float fa[V];
 #pragma unroll
-            for (int i = 0; i < V; i++) term[i] = 0.0f;
-            if (rv && sb < nsb) {
-                int32_t ia[V], ib[V];
-                float fa[V];
+            for (int i = 0; i < V; i++) ia[i] = ib[i] = 0, fa[i] = 0.0f;
+            float dd[NMAT], dmm[NMAT];
 #pragma unroll
-                for (int i = 0; i < V; i++) ia[i] = ib[i] = 0, fa[i] = 0.0f;
-                float dd[NMAT], dmm[NMAT];
+            for (int m = 0; m < NMAT; m++) dd[m] = dmm[m] = 0.0f;
+            if (live) {
 #pragma unroll 1
                 for (uint32_t p = 4u * sb; p < 4u * sb + 4u && p < jb.npair; p++) {
                     const bool two = 2u * p + 1u < jb.n_units;
@@ -475,14 +480,15 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, con
                         pm_decode_pair<Q>((m == 0 ? w0 : w1) + (size_t)j * jb.rb, p, two, jb.grid, W[m]);
                         dd[m] = W[m].d, dmm[m] = W[m].dm;
                     }
+                    const uint32_t ps = pm_pslot(p, P);
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
-                        const uint4 A = ac.x[(0 * PM_TT + t) * P + p];
-                        const uint4 B = ac.x[(1 * PM_TT + t) * P + p];
-                        const uint4 C = ac.x[(2 * PM_TT + t) * P + p];
-                        const uint4 D = ac.x[(3 * PM_TT + t) * P + p];
+                        const uint4 A = ac.x[(0 * PM_TT + t) * P + ps];
+                        const uint4 B = ac.x[(1 * PM_TT + t) * P + ps];
+                        const uint4 C = ac.x[(2 * PM_TT + t) * P + ps];
+                        const uint4 D = ac.x[(3 * PM_TT + t) * P + ps];
                         int4 bs = make_int4(0, 0, 0, 0);
-                        if constexpr (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bs = ac.bs[t * P + p];
+                        if constexpr (Q == PM_QUANT_Q4_K || Q == PM_QUANT_Q2_K) bs = ac.bs[t * P + ps];
 #pragma unroll
                         for (int m = 0; m < NMAT; m++)
                             pm_pair_acc<Q>(W[m], A, B, C, D, bs, two, ia[m * NT + t], ib[m * NT + t], fa[m * NT + t]);
@@ -490,18 +496,17 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, con
                         if ((t & 1) == 1) asm volatile("" ::: "memory");
                     }
                 }
-#pragma unroll
-                for (int t = 0; t < NT; t++) {
-                    const float yd = ac.d[t * ac.NB + sb];
-#pragma unroll
-                    for (int m = 0; m < NMAT; m++)
-                        term[m * NT + t] = pm_sb_term<Q>(dd[m], dmm[m], yd, ia[m * NT + t], ib[m * NT + t],
-                                                         fa[m * NT + t]);
-                }
             }
-            /* this round's terms: [v][lane] (skewed rows: conflict-free) */
+            /* this round's terms, [v][lane] (skewed rows: conflict-free);
+             * lanes without a super-block this round write zeros (never read) */
 #pragma unroll
-            for (int i = 0; i < V; i++) tm[i * PM_TERM_P + lane] = term[i];
+            for (int t = 0; t < NT; t++) {
+                const float yd = live ? ac.d[t * ac.NB + sb] : 0.0f;
+#pragma unroll
+                for (int m = 0; m < NMAT; m++)
+                    tm[(m * NT + t) * PM_TERM_P + lane] =
+                        pm_sb_term<Q>(dd[m], dmm[m], yd, ia[m * NT + t], ib[m * NT + t], fa[m * NT + t]);
+            }
             __syncwarp();
             /* job lanes add the round's LPR terms in super-block order */
 #pragma unroll

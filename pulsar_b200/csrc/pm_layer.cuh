@@ -920,7 +920,7 @@ static pm_skp pm_skp_for(uint32_t nmat, const pm_skind &r, const pm_skind &s, bo
     P.k[1] = s;
     const uint32_t W = (uint32_t)pm_sk_warps((int)nmat);
     const uint32_t budget = pm_sk_minb(nmat) == 1 ? 200u * 1024u : 110u * 1024u;
-    P.P = r.npair > s.npair ? r.npair : s.npair;
+    P.P = ((r.npair > s.npair ? r.npair : s.npair) + 3u) & ~3u; /* pair slots: whole super-blocks */
     const uint32_t nb0 = (r.n_units + 7u) / 8u, nb1 = (s.n_units + 7u) / 8u;
     P.NB = nb0 > nb1 ? nb0 : nb1;
     uint32_t off = grid ? 2048u : 0u;

@@ -279,3 +279,33 @@ extern "C" int pulsar_moe_selftest(void) {
            st_moe_one(PM_QUANT_IQ2_XXS, 512, 256, 0) && st_moe_one(PM_QUANT_MXFP4, 704, 704, 2) &&
            st_moe_one(PM_QUANT_Q8_0, 704, 512, 0);
 }
+
+/* ------------------------------------------------- bounded-wait check */
+
+#include "pm_device.cuh"
+
+/* One thread waits, with the kernels' bounded wait, on an mbarrier phase
+ * that nothing completes (count 1, no arrival): the wait runs out after
+ * `cycles` SM cycles, records PM_ERR_TIMEOUT in the error word and
+ * returns.  No copy is in flight and nothing is left waiting. */
+__global__ void pm_wait_selftest_kernel(uint32_t *err, long long cycles) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    pm_mbar_init(&bar, 1);
+    pm_fence_barrier_init();
+    const bool ok = pm_mbar_wait_sleep(&bar, 0, err, cycles);
+    if (ok) atomicOr(err, 0x80000000u); /* completed: must not happen */
+}
+
+extern "C" uint32_t pulsar_wait_selftest(uint64_t cycles) {
+    if (cycles == 0 || cycles > (1ull << 31)) return 0xffffffffu;
+    uint32_t *err = nullptr, host = 0xffffffffu;
+    if (!pm_ok(cudaMalloc(&err, 4), "wait selftest alloc")) return 0xffffffffu;
+    if (pm_ok(cudaMemset(err, 0, 4), "wait selftest clear")) {
+        pm_wait_selftest_kernel<<<1, 32>>>(err, (long long)cycles);
+        if (pm_ok(cudaGetLastError(), "wait selftest launch") && pm_ok(cudaDeviceSynchronize(), "wait selftest"))
+            cudaMemcpy(&host, err, 4, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(err);
+    return host;
+}
