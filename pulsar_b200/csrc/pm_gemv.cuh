@@ -347,7 +347,6 @@ struct pm_rowjob {
     float *out;
     const float *b0, *b1; /* gate / up bias rows of the expert (or null) */
     const float *wts;     /* route weight per pair */
-    float *terms;         /* this warp's [PM_TERM_V][PM_TERM_P] super-block terms */
 };
 
 #define PM_TERM_V 16u /* NMAT * tokens */
@@ -442,15 +441,14 @@ __device__ __forceinline__ float pm_sb_term(float d, float dm, float yd, int32_t
  * lane's sequential `total +=`.  EPI 0: gate/up -> mid = glu(g + bg,
  * u + bu) * w;  EPI 1: down -> partial. */
 template <int Q, int NMAT, int NT, int LPR, int EPI>
-__device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, const uint8_t *w1, uint32_t rows,
-                                     uint32_t row_g) {
+__device__ __noinline__ void pm_rows(const pm_rowjob &jb, float *tm, const uint8_t *w0, const uint8_t *w1,
+                                     uint32_t rows, uint32_t row_g) {
     constexpr int RPP = 32 / LPR;
     constexpr int V = NMAT * NT;
     const uint32_t lane = threadIdx.x & 31u, sub = lane / LPR, sl = lane % LPR;
     const pm_acts &ac = jb.acts;
     const uint32_t P = ac.P;
     const uint32_t nsb = (jb.npair + 3u) / 4u, rounds = (nsb + LPR - 1u) / LPR;
-    float *tm = jb.terms;
     constexpr uint32_t JOBS = (uint32_t)(RPP * NT); /* (row of the pass, token) */
     for (uint32_t j0 = 0; j0 < rows; j0 += RPP) {
         const uint32_t j = j0 + sub;
@@ -471,7 +469,7 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, con
 #pragma unroll
             for (int m = 0; m < NMAT; m++) dd[m] = dmm[m] = 0.0f;
             if (live) {
-#pragma unroll 1
+#pragma unroll 2
                 for (uint32_t p = 4u * sb; p < 4u * sb + 4u && p < jb.npair; p++) {
                     const bool two = 2u * p + 1u < jb.n_units;
                     pm_wp W[NMAT];
@@ -517,9 +515,14 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, con
                     const uint32_t nlim = nsb - rd * LPR < LPR ? nsb - rd * LPR : LPR;
 #pragma unroll
                     for (int m = 0; m < NMAT; m++) {
+                        const float *src = tm + (m * NT + jt) * PM_TERM_P + jr * LPR;
+                        float tv[LPR];
+#pragma unroll
+                        for (int l = 0; l < LPR; l++) tv[l] = src[l]; /* all loads first, then the ordered adds */
                         float a = acc[m][q];
-                        for (uint32_t l = 0; l < nlim; l++)
-                            a = __fadd_rn(a, tm[(m * NT + jt) * PM_TERM_P + jr * LPR + l]);
+#pragma unroll
+                        for (int l = 0; l < LPR; l++)
+                            if ((uint32_t)l < nlim) a = __fadd_rn(a, tv[l]);
                         acc[m][q] = a;
                     }
                 }
@@ -547,28 +550,28 @@ __device__ __noinline__ void pm_rows(const pm_rowjob &jb, const uint8_t *w0, con
 }
 
 template <int Q, int NMAT, int LPR, int EPI>
-__device__ __forceinline__ void pm_rows_nt(const pm_rowjob &jb, const uint8_t *w0, const uint8_t *w1, uint32_t rows,
-                                           uint32_t row_g) {
+__device__ __forceinline__ void pm_rows_nt(const pm_rowjob &jb, float *tm, const uint8_t *w0, const uint8_t *w1,
+                                           uint32_t rows, uint32_t row_g) {
     switch (jb.nt) {
-    case 1: pm_rows<Q, NMAT, 1, LPR, EPI>(jb, w0, w1, rows, row_g); break;
-    case 2: pm_rows<Q, NMAT, 2, LPR, EPI>(jb, w0, w1, rows, row_g); break;
-    case 3: pm_rows<Q, NMAT, 3, LPR, EPI>(jb, w0, w1, rows, row_g); break;
-    case 4: pm_rows<Q, NMAT, 4, LPR, EPI>(jb, w0, w1, rows, row_g); break;
+    case 1: pm_rows<Q, NMAT, 1, LPR, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    case 2: pm_rows<Q, NMAT, 2, LPR, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    case 3: pm_rows<Q, NMAT, 3, LPR, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    case 4: pm_rows<Q, NMAT, 4, LPR, EPI>(jb, tm, w0, w1, rows, row_g); break;
     case 5:
-    case 6: pm_rows<Q, NMAT, 6, LPR, EPI>(jb, w0, w1, rows, row_g); break;
-    default: pm_rows<Q, NMAT, 8, LPR, EPI>(jb, w0, w1, rows, row_g); break;
+    case 6: pm_rows<Q, NMAT, 6, LPR, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    default: pm_rows<Q, NMAT, 8, LPR, EPI>(jb, tm, w0, w1, rows, row_g); break;
     }
 }
 
 template <int Q, int NMAT, int EPI>
-__device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, uint32_t lpr, const uint8_t *w0, const uint8_t *w1,
-                                            uint32_t rows, uint32_t row_g) {
+__device__ __forceinline__ void pm_rows_any(const pm_rowjob &jb, float *tm, uint32_t lpr, const uint8_t *w0,
+                                            const uint8_t *w1, uint32_t rows, uint32_t row_g) {
     switch (lpr) {
-    case 2: pm_rows_nt<Q, NMAT, 2, EPI>(jb, w0, w1, rows, row_g); break;
-    case 4: pm_rows_nt<Q, NMAT, 4, EPI>(jb, w0, w1, rows, row_g); break;
-    case 8: pm_rows_nt<Q, NMAT, 8, EPI>(jb, w0, w1, rows, row_g); break;
-    case 16: pm_rows_nt<Q, NMAT, 16, EPI>(jb, w0, w1, rows, row_g); break;
-    default: pm_rows_nt<Q, NMAT, 32, EPI>(jb, w0, w1, rows, row_g); break;
+    case 2: pm_rows_nt<Q, NMAT, 2, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    case 4: pm_rows_nt<Q, NMAT, 4, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    case 8: pm_rows_nt<Q, NMAT, 8, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    case 16: pm_rows_nt<Q, NMAT, 16, EPI>(jb, tm, w0, w1, rows, row_g); break;
+    default: pm_rows_nt<Q, NMAT, 32, EPI>(jb, tm, w0, w1, rows, row_g); break;
     }
 }
 

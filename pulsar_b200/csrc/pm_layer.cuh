@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
     pm_layer_sk_kernel(const __grid_constant__ pm_layer_args a, const __grid_constant__ pm_skp P) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint32_t s_cnt[2], s_lim[4], s_tok[PM_TT];
+    __shared__ pm_rowjob s_jb;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint64_t *grid = pm_grid_fill(smem, QR == PM_QUANT_IQ2_XXS || QS == PM_QUANT_IQ2_XXS);
     uint64_t *bars = (uint64_t *)(smem + P.off_bar) + warp * P.S;
@@ -378,23 +379,24 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
             pm_acts_stage_f32(acts, s.nt, rows, s.kind == 0 ? a.Fr : a.Fs);
         }
         if (tid < s.nt) s_tok[tid] = __ldcg(s.pairs + tid);
+        if (tid == 0) { /* the segment's fixed job fields, in shared memory (read by every warp) */
+            s_jb.rb = kd.rb;
+            s_jb.npair = kd.npair;
+            s_jb.n_units = kd.n_units;
+            s_jb.nt = s.nt;
+            s_jb.act = a.act;
+            s_jb.ostride = EPI == 0 ? a.Fmax : a.H;
+            s_jb.acts = acts;
+            s_jb.grid = grid;
+            s_jb.tokpair = s_tok;
+            s_jb.out = EPI == 0 ? a.mid : a.partial;
+            s_jb.b0 = s.b0;
+            s_jb.b1 = s.b1;
+            s_jb.wts = a.w;
+        }
         __syncthreads();
-        /* the segment's fixed job fields */
-        pm_rowjob jb;
-        jb.rb = kd.rb;
-        jb.npair = kd.npair;
-        jb.n_units = kd.n_units;
-        jb.nt = s.nt;
-        jb.act = a.act;
-        jb.ostride = EPI == 0 ? a.Fmax : a.H;
-        jb.acts = acts;
-        jb.grid = grid;
-        jb.tokpair = s_tok;
-        jb.out = EPI == 0 ? a.mid : a.partial;
-        jb.b0 = s.b0;
-        jb.b1 = s.b1;
-        jb.wts = a.w;
-        jb.terms = (float *)(smem + P.off_terms) + warp * (PM_TERM_V * PM_TERM_P);
+        const pm_rowjob &jb = s_jb;
+        float *const terms = (float *)(smem + P.off_terms) + warp * (PM_TERM_V * PM_TERM_P);
         const uint32_t bytes_row = (uint32_t)kd.rb;
         if (kd.direct) { /* rows straight from global memory, no ring stage */
             while (itc.k == k) {
@@ -402,9 +404,9 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
                 uint32_t r, rows;
                 pm_stage_src<NMAT>(s, kd, itc, src, r, rows);
                 if (s.kind == 0)
-                    pm_rows_any<QR, NMAT, EPI>(jb, kd.lpr, src[0], NMAT == 2 ? src[1] : nullptr, rows, r);
+                    pm_rows_any<QR, NMAT, EPI>(jb, terms, kd.lpr, src[0], NMAT == 2 ? src[1] : nullptr, rows, r);
                 else
-                    pm_rows_any<QS, NMAT, EPI>(jb, kd.lpr, src[0], NMAT == 2 ? src[1] : nullptr, rows, r);
+                    pm_rows_any<QS, NMAT, EPI>(jb, terms, kd.lpr, src[0], NMAT == 2 ? src[1] : nullptr, rows, r);
                 itc.g += (uint32_t)pm_sk_warps(NMAT);
                 pm_it_norm<EPI>(itc, a, tab, sl, P);
             }
@@ -423,9 +425,9 @@ __global__ void __launch_bounds__(32 * pm_sk_warps(NMAT), pm_sk_minb(NMAT))
             const uint8_t *w0 = pm_stage_ptr<NMAT>(stg, src, rows * bytes_row, 0);
             const uint8_t *w1 = NMAT == 2 ? pm_stage_ptr<NMAT>(stg, src, rows * bytes_row, 1) : nullptr;
             if (s.kind == 0)
-                pm_rows_any<QR, NMAT, EPI>(jb, kd.lpr, w0, w1, rows, r);
+                pm_rows_any<QR, NMAT, EPI>(jb, terms, kd.lpr, w0, w1, rows, r);
             else
-                pm_rows_any<QS, NMAT, EPI>(jb, kd.lpr, w0, w1, rows, r);
+                pm_rows_any<QS, NMAT, EPI>(jb, terms, kd.lpr, w0, w1, rows, r);
             __syncwarp();
             if (iti.k < sl.n_seg) { /* refill the slot just consumed */
                 if (lane == 0) {
