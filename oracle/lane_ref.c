@@ -11,7 +11,7 @@
 #include <unistd.h>
 
 #include "oracle.h"
-#include "pm_format.h"
+#include "ref_format.h"
 
 /* ---------------------------------------------------------------- glu */
 
@@ -103,7 +103,7 @@ int orc_router_select(int32_t *selected, float *weights, const float *logits, co
         float *w = weights + (size_t)t * n_slot;
         for (uint32_t e = 0; e < n_expert; e++) {
             float raw = lg[e];
-            float p = softmax_mode == 1 ? raw : pm_sigmoid(raw);
+            float p = softmax_mode == 1 ? raw : orf_sigmoid(raw);
             prob[e] = softmax_mode == 2 ? raw : p;
             score[e] = p + (bias ? bias[e] : 0.0f);
         }
@@ -164,12 +164,12 @@ int orc_router_select(int32_t *selected, float *weights, const float *logits, co
             float m = -INFINITY;
             for (uint32_t k = 0; k < n_slot; k++) {
                 float xv = w[k];
-                w[k] = xv < 0.0f ? xv - log1pf(pm_expf(xv)) : -log1pf(pm_expf(-xv));
+                w[k] = xv < 0.0f ? xv - log1pf(orf_expf(xv)) : -log1pf(orf_expf(-xv));
                 m = fmaxf(m, w[k]);
             }
             float es = 0.0f;
             for (uint32_t k = 0; k < n_slot; k++) {
-                w[k] = pm_expf(w[k] - m);
+                w[k] = orf_expf(w[k] - m);
                 es += w[k];
             }
             for (uint32_t k = 0; k < n_slot; k++) w[k] = w[k] / es * weight_scale;
@@ -178,7 +178,7 @@ int orc_router_select(int32_t *selected, float *weights, const float *logits, co
             for (uint32_t k = 0; k < k_used; k++) m = fmaxf(m, w[k]);
             float es = 0.0f;
             for (uint32_t k = 0; k < k_used; k++) {
-                w[k] = pm_expf(w[k] - m);
+                w[k] = orf_expf(w[k] - m);
                 es += w[k];
             }
             for (uint32_t k = 0; k < k_used; k++) w[k] = w[k] / es * weight_scale;
@@ -198,8 +198,8 @@ typedef struct {
     /* shared read-only state */
     const orc_expert_ptrs *ptrs;
     const float *w;
-    const pm_block_q8K *xq;  /* [n_tok][H blocks] */
-    pm_block_q8K *midq;      /* [n_tok*n_slot][F blocks] */
+    const orf_q8k *xq;  /* [n_tok][H blocks] */
+    orf_q8k *midq;      /* [n_tok*n_slot][F blocks] */
     float *mid;              /* [n_tok*n_slot][Fmax] */
     float *out;
     uint32_t H, n_tok, n_slot, n_routed, Fmax;
@@ -226,7 +226,7 @@ static void job_a(lane_ctx *c, uint32_t job) {
     uint32_t lo = chunk * 256, hi = lo + 256 < F ? lo + 256 : F;
     const orc_expert_ptrs *p = &c->ptrs[pair];
     float *mid = c->mid + (size_t)pair * c->Fmax;
-    const pm_block_q8K *xq = c->xq + (size_t)t * ((c->H + 255) / 256);
+    const orf_q8k *xq = c->xq + (size_t)t * ((c->H + 255) / 256);
     for (uint32_t j = lo; j < hi; j++) {
         if (!p->gate || !p->up) {
             mid[j] = 0.0f;
@@ -254,7 +254,7 @@ static void job_b(lane_ctx *c, uint32_t job) {
             const orc_expert_ptrs *p = &c->ptrs[(size_t)t * c->n_slot + s];
             if (!p->down) continue;
             int cl = slot_class(c, s);
-            const pm_block_q8K *mq = c->midq + ((size_t)t * c->n_slot + s) * fb;
+            const orf_q8k *mq = c->midq + ((size_t)t * c->n_slot + s) * fb;
             sum += orc_vec_dot((int)c->quant[cl], p->down + (size_t)r * c->rb_down[cl], mq, c->F[cl]);
         }
         float b = 0.0f;
@@ -324,9 +324,9 @@ int orc_moe_ffn(float *out, float *mid_out, const orc_expert_ptrs *ptrs, const f
     if (n_threads <= 0) n_threads = (int)sysconf(_SC_NPROCESSORS_ONLN);
 
     const uint32_t hb = (H + 255) / 256, fb = (c.Fmax + 255) / 256;
-    pm_block_q8K *xq = (pm_block_q8K *)malloc((size_t)n_tok * hb * sizeof(pm_block_q8K));
+    orf_q8k *xq = (orf_q8k *)malloc((size_t)n_tok * hb * sizeof(orf_q8k));
     float *mid = (float *)calloc((size_t)n_tok * n_slot * c.Fmax, sizeof(float));
-    pm_block_q8K *midq = (pm_block_q8K *)calloc((size_t)n_tok * n_slot * fb, sizeof(pm_block_q8K));
+    orf_q8k *midq = (orf_q8k *)calloc((size_t)n_tok * n_slot * fb, sizeof(orf_q8k));
     for (uint32_t t = 0; t < n_tok; t++) orc_quantize_q8k(x + (size_t)t * H, H, xq + (size_t)t * hb);
     c.xq = xq;
     c.mid = mid;

@@ -36,7 +36,7 @@ size_t orc_quantize_row_q2_k(const float *x, size_t n, uint8_t *out);
 size_t orc_quantize_row_q4_k(const float *x, size_t n, uint8_t *out);
 size_t orc_quantize_row_iq2_xxs(const float *x, const float *qw, size_t n, uint8_t *out);
 size_t orc_quantize_row_mxfp4(const float *x, size_t n, uint8_t *out);
-/* rows x n matrix, one call; quant = PM_QUANT_* code; qw may be NULL
+/* rows x n matrix, one call; quant = ORF_* code (the reference quant codes); qw may be NULL
  * (iq2_xxs then uses a uniform importance of 1.0) */
 int orc_quantize_rows(int quant, const float *x, size_t rows, size_t n, const float *qw, uint8_t *out);
 uint64_t orc_row_bytes(int quant, uint64_t n);
@@ -83,7 +83,7 @@ int orc_moe_ffn(float *out, float *mid_out, const orc_expert_ptrs *ptrs, const f
                 uint32_t F_s, uint32_t quant_s, uint64_t rb_gu_s, uint64_t rb_down_s,
                 uint32_t act_op, int n_threads);
 
-/* pm_expf / pm_sigmoid exported for the math tests */
+/* orf_expf / orf_sigmoid exported for the math tests */
 float orc_expf(float x);
 float orc_sigmoid(float x);
 uint64_t orc_iq2xxs_grid(int i);

@@ -13,7 +13,7 @@
 #include <string.h>
 
 #include "oracle.h"
-#include "pm_format.h"
+#include "ref_format.h"
 
 static int nearest_int(float x) { return (int)roundf(x); }
 static int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
@@ -29,7 +29,7 @@ size_t orc_quantize_row_q8_0(const float *x, size_t n, uint8_t *out) {
         for (size_t i = 0; i < len; i++) amax = fmaxf(amax, fabsf(x[b0 + i]));
         float d = amax / 127.0f;
         float id = d > 0.0f ? 1.0f / d : 0.0f;
-        uint16_t h = pm_f32_to_f16(d);
+        uint16_t h = orf_to_f16(d);
         out[o++] = (uint8_t)(h & 0xff);
         out[o++] = (uint8_t)(h >> 8);
         for (size_t i = 0; i < 32; i++) {
@@ -166,7 +166,7 @@ size_t orc_quantize_row_q2_k(const float *x, size_t n, uint8_t *out) {
                 out[o++] = (uint8_t)(lall[base] | (lall[base + 32] << 2) | (lall[base + 64] << 4) |
                                      (lall[base + 96] << 6));
             }
-        uint16_t hd = pm_f32_to_f16(d), hm = pm_f32_to_f16(dmin);
+        uint16_t hd = orf_to_f16(d), hm = orf_to_f16(dmin);
         out[o++] = (uint8_t)(hd & 0xff);
         out[o++] = (uint8_t)(hd >> 8);
         out[o++] = (uint8_t)(hm & 0xff);
@@ -233,8 +233,8 @@ size_t orc_quantize_row_q4_k(const float *x, size_t n, uint8_t *out) {
         float d = max_scale > 0.0f ? max_scale / 63.0f : 0.0f;
         float dmin = max_min > 0.0f ? max_min / 63.0f : 0.0f;
         /* requant with the f16-rounded scales */
-        float dq = pm_f16_to_f32(pm_f32_to_f16(d));
-        float mq = pm_f16_to_f32(pm_f32_to_f16(dmin));
+        float dq = orf_f16(orf_to_f16(d));
+        float mq = orf_f16(orf_to_f16(dmin));
         for (int j = 0; j < 8; j++) {
             float dj = dq * (float)sc_q[j];
             if (dj == 0.0f) {
@@ -245,7 +245,7 @@ size_t orc_quantize_row_q4_k(const float *x, size_t n, uint8_t *out) {
             for (int l = 0; l < 32; l++)
                 lall[32 * j + l] = (uint8_t)clampi(nearest_int((blk[32 * j + l] + mj) / dj), 0, 15);
         }
-        uint16_t hd = pm_f32_to_f16(d), hm = pm_f32_to_f16(dmin);
+        uint16_t hd = orf_to_f16(d), hm = orf_to_f16(dmin);
         out[o++] = (uint8_t)(hd & 0xff);
         out[o++] = (uint8_t)(hd >> 8);
         out[o++] = (uint8_t)(hm & 0xff);
@@ -286,7 +286,7 @@ static const iq2_tables *iq2_get(void) {
     if (g_iq2) return g_iq2;
     iq2_tables *t = (iq2_tables *)calloc(1, sizeof(iq2_tables));
     for (int i = 0; i < 256; i++)
-        for (int k = 0; k < 8; k++) t->grid[i][k] = (int8_t)(2 * ((PM_IQ2XXS_KGRID[i] >> (2 * k)) & 3) + 1);
+        for (int k = 0; k < 8; k++) t->grid[i][k] = (int8_t)(2 * ((ORF_KGRID[i] >> (2 * k)) & 3) + 1);
     for (int i = 0; i < KMAP_SIZE; i++) t->kmap[i] = -1;
     for (int i = 0; i < 256; i++) {
         uint32_t index = 0;
@@ -568,7 +568,7 @@ size_t orc_quantize_row_iq2_xxs(const float *x, const float *qw, size_t n, uint8
             int l = clampi(nearest_int(0.5f * (id * scales[ib] - 1.0f)), 0, 15);
             q2[2 * ib + 1] |= (uint32_t)l << 28;
         }
-        uint16_t hd = pm_f32_to_f16(d);
+        uint16_t hd = orf_to_f16(d);
         out[o++] = (uint8_t)(hd & 0xff);
         out[o++] = (uint8_t)(hd >> 8);
         for (int i = 0; i < 16; i++) {
@@ -634,11 +634,11 @@ size_t orc_quantize_row_mxfp4(const float *x, size_t n, uint8_t *out) {
 
 uint64_t orc_row_bytes(int quant, uint64_t n) {
     switch (quant) {
-    case PM_QUANT_Q2_K: return n / 256 * PM_Q2_K_BYTES;
-    case PM_QUANT_Q4_K: return n / 256 * PM_Q4_K_BYTES;
-    case PM_QUANT_IQ2_XXS: return n / 256 * PM_IQ2_XXS_BYTES;
-    case PM_QUANT_Q8_0: return (n + 31) / 32 * PM_Q8_0_BLOCK;
-    case PM_QUANT_MXFP4: return (n + 31) / 32 * PM_MXFP4_BLOCK;
+    case ORF_Q2_K: return n / 256 * ORF_Q2_K_BYTES;
+    case ORF_Q4_K: return n / 256 * ORF_Q4_K_BYTES;
+    case ORF_IQ2_XXS: return n / 256 * ORF_IQ2_XXS_BYTES;
+    case ORF_Q8_0: return (n + 31) / 32 * ORF_Q8_0_BLOCK;
+    case ORF_MXFP4: return (n + 31) / 32 * ORF_MXFP4_BLOCK;
     default: return 0;
     }
 }
@@ -650,11 +650,11 @@ int orc_quantize_rows(int quant, const float *x, size_t rows, size_t n, const fl
         const float *xr = x + r * n;
         uint8_t *o = out + r * rb;
         switch (quant) {
-        case PM_QUANT_Q2_K: orc_quantize_row_q2_k(xr, n, o); break;
-        case PM_QUANT_Q4_K: orc_quantize_row_q4_k(xr, n, o); break;
-        case PM_QUANT_IQ2_XXS: orc_quantize_row_iq2_xxs(xr, qw ? qw : NULL, n, o); break;
-        case PM_QUANT_Q8_0: orc_quantize_row_q8_0(xr, n, o); break;
-        case PM_QUANT_MXFP4: orc_quantize_row_mxfp4(xr, n, o); break;
+        case ORF_Q2_K: orc_quantize_row_q2_k(xr, n, o); break;
+        case ORF_Q4_K: orc_quantize_row_q4_k(xr, n, o); break;
+        case ORF_IQ2_XXS: orc_quantize_row_iq2_xxs(xr, qw ? qw : NULL, n, o); break;
+        case ORF_Q8_0: orc_quantize_row_q8_0(xr, n, o); break;
+        case ORF_MXFP4: orc_quantize_row_mxfp4(xr, n, o); break;
         default: return 0;
         }
     }
@@ -665,14 +665,14 @@ int orc_quantize_rows(int quant, const float *x, size_t rows, size_t n, const fl
 
 int orc_dequant_row(int quant, const uint8_t *row, size_t n, float *out) {
     switch (quant) {
-    case PM_QUANT_Q4_K: /* cpu_dot.rs:224-240 dequant_q4_k */
+    case ORF_Q4_K: /* cpu_dot.rs:224-240 dequant_q4_k */
         for (size_t ib = 0; ib < n / 256; ib++) {
-            const uint8_t *b = row + ib * PM_Q4_K_BYTES;
-            float d = pm_f16_to_f32(pm_ld_u16(b)), dmin = pm_f16_to_f32(pm_ld_u16(b + 2));
+            const uint8_t *b = row + ib * ORF_Q4_K_BYTES;
+            float d = orf_f16(orf_u16(b)), dmin = orf_f16(orf_u16(b + 2));
             for (int j = 0; j < 4; j++) {
                 int sc1, m1, sc2, m2;
-                pm_k4_scale_min(2 * j, b + 4, &sc1, &m1);
-                pm_k4_scale_min(2 * j + 1, b + 4, &sc2, &m2);
+                orf_k4_pair(2 * j, b + 4, &sc1, &m1);
+                orf_k4_pair(2 * j + 1, b + 4, &sc2, &m2);
                 for (int i = 0; i < 32; i++)
                     out[ib * 256 + 64 * j + i] = d * (float)sc1 * (float)(b[16 + 32 * j + i] & 15) - dmin * (float)m1;
                 for (int i = 0; i < 32; i++)
@@ -680,10 +680,10 @@ int orc_dequant_row(int quant, const uint8_t *row, size_t n, float *out) {
             }
         }
         return 1;
-    case PM_QUANT_Q2_K: /* cpu_dot.rs:870-890 (test-side dequant_q2_k) */
+    case ORF_Q2_K: /* cpu_dot.rs:870-890 (test-side dequant_q2_k) */
         for (size_t ib = 0; ib < n / 256; ib++) {
-            const uint8_t *b = row + ib * PM_Q2_K_BYTES;
-            float d = pm_f16_to_f32(pm_ld_u16(b + 80)), dmin = pm_f16_to_f32(pm_ld_u16(b + 82));
+            const uint8_t *b = row + ib * ORF_Q2_K_BYTES;
+            float d = orf_f16(orf_u16(b + 80)), dmin = orf_f16(orf_u16(b + 82));
             for (int c = 0; c < 16; c++) {
                 int k = c / 8, js = (c % 8) / 2, half = c % 2;
                 for (int i = 0; i < 16; i++) {
@@ -693,16 +693,16 @@ int orc_dequant_row(int quant, const uint8_t *row, size_t n, float *out) {
             }
         }
         return 1;
-    case PM_QUANT_IQ2_XXS: /* cpu_dot.rs:785-806 dequant_row_iq2_xxs */
+    case ORF_IQ2_XXS: /* cpu_dot.rs:785-806 dequant_row_iq2_xxs */
         for (size_t ib = 0; ib < n / 256; ib++) {
-            const uint8_t *b = row + ib * PM_IQ2_XXS_BYTES;
-            float d = pm_f16_to_f32(pm_ld_u16(b));
+            const uint8_t *b = row + ib * ORF_IQ2_XXS_BYTES;
+            float d = orf_f16(orf_u16(b));
             for (int g = 0; g < 8; g++) {
-                uint32_t a0 = pm_ld_u32(b + 2 + 8 * g), a1 = pm_ld_u32(b + 6 + 8 * g);
+                uint32_t a0 = orf_u32(b + 2 + 8 * g), a1 = orf_u32(b + 6 + 8 * g);
                 float db = 0.125f * d * (float)(2 * (a1 >> 28) + 1);
                 for (int k = 0; k < 4; k++) {
-                    uint64_t gv = pm_iq2xxs_expand(PM_IQ2XXS_KGRID[(a0 >> (8 * k)) & 255]);
-                    uint32_t sm = pm_ksigns((a1 >> (7 * k)) & 127);
+                    uint64_t gv = orf_grid8(ORF_KGRID[(a0 >> (8 * k)) & 255]);
+                    uint32_t sm = orf_signs8((a1 >> (7 * k)) & 127);
                     for (int i = 0; i < 8; i++) {
                         float v = db * (float)(int8_t)((gv >> (8 * i)) & 255);
                         out[ib * 256 + 32 * g + 8 * k + i] = ((sm >> i) & 1) ? -v : v;
@@ -711,20 +711,20 @@ int orc_dequant_row(int quant, const uint8_t *row, size_t n, float *out) {
             }
         }
         return 1;
-    case PM_QUANT_MXFP4:
+    case ORF_MXFP4:
         for (size_t b0 = 0; b0 < n; b0 += 32) {
-            const uint8_t *b = row + (b0 / 32) * PM_MXFP4_BLOCK;
-            float s = pm_mxfp4_scale_half(b[0]);
+            const uint8_t *b = row + (b0 / 32) * ORF_MXFP4_BLOCK;
+            float s = orf_e8m0_half(b[0]);
             for (int i = 0; i < 16; i++) {
-                if (b0 + i < n) out[b0 + i] = s * (float)pm_mxfp4_kv(b[1 + i] & 15);
-                if (b0 + 16 + i < n) out[b0 + 16 + i] = s * (float)pm_mxfp4_kv(b[1 + i] >> 4);
+                if (b0 + i < n) out[b0 + i] = s * (float)orf_e2m1x2(b[1 + i] & 15);
+                if (b0 + 16 + i < n) out[b0 + 16 + i] = s * (float)orf_e2m1x2(b[1 + i] >> 4);
             }
         }
         return 1;
-    case PM_QUANT_Q8_0: /* cpu_dot.rs:206-216 dequant_q8_0 */
+    case ORF_Q8_0: /* cpu_dot.rs:206-216 dequant_q8_0 */
         for (size_t b0 = 0; b0 < n; b0 += 32) {
-            const uint8_t *b = row + (b0 / 32) * PM_Q8_0_BLOCK;
-            float d = pm_f16_to_f32(pm_ld_u16(b));
+            const uint8_t *b = row + (b0 / 32) * ORF_Q8_0_BLOCK;
+            float d = orf_f16(orf_u16(b));
             for (int i = 0; i < 32 && b0 + i < n; i++) out[b0 + i] = (float)(int8_t)b[2 + i] * d;
         }
         return 1;
@@ -737,12 +737,12 @@ int orc_dequant_row(int quant, const uint8_t *row, size_t n, float *out) {
 /* crates/quant/src/cpu_dot.rs:26-50 quantize_row_q8_k, on 292-byte blocks;
  * a partial tail block quantizes as if zero-padded (cu:1499-1505) */
 void orc_quantize_q8k(const float *x, size_t n, void *out_blocks) {
-    pm_block_q8K *out = (pm_block_q8K *)out_blocks;
+    orf_q8k *out = (orf_q8k *)out_blocks;
     size_t nb = (n + 255) / 256;
     for (size_t b = 0; b < nb; b++) {
         float v[256];
         for (int i = 0; i < 256; i++) v[i] = b * 256 + i < n ? x[b * 256 + i] : 0.0f;
-        pm_block_q8K *y = out + b;
+        orf_q8k *y = out + b;
         float amax = 0.0f;
         for (int i = 0; i < 256; i++) amax = fmaxf(amax, fabsf(v[i]));
         if (amax == 0.0f) {
@@ -767,25 +767,25 @@ void orc_quantize_q8k(const float *x, size_t n, void *out_blocks) {
 
 void orc_quantize_q8k_rows(const float *x, size_t n, size_t rows, void *out_blocks) {
     size_t nb = (n + 255) / 256;
-    for (size_t r = 0; r < rows; r++) orc_quantize_q8k(x + r * n, n, (pm_block_q8K *)out_blocks + r * nb);
+    for (size_t r = 0; r < rows; r++) orc_quantize_q8k(x + r * n, n, (orf_q8k *)out_blocks + r * nb);
 }
 
 /* ------------------------------------------------------------------ dots */
 
 /* cpu_dot.rs:250-279 vec_dot_q4_k_q8_k_scalar */
-static float dot_q4_k(const uint8_t *row, const pm_block_q8K *x, size_t nb) {
+static float dot_q4_k(const uint8_t *row, const orf_q8k *x, size_t nb) {
     float total = 0.0f;
     for (size_t ib = 0; ib < nb; ib++) {
-        const uint8_t *b = row + ib * PM_Q4_K_BYTES;
-        float xd = pm_f16_to_f32(pm_ld_u16(b)), xmin = pm_f16_to_f32(pm_ld_u16(b + 2));
+        const uint8_t *b = row + ib * ORF_Q4_K_BYTES;
+        float xd = orf_f16(orf_u16(b)), xmin = orf_f16(orf_u16(b + 2));
         const uint8_t *q4 = b + 16;
         const int8_t *q8 = x[ib].qs;
         const int16_t *bs = x[ib].bsums;
         int isum = 0, msum = 0;
         for (int j = 0; j < 4; j++) {
             int sc1, m1, sc2, m2;
-            pm_k4_scale_min(2 * j, b + 4, &sc1, &m1);
-            pm_k4_scale_min(2 * j + 1, b + 4, &sc2, &m2);
+            orf_k4_pair(2 * j, b + 4, &sc1, &m1);
+            orf_k4_pair(2 * j + 1, b + 4, &sc2, &m2);
             int s1 = 0, s2 = 0;
             for (int i = 0; i < 32; i++) {
                 uint8_t v = q4[32 * j + i];
@@ -801,12 +801,12 @@ static float dot_q4_k(const uint8_t *row, const pm_block_q8K *x, size_t nb) {
 }
 
 /* cpu_dot.rs:732-767 vec_dot_q2_k_q8_k_scalar */
-static float dot_q2_k(const uint8_t *row, const pm_block_q8K *x, size_t nb) {
+static float dot_q2_k(const uint8_t *row, const orf_q8k *x, size_t nb) {
     float total = 0.0f;
     for (size_t ib = 0; ib < nb; ib++) {
-        const uint8_t *b = row + ib * PM_Q2_K_BYTES;
+        const uint8_t *b = row + ib * ORF_Q2_K_BYTES;
         const uint8_t *sc = b, *q2 = b + 16;
-        float xd = pm_f16_to_f32(pm_ld_u16(b + 80)), xmin = pm_f16_to_f32(pm_ld_u16(b + 82));
+        float xd = orf_f16(orf_u16(b + 80)), xmin = orf_f16(orf_u16(b + 82));
         const int8_t *q8 = x[ib].qs;
         const int16_t *bs = x[ib].bsums;
         int summs = 0;
@@ -829,20 +829,20 @@ static float dot_q2_k(const uint8_t *row, const pm_block_q8K *x, size_t nb) {
 }
 
 /* cpu_dot.rs:92-122 vec_dot_iq2_xxs_q8_k_scalar */
-static float dot_iq2_xxs(const uint8_t *row, const pm_block_q8K *x, size_t nb) {
+static float dot_iq2_xxs(const uint8_t *row, const orf_q8k *x, size_t nb) {
     float total = 0.0f;
     for (size_t ib = 0; ib < nb; ib++) {
-        const uint8_t *b = row + ib * PM_IQ2_XXS_BYTES;
-        float xd = pm_f16_to_f32(pm_ld_u16(b));
+        const uint8_t *b = row + ib * ORF_IQ2_XXS_BYTES;
+        float xd = orf_f16(orf_u16(b));
         const int8_t *q8 = x[ib].qs;
         int bsum = 0;
         for (int g = 0; g < 8; g++) {
-            uint32_t a0 = pm_ld_u32(b + 2 + 8 * g), a1 = pm_ld_u32(b + 6 + 8 * g);
+            uint32_t a0 = orf_u32(b + 2 + 8 * g), a1 = orf_u32(b + 6 + 8 * g);
             int ls = (int)(2 * (a1 >> 28) + 1);
             int sumi = 0;
             for (int k = 0; k < 4; k++) {
-                uint64_t gv = pm_iq2xxs_expand(PM_IQ2XXS_KGRID[(a0 >> (8 * k)) & 255]);
-                uint32_t sm = pm_ksigns((a1 >> (7 * k)) & 127);
+                uint64_t gv = orf_grid8(ORF_KGRID[(a0 >> (8 * k)) & 255]);
+                uint32_t sm = orf_signs8((a1 >> (7 * k)) & 127);
                 for (int i = 0; i < 8; i++) {
                     int w = (int)((gv >> (8 * i)) & 255);
                     if ((sm >> i) & 1) w = -w;
@@ -861,20 +861,20 @@ static float dot_iq2_xxs(const uint8_t *row, const pm_block_q8K *x, size_t nb) {
  * q8, scaled by 2^(e-128); per super-block yd * sum.  A partial tail
  * super-block only visits its real 32-blocks (the q8 tail is zero, so the
  * reference's extra blocks add exactly 0). */
-static float dot_mxfp4(const uint8_t *row, const pm_block_q8K *x, size_t n) {
+static float dot_mxfp4(const uint8_t *row, const orf_q8k *x, size_t n) {
     float total = 0.0f;
     size_t nblk = (n + 31) / 32;
     for (size_t ib = 0; ib < (n + 255) / 256; ib++) {
         const int8_t *q8 = x[ib].qs;
         float sumf = 0.0f;
         for (size_t b = 0; b < 8 && ib * 8 + b < nblk; b++) {
-            const uint8_t *bp = row + (ib * 8 + b) * PM_MXFP4_BLOCK;
+            const uint8_t *bp = row + (ib * 8 + b) * ORF_MXFP4_BLOCK;
             int sumi = 0;
             for (int i = 0; i < 16; i++) {
-                sumi += pm_mxfp4_kv(bp[1 + i] & 15) * q8[b * 32 + i];
-                sumi += pm_mxfp4_kv(bp[1 + i] >> 4) * q8[b * 32 + 16 + i];
+                sumi += orf_e2m1x2(bp[1 + i] & 15) * q8[b * 32 + i];
+                sumi += orf_e2m1x2(bp[1 + i] >> 4) * q8[b * 32 + 16 + i];
             }
-            sumf += pm_mxfp4_scale_half(bp[0]) * (float)sumi;
+            sumf += orf_e8m0_half(bp[0]) * (float)sumi;
         }
         total += x[ib].d * sumf;
     }
@@ -883,17 +883,17 @@ static float dot_mxfp4(const uint8_t *row, const pm_block_q8K *x, size_t n) {
 
 /* Q8_0 x q8_K, the reference GPU math (cu:2174-2190): a zero integer sum
  * skips its block scale */
-static float dot_q8_0(const uint8_t *row, const pm_block_q8K *x, size_t n) {
+static float dot_q8_0(const uint8_t *row, const orf_q8k *x, size_t n) {
     float total = 0.0f;
     size_t nblk = (n + 31) / 32;
     for (size_t ib = 0; ib < (n + 255) / 256; ib++) {
         const int8_t *q8 = x[ib].qs;
         float sumf = 0.0f;
         for (size_t b = 0; b < 8 && ib * 8 + b < nblk; b++) {
-            const uint8_t *bp = row + (ib * 8 + b) * PM_Q8_0_BLOCK;
+            const uint8_t *bp = row + (ib * 8 + b) * ORF_Q8_0_BLOCK;
             int sumi = 0;
             for (int i = 0; i < 32; i++) sumi += (int8_t)bp[2 + i] * q8[b * 32 + i];
-            if (sumi != 0) sumf += pm_f16_to_f32(pm_ld_u16(bp)) * (float)sumi;
+            if (sumi != 0) sumf += orf_f16(orf_u16(bp)) * (float)sumi;
         }
         total += x[ib].d * sumf;
     }
@@ -901,17 +901,17 @@ static float dot_q8_0(const uint8_t *row, const pm_block_q8K *x, size_t n) {
 }
 
 float orc_vec_dot(int quant, const uint8_t *row, const void *xq_blocks, size_t n) {
-    const pm_block_q8K *x = (const pm_block_q8K *)xq_blocks;
+    const orf_q8k *x = (const orf_q8k *)xq_blocks;
     switch (quant) {
-    case PM_QUANT_Q4_K: return dot_q4_k(row, x, n / 256);
-    case PM_QUANT_Q2_K: return dot_q2_k(row, x, n / 256);
-    case PM_QUANT_IQ2_XXS: return dot_iq2_xxs(row, x, n / 256);
-    case PM_QUANT_MXFP4: return dot_mxfp4(row, x, n);
-    case PM_QUANT_Q8_0: return dot_q8_0(row, x, n);
+    case ORF_Q4_K: return dot_q4_k(row, x, n / 256);
+    case ORF_Q2_K: return dot_q2_k(row, x, n / 256);
+    case ORF_IQ2_XXS: return dot_iq2_xxs(row, x, n / 256);
+    case ORF_MXFP4: return dot_mxfp4(row, x, n);
+    case ORF_Q8_0: return dot_q8_0(row, x, n);
     default: return NAN;
     }
 }
 
-float orc_expf(float x) { return pm_expf(x); }
-float orc_sigmoid(float x) { return pm_sigmoid(x); }
-uint64_t orc_iq2xxs_grid(int i) { return pm_iq2xxs_expand(PM_IQ2XXS_KGRID[i & 255]); }
+float orc_expf(float x) { return orf_expf(x); }
+float orc_sigmoid(float x) { return orf_sigmoid(x); }
+uint64_t orc_iq2xxs_grid(int i) { return orf_grid8(ORF_KGRID[i & 255]); }
