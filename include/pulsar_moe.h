@@ -174,6 +174,11 @@ typedef struct pulsar_moe_layer_desc {
      * of the call's error word, the kernel drains what it has in flight and
      * returns; the output of that call is then invalid. */
     uint64_t wait_cycles;
+    /* qwen35 shared-expert gate (crates/engine/src/real/qwen35.rs:2167-2169):
+     * [n_embd] f32 or NULL.  With it, the shared expert's output row of
+     * token t is scaled by sigmoid(shared_gate_w . x[t]) before it joins the
+     * routed sum (the dot in the router's fixed f32 order). */
+    const float *shared_gate_w;
 } pulsar_moe_layer_desc;
 
 /* pulsar_rms_norm on an explicit stream (cudaStream_t, NULL = per-thread default) */

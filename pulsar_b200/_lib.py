@@ -53,7 +53,7 @@ class LayerDesc(ctypes.Structure):
         ("expert_lo", ctypes.c_uint32), ("expert_hi", ctypes.c_uint32),
         ("shared_row_bytes_gu", ctypes.c_uint64), ("shared_row_bytes_down", ctypes.c_uint64),
         ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p), ("shared_down", ctypes.c_void_p),
-        ("wait_cycles", ctypes.c_uint64),
+        ("wait_cycles", ctypes.c_uint64), ("shared_gate_w", ctypes.c_void_p),
     ]
 
 

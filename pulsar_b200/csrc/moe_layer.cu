@@ -137,6 +137,7 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T, bool
         L.tcp = o, o = pm_al(o + (size_t)L.ks_max * per);
     }
     L.partial = o, o = pm_al(o + (size_t)T * L.n_slot * L.H * 4);
+    L.shg = o, o = pm_al(o + (d->shared_gate_w && L.S ? (size_t)T * 4 : 0)); /* shared-expert gate logits */
     /* control words: [0] selection arrival counter, [1] error word; both
      * cleared by the first kernel of every call */
     L.ctl = o, o = pm_al(o + 8);
@@ -470,8 +471,14 @@ __global__ void pm_layer_combine_kernel(const __grid_constant__ pm_layer_args a)
             if (a.down_b) b = __fadd_rn(b, __fmul_rn(a.w[t * a.n_slot + s], a.down_b[(uint64_t)e * a.H + r]));
         }
     }
-    if (t - a.sh_t0 < a.sh_nt) /* unsigned: t >= sh_t0 and t < sh_t0 + sh_nt */
-        for (uint32_t s = a.k; s < a.n_slot; s++) v += a.partial[(uint64_t)(t * a.n_slot + s) * a.H + r];
+    if (t - a.sh_t0 < a.sh_nt) { /* unsigned: t >= sh_t0 and t < sh_t0 + sh_nt */
+        /* qwen35: shared output x sigmoid(gate logit), 1 / (1 + e^-s) as the reference forms it */
+        const float g = a.shg ? __fdiv_rn(1.0f, __fadd_rn(1.0f, pm_exp_f32(-a.shg[t]))) : 1.0f;
+        for (uint32_t s = a.k; s < a.n_slot; s++) {
+            const float p = a.partial[(uint64_t)(t * a.n_slot + s) * a.H + r];
+            v += a.shg ? __fmul_rn(p, g) : p;
+        }
+    }
     if (b != 0.0f) v += b;
     if (a.residual && t - a.res_t0 < a.res_nt) v += a.residual[(uint64_t)(t - a.res_t0) * a.H + r];
     a.out[gid] = v;
@@ -626,6 +633,7 @@ static void pm_fill_args(pm_layer_args &a, const pulsar_moe_layer_desc *d, const
                             : PM_WAIT_CYCLES;
     /* single GPU: every token is this call's, the shared expert serves all
      * of them (on the shard that owns expert 0 when the experts are split) */
+    a.shg = d->shared_gate_w && L.S ? (const float *)(b + L.shg) : nullptr;
     a.sel_t0 = 0, a.sel_nt = L.T;
     a.sh_t0 = 0, a.sh_nt = a.lo == 0 ? L.T : 0u;
     a.res_t0 = 0, a.res_nt = L.T;
@@ -676,6 +684,9 @@ static int pm_moe_layer_run(const pulsar_moe_layer_desc *d, const pm_ep &ep, flo
     pm_ev(ev, 0, st);
     if (!pm_launch_router_logits_q8(a.logits + (uint64_t)t0 * L.E, d->router_w, x, d->router_logit_b, L.E, L.H,
                                     n_tok, a.xq + (uint64_t)t0 * L.hb, a.sel_done, st))
+        return 0;
+    if (a.shg && !pm_launch_router_logits_q8((float *)a.shg + t0, d->shared_gate_w, x, nullptr, 1u, L.H, n_tok,
+                                             nullptr, nullptr, st))
         return 0;
     pm_ev(ev, 1, st);
     pm_ev(ev, 2, st); /* q8_K of x is written by the router kernel */

@@ -83,7 +83,7 @@ struct pm_layout {
     uint64_t tc_slot_bytes;
     size_t tc_ord, tc_first, tcb, tcx, tclo;
     size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, tc_tile, pairs, mid,
-        midq, tcp, partial, epo, ctl, total;
+        midq, tcp, partial, epo, shg, ctl, total;
 };
 
 
@@ -128,6 +128,7 @@ struct pm_layer_args {
      *  res_t0, res_nt  tokens whose residual rows this call adds
      * phase: 0 selection then CSR in one launch, 1 selection only, 2 CSR only */
     uint32_t sel_t0, sel_nt, sh_t0, sh_nt, res_t0, res_nt, phase;
+    const float *shg; /* [T] shared-expert gate logits (qwen35), or null */
     /* io */
     float *out;
     const float *residual;

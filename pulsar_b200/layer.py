@@ -41,6 +41,7 @@ class LayerSpec:
     shared_n_ff: int = 0
     biases: bool = False          # per-expert gate/up/down biases + router logit bias
     router_q8_0: bool = False     # router weights stored as Q8_0 and used as their exact f32 dequant
+    shared_gate: bool = False     # qwen35 sigmoid gate on the shared expert's output (a [n_embd] vector)
     weight_std: float = 0.02
     bias_std: float = 0.01
 
@@ -60,6 +61,7 @@ class MoeLayer:
     shared_gate: torch.Tensor | None = None
     shared_up: torch.Tensor | None = None
     shared_down: torch.Tensor | None = None
+    shared_gate_w: torch.Tensor | None = None
     expert_lo: int = 0
     expert_hi: int = 0
     slab_lo: int = 0              # first expert held in the routed slabs (shards hold [slab_lo, expert_hi))
@@ -110,6 +112,7 @@ class MoeLayer:
             d.shared_row_bytes_gu = row_bytes(s.shared_quant, s.n_embd)
             d.shared_row_bytes_down = row_bytes(s.shared_quant, s.shared_n_ff)
             d.shared_gate, d.shared_up, d.shared_down = ptr(self.shared_gate), ptr(self.shared_up), ptr(self.shared_down)
+            d.shared_gate_w = ptr(self.shared_gate_w)
         d.expert_lo, d.expert_hi = self.expert_lo, self.expert_hi
         self._desc = d
         return d
@@ -273,6 +276,8 @@ def make_layer(spec: LayerSpec, seed: int, device="cuda", lo: int = 0, hi: int =
         layer.shared_gate = _quantized(s.shared_n_ff, s.n_embd, sq, s.weight_std, gen(9), dev, qw=qs)
         layer.shared_up = _quantized(s.shared_n_ff, s.n_embd, sq, s.weight_std, gen(10), dev, qw=qs)
         layer.shared_down = _quantized(s.n_embd, s.shared_n_ff, sq, s.weight_std, gen(11), dev, qw=qsf)
+        if s.shared_gate:
+            layer.shared_gate_w = (torch.randn((s.n_embd,), generator=gen(12), device=dev) * s.weight_std).contiguous()
     return layer
 
 

@@ -154,9 +154,11 @@ class DeviceMirror:
         self.logit_b, self.select_b = h(layer.router_logit_b), h(layer.router_select_b)
         self.gate_b, self.up_b, self.down_b = h(layer.gate_b), h(layer.up_b), h(layer.down_b)
         self.shared = None
+        self.shared_gate_w = None
         if s.shared_quant is not None:
             sq, Fs = s.shared_quant, s.shared_n_ff
             self.shared = dict(quant=sq, F=Fs, rb_gu=orc.row_bytes(sq, self.H), rb_dn=orc.row_bytes(sq, Fs))
+            self.shared_gate_w = h(layer.shared_gate_w)
             for n, t, rows, rb in (("gate", layer.shared_gate, Fs, self.shared["rb_gu"]),
                                    ("up", layer.shared_up, Fs, self.shared["rb_gu"]),
                                    ("down", layer.shared_down, self.H, self.shared["rb_dn"])):
@@ -197,6 +199,20 @@ class DeviceMirror:
         if ns:
             s = self.shared
             sh = (s["F"], s["quant"], s["rb_gu"], s["rb_dn"])
+        if ns and self.shared_gate_w is not None:
+            # qwen35 (real/qwen35.rs:2160-2169): moe_out + sigmoid(gate_w . x) * shared_out
+            routed = orc.moe_ffn(x, [r[:self.k] for r in slots], np.ascontiguousarray(ws[:, :self.k]), self.H,
+                                 self.k, (self.F, self.quant, self.rb_gu, self.rb_dn), None, act_op=self.act_op,
+                                 return_mid=return_mid)
+            mid = None
+            if return_mid:
+                routed, mid = routed
+            shared = orc.moe_ffn(x, [r[self.k:] for r in slots], np.ascontiguousarray(ws[:, self.k:]), self.H, 0,
+                                 (self.F, self.quant, self.rb_gu, self.rb_dn), sh, act_op=self.act_op)
+            s_ = orc.router_logits(self.shared_gate_w[None, :], x)[:, 0]
+            g = (np.float32(1.0) / (np.float32(1.0) + np.exp(-s_).astype(np.float32))).astype(np.float32)
+            out = (routed + shared * g[:, None]).astype(np.float32)
+            return (out, mid) if return_mid else out
         return orc.moe_ffn(x, slots, ws, self.H, self.k, (self.F, self.quant, self.rb_gu, self.rb_dn), sh,
                            act_op=self.act_op, return_mid=return_mid)
 

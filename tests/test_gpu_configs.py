@@ -22,6 +22,8 @@ lane's order, so the mid rows (glu * route weight) match the oracle's bit
 for bit except where the glu's exponential rounds differently (the CPU
 lane's f32 expf vs the binary64 exponential rounded to f32): measured at
 <= 3 ulp in ~0.03% of values; the test allows <= 4 ulp in <= 0.1%.
+C2g is config 2 with the qwen35 sigmoid gate on the shared expert's output
+(real/qwen35.rs:2160-2169), against the oracle's routed + gate x shared.
 C3 at 2048 tokens also checks the dequantized weights of the tensor-core
 path: the MXFP4 weight images hold the oracle's f32 dequant exactly, with
 no lo part.
@@ -38,20 +40,26 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-3
 SUBSET = 48
-CASES = [("C1", 1), ("C2", 1), ("C2", 8), ("C2", 64), ("C3", 1), ("C3", 2048), ("C4", 1), ("C4", 32),
-         ("C4", 256), ("C5", 64), ("C5", 4096)]
+CASES = [("C1", 1), ("C2", 1), ("C2", 8), ("C2", 64), ("C2g", 1), ("C2g", 64), ("C3", 1), ("C3", 2048),
+         ("C4", 1), ("C4", 32), ("C4", 256), ("C5", 64), ("C5", 4096)]
 _CUR = {}
 
 
 def layer_for(name):
-    """one layer of config `name` on the device (kept while the next cases use it)"""
+    """one layer of config `name` on the device (kept while the next cases use it);
+    "C2g": config 2 with the qwen35 sigmoid gate on its shared expert"""
     if name not in _CUR:
         _CUR.clear()
         gc.collect()
         torch.cuda.empty_cache()
+        from dataclasses import replace
+
         from pulsar_b200 import make_layer
         from pulsar_b200.configs import CONFIGS
-        L = make_layer(CONFIGS[name]["spec"], seed=7000 + int(name[1]), device="cuda")
+        spec = CONFIGS[name[:2]]["spec"]
+        if name == "C2g":
+            spec = replace(spec, shared_gate=True)
+        L = make_layer(spec, seed=7000 + int(name[1]), device="cuda")
         torch.cuda.synchronize()
         _CUR[name] = (L, DeviceMirror(L))
     return _CUR[name]
@@ -93,13 +101,13 @@ def test_config_true_shape(oracle, name, T):
         ns, fm = v.n_slot, v.f_max
         mid = rd(v.mid, T * ns * fm, np.float32).reshape(T, ns, fm)[idx]
         diff = 0
-        for s in range(ns):
+        for s in range(ref_mid.shape[1]):  # the gated layer's oracle returns the routed slots' rows
             F = M.F if s < M.k else M.shared["F"]
             a, b = mid[:, s, :F], ref_mid[:, s, :F]
             ulp = np.abs(a.view(np.int32).astype(np.int64) - b.view(np.int32).astype(np.int64))
             diff += int(np.count_nonzero(ulp))
             assert int(ulp.max()) <= 4, (name, T, s, int(ulp.max()))
-        total = len(idx) * ns * M.F
+        total = len(idx) * ref_mid.shape[1] * M.F
         print(f"{name} T={T}: mid bits differ in {diff} of {total}")
         assert diff <= max(3, total // 1000), (name, T, diff)
     if name == "C3" and T == 2048:
