@@ -179,7 +179,13 @@ typedef struct pulsar_moe_layer_desc {
      * token t is scaled by sigmoid(shared_gate_w . x[t]) before it joins the
      * routed sum (the dot in the router's fixed f32 order). */
     const float *shared_gate_w;
+    /* PULSAR_LAYER_* path flags (0 = the default paths) */
+    uint32_t path_flags;
 } pulsar_moe_layer_desc;
+
+/* path_flags: keep routed Q2_K experts off the integer tensor-core passes
+ * (dp4a engine / fp16 tensor-core tiles instead; for comparisons) */
+#define PULSAR_LAYER_NO_I8 1u
 
 /* pulsar_rms_norm on an explicit stream (cudaStream_t, NULL = per-thread default) */
 int pulsar_rms_norm_stream(void *out, const void *x, const void *w, uint32_t n, uint32_t rows, float eps,

@@ -26,6 +26,7 @@ QUANT_MXFP4 = 12
 QUANTS = {"Q2_K": QUANT_Q2_K, "IQ2_XXS": QUANT_IQ2_XXS, "Q4_K": QUANT_Q4_K, "Q8_0": QUANT_Q8_0,
           "MXFP4": QUANT_MXFP4}
 Q8K_BLOCK_BYTES = 292
+LAYER_NO_I8 = 1  # path_flags: routed Q2_K experts off the integer tensor cores
 
 
 class KernelError(RuntimeError):
@@ -53,7 +54,7 @@ class LayerDesc(ctypes.Structure):
         ("expert_lo", ctypes.c_uint32), ("expert_hi", ctypes.c_uint32),
         ("shared_row_bytes_gu", ctypes.c_uint64), ("shared_row_bytes_down", ctypes.c_uint64),
         ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p), ("shared_down", ctypes.c_void_p),
-        ("wait_cycles", ctypes.c_uint64), ("shared_gate_w", ctypes.c_void_p),
+        ("wait_cycles", ctypes.c_uint64), ("shared_gate_w", ctypes.c_void_p), ("path_flags", ctypes.c_uint32),
     ]
 
 

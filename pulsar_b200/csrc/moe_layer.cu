@@ -54,9 +54,19 @@ static int pm_sm_count() {
 /* ------------------------------------------------------------ layout */
 static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
 
+/* routed Q2_K experts on the integer tensor cores (pm_tci8.cuh): whole
+ * super-blocks, 128-row blocks, and the select kernel's 20-bit cost / 12-bit
+ * tile packing; the descriptor's PULSAR_LAYER_NO_I8 flag keeps them on the
+ * dp4a / fp16 tensor-core paths */
+static bool pm_i8_on(const pulsar_moe_layer_desc *d, uint32_t T) {
+    const uint64_t routed = (uint64_t)T * d->n_used;
+    return !(d->path_flags & PULSAR_LAYER_NO_I8) && d->quant == PM_QUANT_Q2_K && d->n_embd % 256u == 0 &&
+           d->n_ff % 256u == 0 && routed < (1u << 19) && routed / PM_I8_N + d->n_expert < 4000u;
+}
+
 /* tensor-core path available for the routed / shared experts */
-static bool pm_tc_on_r(const pulsar_moe_layer_desc *d) {
-    return pm_tc_fmt(d->quant) && d->n_embd % 64 == 0 && d->n_ff % 64 == 0;
+static bool pm_tc_on_r(const pulsar_moe_layer_desc *d, uint32_t T) {
+    return pm_tc_fmt(d->quant) && d->n_embd % 64 == 0 && d->n_ff % 64 == 0 && !pm_i8_on(d, T);
 }
 static bool pm_tc_on_s(const pulsar_moe_layer_desc *d) {
     return d->n_shared && pm_tc_fmt(d->shared_quant) && d->n_embd % 64 == 0 && d->shared_n_ff % 64 == 0;
@@ -96,10 +106,13 @@ static pm_layout pm_make_layout(const pulsar_moe_layer_desc *d, uint32_t T, bool
     L.tc_tile = o, o = pm_al(o + (size_t)L.max_tc * 8);
     L.tc_ord = o, o = pm_al(o + (size_t)L.max_tc * 4);
     L.tc_first = o, o = pm_al(o + (size_t)L.max_tc * 4);
+    /* integer tensor-core tiles: every routed expert's tokens in chunks of PM_I8_N */
+    L.max_i8 = (uint32_t)((routed < L.E ? routed : L.E) + routed / PM_I8_N + 1);
+    L.i8_tile = o, o = pm_al(o + (pm_i8_on(d, T) ? (size_t)L.max_i8 * 8 : 0));
     /* tensor-core operand images: token images of every tile, expanded
      * weight images of up to tc_slots experts at a time */
     {
-        const bool tr = pm_tc_on_r(d), ts = pm_tc_on_s(d);
+        const bool tr = pm_tc_on_r(d, T), ts = pm_tc_on_s(d);
         const uint64_t n_r = tr ? (routed / PM_TC_MIN < L.E ? routed / PM_TC_MIN : L.E) : 0;
         const uint64_t n_items = T >= PM_TC_MIN ? n_r + (ts ? L.S : 0u) : 0;
         uint64_t sb = 0;
@@ -244,10 +257,14 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
         const uint32_t e = c0 + threadIdx.x;
         const uint32_t v = e < a.E ? cnt[e] : 0u;
         const bool tcq = a.tc_r && v >= PM_TC_MIN; /* this expert's tokens go to tensor-core tiles */
-        const uint32_t nw = tcq ? 0u : (v + PM_TT - 1) / PM_TT;
+        const bool i8q = !tcq && a.i8 && v;       /* ... or to integer tensor-core tiles of <= 32 */
+        const uint32_t nw = tcq || i8q ? 0u : (v + PM_TT - 1) / PM_TT;
         const uint32_t nti = tcq ? (v + PM_TC_N - 1) / PM_TC_N : 0u;
-        /* .y packs items (high 16 bits) and tensor-core tiles (low 16 bits) */
-        const uint4 own = make_uint4(v, ((v ? 1u : 0u) << 16) | nti, nw, PM_SK_CR * nw + (tcq ? 0u : v));
+        const uint32_t ni8 = i8q ? (v + PM_I8_N - 1) / PM_I8_N : 0u;
+        /* .y packs items (high 16 bits) and tensor-core tiles (low 16 bits); .w packs the
+         * stream-K cost (low 20 bits) and the integer tiles (high 12 bits) */
+        const uint4 own = make_uint4(v, ((v ? 1u : 0u) << 16) | nti, nw,
+                                     PM_SK_CR * nw + (tcq || i8q ? 0u : v) + (ni8 << 20));
         uint4 x = own;
 #pragma unroll 1
         for (uint32_t o = 1; o < 32u; o <<= 1) {
@@ -262,7 +279,8 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
         for (uint32_t w2 = 0; w2 < wid; w2++) pre = pm_add4(pre, wsum[w2]);
         const uint4 incl = pm_add4(pre, x);
         const uint32_t start = incl.x - own.x, item = (incl.y >> 16) - (own.y >> 16);
-        const uint32_t tt0 = (incl.y & 0xffffu) - nti, w0 = incl.z - own.z, cst = incl.w - own.w;
+        const uint32_t tt0 = (incl.y & 0xffffu) - nti, w0 = incl.z - own.z;
+        const uint32_t cst = (incl.w & 0xfffffu) - (own.w & 0xfffffu), i80 = (incl.w >> 20) - ni8;
         if (e < a.E) {
             cnt[e] = start;
             if (v) {
@@ -278,6 +296,8 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
                 }
 #pragma unroll 1
                 for (uint32_t j = 0; j < nti; j++) a.tc_tile[tt0 + j] = make_uint2(item, j * PM_TC_N);
+#pragma unroll 1
+                for (uint32_t j = 0; j < ni8; j++) a.i8_tile[i80 + j] = make_uint2(item, j * PM_I8_N);
             }
         }
         __syncthreads();
@@ -285,7 +305,7 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
         __syncthreads();
     }
     const uint32_t tot_pairs = carry.x, tot_items = carry.y >> 16, tot_tc = carry.y & 0xffffu;
-    const uint32_t tot_work = carry.z, tot_cost = carry.w;
+    const uint32_t tot_work = carry.z, tot_cost = carry.w & 0xfffffu, tot_i8 = carry.w >> 20;
     /* fill the pair lists in (token, slot) order */
     if (masks) {
         for (uint32_t q = threadIdx.x; q < n_routed; q += blockDim.x) {
@@ -390,6 +410,7 @@ __global__ void __launch_bounds__(256) pm_layer_select_kernel(const __grid_const
         a.n_items[3] = tot_work;
         a.n_items[4] = n_tc;
         a.n_items[5] = ks;
+        a.n_items[7] = tot_i8;
         a.sk_c[tot_work + n_sh * sh_chunks] = tot_cost + n_sh * sh_cost;
         *a.sel_done = 0;
     }
@@ -621,7 +642,10 @@ static void pm_fill_args(pm_layer_args &a, const pulsar_moe_layer_desc *d, const
     a.midq = (pm_block_q8K *)(b + L.midq);
     a.tcp = (float *)(b + L.tcp);
     a.ks_max = L.ks_max;
-    a.tc_r = pm_tc_on_r(d);
+    a.tc_r = pm_tc_on_r(d, L.T);
+    a.i8 = pm_i8_on(d, L.T) ? 1u : 0u;
+    a.i8_tile = (uint2 *)(b + L.i8_tile);
+    a.max_i8 = L.max_i8;
     a.tc_s = pm_tc_on_s(d);
     a.n_sm = (uint32_t)pm_sm_count();
     a.mid = (float *)(b + L.mid);

@@ -79,9 +79,9 @@ static bool pm_tc_fmt(uint32_t q) {
 struct pm_layout {
     uint32_t T, E, k, S, n_slot, H, Fr, Fs, Fmax, hb, fb, max_items;
     uint32_t max_work;
-    uint32_t max_tc, ks_max, tc_slots, tc_waves;
+    uint32_t max_tc, ks_max, tc_slots, tc_waves, max_i8;
     uint64_t tc_slot_bytes;
-    size_t tc_ord, tc_first, tcb, tcx, tclo;
+    size_t tc_ord, tc_first, tcb, tcx, tclo, i8_tile;
     size_t logits, sel, w, xq, n_items, item_expert, item_start, work_item, work_t0, wd, sk_c, tc_tile, pairs, mid,
         midq, tcp, partial, epo, shg, ctl, total;
 };
@@ -128,11 +128,15 @@ struct pm_layer_args {
      *  res_t0, res_nt  tokens whose residual rows this call adds
      * phase: 0 selection then CSR in one launch, 1 selection only, 2 CSR only */
     uint32_t sel_t0, sel_nt, sh_t0, sh_nt, res_t0, res_nt, phase;
+    uint2 *i8_tile;           /* integer tensor-core tiles (item, first token); count n_items[7] */
+    uint32_t i8, max_i8;      /* routed experts on the integer tensor cores */
     const float *shg; /* [T] shared-expert gate logits (qwen35), or null */
     /* io */
     float *out;
     const float *residual;
 };
+
+#include "pm_tci8.cuh"
 
 /* launchers of the kernels defined in moe_layer.cu */
 int pm_launch_tc_mid(const pm_layer_args &a, const pm_layout &L, cudaStream_t st);
@@ -1017,6 +1021,8 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     /* 4: gate/up -> tensor-core split-K sums, dp4a work units -> mid */
     if constexpr (TC)
         if (tc && !pm_tc_launch<QR, QS, 2>(a, L, st)) return 0;
+    if constexpr (QR == PM_QUANT_Q2_K) /* routed Q2_K experts on the integer tensor cores */
+        if (a.i8 && !pm_i8_launch<QR, 2>(a, st)) return 0;
     const pm_skind gr = pm_kind_for(2, a.rb_gu_r, a.H);
     const pm_skp pg = pm_skp_for(2, gr, a.S ? pm_kind_for(2, a.rb_gu_s, a.H) : gr, grid);
     auto kgu = pm_layer_sk_kernel<QR, QS, 2, 0>;
@@ -1028,10 +1034,14 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     if (tc) { /* tensor-core pairs: mid and its q8_K */
         if (!pm_launch_tc_mid(a, L, st)) return 0;
     }
+    if constexpr (QR == PM_QUANT_Q2_K)
+        if (a.i8 && !pm_i8_midq_launch(a, st)) return 0;
     pm_ev(ev, 4, st);
     /* 5: down -> partial rows */
     if constexpr (TC)
         if (tc && !pm_tc_launch<QR, QS, 1>(a, L, st)) return 0;
+    if constexpr (QR == PM_QUANT_Q2_K)
+        if (a.i8 && !pm_i8_launch<QR, 1>(a, st)) return 0;
     const pm_skind dr = pm_kind_for(1, a.rb_dn_r, a.Fr);
     const pm_skp pd = pm_skp_for(1, dr, a.S ? pm_kind_for(1, a.rb_dn_s, a.Fs) : dr, grid);
     auto kdn = pm_layer_sk_kernel<QR, QS, 1, 1>;

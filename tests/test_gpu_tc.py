@@ -30,6 +30,7 @@ def test_tensor_core_tiles(oracle, quant, shared, T):
     _, sel, w = L.oracle_route(x)
     ref, ref_mid = L.oracle_ffn(x, sel, w, return_mid=True)
     dl = L.to_device()
+    dl.desc().path_flags = 1  # PULSAR_LAYER_NO_I8: Q2_K experts on the fp16 tiles too
     wst = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
     out = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
     dl.forward(torch.from_numpy(x).cuda(), out, wst)
@@ -85,6 +86,7 @@ def test_tensor_core_weight_images(oracle, quant):
     L = HostLayer(H=512, F=512, E=4, k=2, quant=quant, seed=31, router_mode=0)
     x = np.random.default_rng(6).normal(0, 1, (T, L.H)).astype(np.float32)
     dl = L.to_device()
+    dl.desc().path_flags = 1  # PULSAR_LAYER_NO_I8: Q2_K experts on the fp16 tiles too
     wst = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
     out = torch.zeros((T, L.H), dtype=torch.float32, device="cuda")
     dl.forward(torch.from_numpy(x).cuda(), out, wst)
