@@ -98,10 +98,11 @@ struct pm_i8_smem {
     static constexpr uint32_t OFF_B = OFF_A + 2u * NM * A;      /* [2 buffers] 32 x 128 */
     static constexpr uint32_t OFF_RAW = OFF_B + 2u * 4096u;     /* [RS][NM][128][PITCH] */
     static constexpr uint32_t RAW_STAGE = NM * 128u * PM_I8_PITCH;
-    static constexpr uint32_t OFF_SIDE = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [AC][NM][128] uint4 */
-    static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 16u; /* [AC][32] 9 words */
+    static constexpr uint32_t OFF_SIDE = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [AC][NM][128] 2 x uint4 */
+    static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 32u; /* [AC][32] 9 words */
     static constexpr uint32_t ASIDE_T = 40u;                    /* yd, lo[4], hi[4] (+ pad) */
     static constexpr uint32_t TOTAL = OFF_ASIDE + PM_I8_AC * PM_I8_N * ASIDE_T;
+    static_assert(TOTAL + 1024u <= 227u * 1024u, "integer tensor-core pass exceeds shared memory");
 };
 
 /* one task = (tile, 128-row block) */
