@@ -40,7 +40,7 @@
 #include "pm_tc.cuh"
 
 #define PM_I8_N 32u      /* tokens per tile (MMA N: 16 or 32) */
-#define PM_I8_RS 4u      /* raw ring depth (super-blocks) */
+#define PM_I8_RS 3u      /* raw ring depth (super-blocks) */
 #define PM_I8_AC 4u      /* tensor-memory / side-data slots (super-blocks) */
 #define PM_I8_PITCH 112u /* raw bytes per row per matrix per super-block (84 + alignment) */
 #define PM_I8_THREADS 288u
@@ -98,7 +98,9 @@ struct pm_i8_smem {
     static constexpr uint32_t OFF_B = OFF_A + 2u * NM * A;      /* [2 buffers] 32 x 128 */
     static constexpr uint32_t OFF_RAW = OFF_B + 2u * 4096u;     /* [RS][NM][128][PITCH] */
     static constexpr uint32_t RAW_STAGE = NM * 128u * PM_I8_PITCH;
-    static constexpr uint32_t OFF_SIDE = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [AC][NM][128] 2 x uint4 */
+    static constexpr uint32_t OFF_ARAW = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [RS][32 tokens] q8_K blocks */
+    static constexpr uint32_t ARAW_T = 320u;                    /* 292 bytes + alignment */
+    static constexpr uint32_t OFF_SIDE = OFF_ARAW + PM_I8_RS * PM_I8_N * ARAW_T; /* [AC][NM][128] 2 x uint4 */
     static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 32u; /* [AC][32] 9 words */
     static constexpr uint32_t ASIDE_T = 40u;                    /* yd, lo[4], hi[4] (+ pad) */
     static constexpr uint32_t TOTAL = OFF_ASIDE + PM_I8_AC * PM_I8_N * ASIDE_T;
@@ -200,39 +202,51 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     const uint32_t G = my_tasks * nsb;
 
     if (warp < 4) {
-        /* ===== decode warps: thread r = weight row r of the block ===== */
-        const uint32_t r = tid;
-        uint32_t issued = 0; /* super-blocks whose raw rows this thread has requested */
+        /* ===== decode warps: thread r = weight row r of the block; threads 4 tk .. 4 tk + 3
+         * (one warp) also carry token tk's activation block ===== */
+        const uint32_t r = tid, tk = r >> 2, q = r & 3u;
+        uint32_t issued = 0;      /* super-blocks whose raw rows this thread has requested */
+        uint32_t iss_task = ~0u;  /* the task of the last request, its token count and pair */
+        pm_i8_task ti;
+        uint32_t iss_pair = 0;
         auto issue = [&](uint32_t g) {
-            pm_i8_task t;
-            pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
-            const uint32_t sb = g % nsb, slot = g % PM_I8_RS;
-            uint32_t bytes = 0;
-            uint8_t *dst = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + r * PM_I8_PITCH;
+            const uint32_t task = g / nsb, sb = g % nsb, slot = g % PM_I8_RS;
+            if (task != iss_task) {
+                pm_i8_task_get<NM>(a, blockIdx.x + task * gridDim.x, nrb, n_tiles, ti);
+                iss_pair = q == 0u && tk < ti.nt ? __ldcg(a.pairs + ti.s0 + tk) : 0u;
+                iss_task = task;
+            }
+            uintptr_t src[NM + 1], s0[NM + 1];
+            uint32_t len[NM + 1], bytes = 0;
 #pragma unroll
-            for (int m = 0; m < NM; m++) {
-                const uintptr_t src = (uintptr_t)(t.w[m] + (uint64_t)r * t.rb + (uint64_t)sb * PM_Q2_K_BYTES);
-                const uintptr_t s0 = src & ~(uintptr_t)15, s1 = (src + PM_Q2_K_BYTES + 15u) & ~(uintptr_t)15;
-                bytes += (uint32_t)(s1 - s0);
+            for (int m = 0; m < NM; m++) src[m] = (uintptr_t)(ti.w[m] + (uint64_t)r * ti.rb + (uint64_t)sb * PM_Q2_K_BYTES);
+            const bool act = q == 0u && tk < ti.nt; /* this thread copies token tk's q8_K block */
+            src[NM] = act ? (uintptr_t)(pm_i8_xrow<NM>(a, iss_pair) + sb) : 0;
+#pragma unroll
+            for (int m = 0; m <= NM; m++) {
+                const uint32_t n = m < NM ? PM_Q2_K_BYTES : PM_Q8_K_BYTES;
+                s0[m] = src[m] & ~(uintptr_t)15;
+                len[m] = (uint32_t)(((src[m] + n + 15u) & ~(uintptr_t)15) - s0[m]);
+                if (m < NM || act) bytes += len[m];
             }
             pm_mbar_arrive_tx(&raw_full[slot], bytes);
+            uint8_t *dst = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + r * PM_I8_PITCH;
 #pragma unroll
-            for (int m = 0; m < NM; m++) {
-                const uintptr_t src = (uintptr_t)(t.w[m] + (uint64_t)r * t.rb + (uint64_t)sb * PM_Q2_K_BYTES);
-                const uintptr_t s0 = src & ~(uintptr_t)15, s1 = (src + PM_Q2_K_BYTES + 15u) & ~(uintptr_t)15;
-                pm_bulk_g2s(dst + (uint32_t)m * 128u * PM_I8_PITCH, (const void *)s0, (uint32_t)(s1 - s0),
+            for (int m = 0; m < NM; m++)
+                pm_bulk_g2s(dst + (uint32_t)m * 128u * PM_I8_PITCH, (const void *)s0[m], len[m], &raw_full[slot]);
+            if (act)
+                pm_bulk_g2s(sm + SM::OFF_ARAW + (slot * PM_I8_N + tk) * SM::ARAW_T, (const void *)s0[NM], len[NM],
                             &raw_full[slot]);
-            }
         };
         while (issued < G && issued < PM_I8_RS) issue(issued++);
         bool fail = false;
         pm_i8_task t;
-        uint32_t my_pair = 0;
+        uint32_t a_off = 0; /* byte offset of token tk's block inside its 16-byte-aligned copy */
         for (uint32_t g = 0; g < G && !fail; g++) {
             const uint32_t sb = g % nsb;
             if (sb == 0) {
                 pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
-                my_pair = (r >> 2) < t.nt ? __ldcg(a.pairs + t.s0 + (r >> 2)) : 0u; /* this thread's B token */
+                a_off = tk < t.nt ? (uint32_t)((uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + t.s0 + tk)) & 15u) : 0u;
             }
             const uint32_t slot = g % PM_I8_RS, x = g % PM_I8_AC;
             if (!pm_mbar_wait_sleep(&raw_full[slot], (g / PM_I8_RS) & 1u, a.err, a.wait)) {
@@ -245,6 +259,9 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 break;
             }
             const uint8_t *raw = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + r * PM_I8_PITCH;
+            /* token tk's q8_K block (292 bytes; 292 * i = 4 mod 16, so blocks sit at 4-byte offsets) */
+            const uint8_t *araw = sm + SM::OFF_ARAW + (slot * PM_I8_N + tk) * SM::ARAW_T;
+            const uint32_t aoff = (a_off + (uint32_t)sb * PM_Q8_K_BYTES) & 15u;
             uint32_t off[NM];
 #pragma unroll
             for (int m = 0; m < NM; m++) {
@@ -268,37 +285,28 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 side[1] = make_uint4((scw[m][2] >> 4) & 0x0f0f0f0fu, (scw[m][3] >> 4) & 0x0f0f0f0fu, 0u, 0u);
             }
             /* per (token, super-block): yd and the bsums split in low / high bytes */
-            if (r < t.nt * 4u && (r & 3u) == 0u) {
-                const pm_block_q8K *xr = pm_i8_xrow<NM>(a, my_pair) + sb;
-                const uint32_t *bw = (const uint32_t *)((const uint8_t *)xr + 260);
+            if (q == 0u && tk < t.nt) {
+                uint32_t bw[9];
+                pm_i8_lds<1>(araw, (aoff + 0u) & ~3u, bw);         /* d */
+                pm_i8_lds<8>(araw, (aoff + 260u) & ~3u, bw + 1);   /* bsums[16] */
                 uint32_t lo[4], hi[4];
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const uint32_t b01 = __ldcg(bw + 2 * q), b23 = __ldcg(bw + 2 * q + 1);
-                    /* bsums j = 4q .. 4q + 3 as int16; low bytes unsigned, high bytes signed */
-                    lo[q] = (b01 & 0xffu) | ((b01 >> 8) & 0xff00u) | ((b23 & 0xffu) << 16) | ((b23 << 8) & 0xff000000u);
-                    hi[q] = ((b01 >> 8) & 0xffu) | ((b01 >> 16) & 0xff00u) | (((b23 >> 8) & 0xffu) << 16) |
-                            (b23 & 0xff000000u);
+                for (int qq = 0; qq < 4; qq++) {
+                    const uint32_t b01 = bw[1 + 2 * qq], b23 = bw[2 + 2 * qq];
+                    /* bsums j = 4qq .. 4qq + 3 as int16; low bytes unsigned, high bytes signed */
+                    lo[qq] = (b01 & 0xffu) | ((b01 >> 8) & 0xff00u) | ((b23 & 0xffu) << 16) | ((b23 << 8) & 0xff000000u);
+                    hi[qq] = ((b01 >> 8) & 0xffu) | ((b01 >> 16) & 0xff00u) | (((b23 >> 8) & 0xffu) << 16) |
+                             (b23 & 0xff000000u);
                 }
-                uint32_t *as = (uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + (r >> 2)) * SM::ASIDE_T);
-                as[0] = __float_as_uint(__ldcg(&xr->d));
+                uint32_t *as = (uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + tk) * SM::ASIDE_T);
+                as[0] = bw[0];
 #pragma unroll
-                for (int q = 0; q < 4; q++) as[1 + q] = lo[q], as[5 + q] = hi[q];
+                for (int qq = 0; qq < 4; qq++) as[1 + qq] = lo[qq], as[5 + qq] = hi[qq];
             }
             /* the two 128-wide K chunks of the super-block */
 #pragma unroll 1
             for (uint32_t h = 0; h < 2; h++) {
                 const uint32_t c = 2u * g + h, ab = c & 1u;
-                /* B: 4 threads per token row, 32 q8 bytes each (loads first, stores after the
-                 * decode so their latency hides behind it); rows past nt are zero */
-                const uint32_t tk = r >> 2, q = r & 3u;
-                uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
-                if (tk < t.nt) {
-                    const pm_block_q8K *xr = pm_i8_xrow<NM>(a, my_pair) + sb;
-                    const uint32_t *src = (const uint32_t *)((const uint8_t *)xr + 4 + 128u * h + 32u * q);
-                    v0 = make_uint4(__ldcg(src), __ldcg(src + 1), __ldcg(src + 2), __ldcg(src + 3));
-                    v1 = make_uint4(__ldcg(src + 4), __ldcg(src + 5), __ldcg(src + 6), __ldcg(src + 7));
-                }
                 if (c >= 2 && !pm_mbar_wait_sleep(&a_empty[ab], ((c >> 1) - 1u) & 1u, a.err, a.wait)) {
                     fail = true;
                     break;
@@ -321,14 +329,19 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                         *(uint4 *)(A + ((j ^ (r & 7u)) << 4)) = o;
                     }
                 }
+                /* B: 4 threads per token row, 32 q8 bytes each from the staged block; rows past nt zero */
+                uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                if (tk < t.nt) pm_i8_lds<8>(araw, aoff + 4u + 128u * h + 32u * q, bv);
                 uint8_t *B = sm + SM::OFF_B + ab * 4096u + (tk >> 3) * 1024u + (tk & 7u) * 128u;
-                *(uint4 *)(B + (((2u * q) ^ (tk & 7u)) << 4)) = v0;
-                *(uint4 *)(B + (((2u * q + 1u) ^ (tk & 7u)) << 4)) = v1;
+                *(uint4 *)(B + (((2u * q) ^ (tk & 7u)) << 4)) = make_uint4(bv[0], bv[1], bv[2], bv[3]);
+                *(uint4 *)(B + (((2u * q + 1u) ^ (tk & 7u)) << 4)) = make_uint4(bv[4], bv[5], bv[6], bv[7]);
                 pm_fence_proxy_async(); /* generic-proxy writes before the MMA reads them */
                 pm_mbar_arrive(&a_full[ab]);
             }
             if (fail) break;
-            /* the raw rows of this super-block are consumed: request a later one */
+            /* the raw rows (and token blocks, read within this warp) of this super-block are
+             * consumed: request a later one into the slot */
+            __syncwarp();
             if (issued < G) issue(issued++);
         }
         if (fail) atomicOr(&s_fail, 1u);
