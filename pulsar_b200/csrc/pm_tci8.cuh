@@ -21,8 +21,11 @@
  * matrices).  Persistent CTAs take tasks round-robin and stream their
  * super-blocks through four pipelines:
  *   raw     each decode thread (one weight row) copies its row's 84 bytes
- *           of every matrix per super-block with a 1-D bulk copy (rounded
- *           out to 16 bytes) into a 4-deep ring, completed on an mbarrier;
+ *           of every matrix per super-block, and the 4 threads of a token
+ *           its q8_K block, in 16-byte asynchronous copies (rounded out)
+ *           into a 3-deep ring, each thread's copies arriving on an mbarrier
+ *           (many small row pieces: the bulk-copy engine would serialize
+ *           hundreds of 100-byte requests per super-block);
  *   decode  4 warps turn raw rows into int8 A tiles (q sc, 128 rows x 128 K,
  *           128-byte swizzle), stage the tokens' q8 values as the B tile
  *           and the per-(row, super-block) scales / per-(token,
@@ -76,6 +79,17 @@ __device__ __forceinline__ void pm_tmem_ld16i(uint32_t taddr, int32_t *v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = (int32_t)r[i];
+}
+
+/* 16-byte asynchronous copy global -> shared (L2 only), both 16-byte aligned */
+__device__ __forceinline__ void pm_cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pm_smem_addr(dst)), "l"(src) : "memory");
+}
+
+/* one arrival on bar once every cp.async this thread issued so far has landed
+ * (the barrier's count includes it) */
+__device__ __forceinline__ void pm_cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(pm_smem_addr(bar)) : "memory");
 }
 
 /* arrive on bar (count 1) after this thread's bulk copies of `bytes` */
@@ -213,30 +227,29 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             const uint32_t task = g / nsb, sb = g % nsb, slot = g % PM_I8_RS;
             if (task != iss_task) {
                 pm_i8_task_get<NM>(a, blockIdx.x + task * gridDim.x, nrb, n_tiles, ti);
-                iss_pair = q == 0u && tk < ti.nt ? __ldcg(a.pairs + ti.s0 + tk) : 0u;
+                iss_pair = tk < ti.nt ? __ldcg(a.pairs + ti.s0 + tk) : 0u;
                 iss_task = task;
             }
-            uintptr_t src[NM + 1], s0[NM + 1];
-            uint32_t len[NM + 1], bytes = 0;
-#pragma unroll
-            for (int m = 0; m < NM; m++) src[m] = (uintptr_t)(ti.w[m] + (uint64_t)r * ti.rb + (uint64_t)sb * PM_Q2_K_BYTES);
-            const bool act = q == 0u && tk < ti.nt; /* this thread copies token tk's q8_K block */
-            src[NM] = act ? (uintptr_t)(pm_i8_xrow<NM>(a, iss_pair) + sb) : 0;
-#pragma unroll
-            for (int m = 0; m <= NM; m++) {
-                const uint32_t n = m < NM ? PM_Q2_K_BYTES : PM_Q8_K_BYTES;
-                s0[m] = src[m] & ~(uintptr_t)15;
-                len[m] = (uint32_t)(((src[m] + n + 15u) & ~(uintptr_t)15) - s0[m]);
-                if (m < NM || act) bytes += len[m];
-            }
-            pm_mbar_arrive_tx(&raw_full[slot], bytes);
             uint8_t *dst = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + r * PM_I8_PITCH;
 #pragma unroll
-            for (int m = 0; m < NM; m++)
-                pm_bulk_g2s(dst + (uint32_t)m * 128u * PM_I8_PITCH, (const void *)s0[m], len[m], &raw_full[slot]);
-            if (act)
-                pm_bulk_g2s(sm + SM::OFF_ARAW + (slot * PM_I8_N + tk) * SM::ARAW_T, (const void *)s0[NM], len[NM],
-                            &raw_full[slot]);
+            for (int m = 0; m < NM; m++) { /* the row's 84 bytes, rounded out to 16-byte pieces */
+                const uintptr_t src = (uintptr_t)(ti.w[m] + (uint64_t)r * ti.rb + (uint64_t)sb * PM_Q2_K_BYTES);
+                const uintptr_t s0 = src & ~(uintptr_t)15;
+                const uint32_t n16 = (uint32_t)((((src + PM_Q2_K_BYTES + 15u) & ~(uintptr_t)15) - s0) >> 4);
+#pragma unroll
+                for (uint32_t k = 0; k < 7; k++)
+                    if (k < n16) pm_cp_async16(dst + (uint32_t)m * 128u * PM_I8_PITCH + 16u * k, (const void *)(s0 + 16u * k));
+            }
+            if (tk < ti.nt) { /* token tk's q8_K block, a quarter per thread of the token */
+                const uintptr_t src = (uintptr_t)(pm_i8_xrow<NM>(a, iss_pair) + sb);
+                const uintptr_t s0 = src & ~(uintptr_t)15;
+                const uint32_t n16 = (uint32_t)((((src + PM_Q8_K_BYTES + 15u) & ~(uintptr_t)15) - s0) >> 4);
+                uint8_t *ad = sm + SM::OFF_ARAW + (slot * PM_I8_N + tk) * SM::ARAW_T;
+#pragma unroll
+                for (uint32_t k = q; k < 20; k += 4)
+                    if (k < n16) pm_cp_async16(ad + 16u * k, (const void *)(s0 + 16u * k));
+            }
+            pm_cp_async_arrive(&raw_full[slot]); /* arrives when this thread's copies have landed */
         };
         while (issued < G && issued < PM_I8_RS) issue(issued++);
         bool fail = false;
