@@ -184,8 +184,11 @@ typedef struct pulsar_moe_layer_desc {
 } pulsar_moe_layer_desc;
 
 /* path_flags: keep routed Q2_K experts off the integer tensor-core passes
- * (dp4a engine / fp16 tensor-core tiles instead; for comparisons) */
+ * (dp4a engine / fp16 tensor-core tiles instead), or put them there even
+ * below the default threshold of 8 tokens per expert on average; for
+ * comparisons and tests */
 #define PULSAR_LAYER_NO_I8 1u
+#define PULSAR_LAYER_FORCE_I8 2u
 
 /* pulsar_rms_norm on an explicit stream (cudaStream_t, NULL = per-thread default) */
 int pulsar_rms_norm_stream(void *out, const void *x, const void *w, uint32_t n, uint32_t rows, float eps,

@@ -26,7 +26,8 @@ QUANT_MXFP4 = 12
 QUANTS = {"Q2_K": QUANT_Q2_K, "IQ2_XXS": QUANT_IQ2_XXS, "Q4_K": QUANT_Q4_K, "Q8_0": QUANT_Q8_0,
           "MXFP4": QUANT_MXFP4}
 Q8K_BLOCK_BYTES = 292
-LAYER_NO_I8 = 1  # path_flags: routed Q2_K experts off the integer tensor cores
+LAYER_NO_I8 = 1     # path_flags: routed Q2_K experts off the integer tensor cores
+LAYER_FORCE_I8 = 2  # path_flags: routed Q2_K experts on the integer tensor cores below the default threshold
 
 
 class KernelError(RuntimeError):

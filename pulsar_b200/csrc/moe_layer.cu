@@ -55,13 +55,16 @@ static int pm_sm_count() {
 static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
 
 /* routed Q2_K experts on the integer tensor cores (pm_tci8.cuh): whole
- * super-blocks, 128-row blocks, and the select kernel's 20-bit cost / 12-bit
- * tile packing; the descriptor's PULSAR_LAYER_NO_I8 flag keeps them on the
- * dp4a / fp16 tensor-core paths */
+ * super-blocks, the select kernel's 20-bit cost / 12-bit tile packing, and
+ * enough tokens per expert on average (T k >= 8 E) for the tiles to pay for
+ * their fixed per-super-block cost; below that the dp4a engine streams the
+ * weights faster.  PULSAR_LAYER_NO_I8 / PULSAR_LAYER_FORCE_I8 override. */
 static bool pm_i8_on(const pulsar_moe_layer_desc *d, uint32_t T) {
     const uint64_t routed = (uint64_t)T * d->n_used;
-    return !(d->path_flags & PULSAR_LAYER_NO_I8) && d->quant == PM_QUANT_Q2_K && d->n_embd % 256u == 0 &&
-           d->n_ff % 256u == 0 && routed < (1u << 19) && routed / PM_I8_N + d->n_expert < 4000u;
+    const bool fits = d->quant == PM_QUANT_Q2_K && d->n_embd % 256u == 0 && d->n_ff % 256u == 0 &&
+                      routed < (1u << 19) && routed / PM_I8_N + d->n_expert < 4000u;
+    if (!fits || (d->path_flags & PULSAR_LAYER_NO_I8)) return false;
+    return (d->path_flags & PULSAR_LAYER_FORCE_I8) || routed >= 8ull * d->n_expert;
 }
 
 /* tensor-core path available for the routed / shared experts */

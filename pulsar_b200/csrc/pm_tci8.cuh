@@ -20,13 +20,15 @@
  * kernel lists them); a task is (tile, 128-row block of the pass's
  * matrices).  Persistent CTAs take tasks round-robin and stream their
  * super-blocks through four pipelines:
- *   raw     each decode thread (one weight row) copies its row's 84 bytes
- *           of every matrix per super-block, and the 4 threads of a token
- *           its q8_K block, in 16-byte asynchronous copies (rounded out)
- *           into a 3-deep ring, each thread's copies arriving on an mbarrier
- *           (many small row pieces: the bulk-copy engine would serialize
- *           hundreds of 100-byte requests per super-block);
- *   decode  4 warps turn raw rows into int8 A tiles (q sc, 128 rows x 128 K,
+ *   raw     every decode thread copies exactly the bytes it later reads
+ *           (its row's 84 bytes of a matrix per super-block, a quarter of a
+ *           token's q8 values, the token's scale and bsums) in 16-byte
+ *           asynchronous copies (rounded out) into a 2-deep ring, one copy
+ *           group per super-block, waited on by the thread itself: no
+ *           cross-thread hand-off on the weight stream (the bulk-copy engine
+ *           would serialize hundreds of 100-byte requests per super-block,
+ *           and a CTA-wide barrier per super-block cost ~1 us);
+ *   decode  8 warps turn raw rows into int8 A tiles (q sc, 128 rows x 128 K,
  *           128-byte swizzle), stage the tokens' q8 values as the B tile
  *           and the per-(row, super-block) scales / per-(token,
  *           super-block) bsums for the epilogue;
@@ -43,10 +45,10 @@
 #include "pm_tc.cuh"
 
 #define PM_I8_N 32u      /* tokens per tile (MMA N: 16 or 32) */
-#define PM_I8_RS 3u      /* raw ring depth (super-blocks) */
+#define PM_I8_RS 2u      /* raw ring depth (super-blocks) */
 #define PM_I8_AC 4u      /* tensor-memory / side-data slots (super-blocks) */
 #define PM_I8_PITCH 112u /* raw bytes per row per matrix per super-block (84 + alignment) */
-#define PM_I8_THREADS 288u
+#define PM_I8_THREADS 416u /* 8 decode warps, 4 epilogue warps, 1 MMA warp */
 
 /* kind::i8 instruction descriptor: A, B signed 8-bit, D s32, K-major */
 __host__ __device__ __forceinline__ uint32_t pm_idesc_i8(uint32_t M, uint32_t N) {
@@ -81,6 +83,12 @@ __device__ __forceinline__ void pm_tmem_ld16i(uint32_t taddr, int32_t *v) {
     for (int i = 0; i < 16; i++) v[i] = (int32_t)r[i];
 }
 
+/* close this thread's group of asynchronous copies / wait until at most N
+ * of its groups are still in flight */
+__device__ __forceinline__ void pm_cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void pm_cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 /* 16-byte asynchronous copy global -> shared (L2 only), both 16-byte aligned */
 __device__ __forceinline__ void pm_cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pm_smem_addr(dst)), "l"(src) : "memory");
@@ -110,11 +118,12 @@ struct pm_i8_smem {
     static constexpr uint32_t A = 16384u;                      /* one 128 x 128 int8 tile */
     static constexpr uint32_t OFF_A = 0;                        /* [2 buffers][NM] */
     static constexpr uint32_t OFF_B = OFF_A + 2u * NM * A;      /* [2 buffers] 32 x 128 */
-    static constexpr uint32_t OFF_RAW = OFF_B + 2u * 4096u;     /* [RS][NM][128][PITCH] */
-    static constexpr uint32_t RAW_STAGE = NM * 128u * PM_I8_PITCH;
-    static constexpr uint32_t OFF_ARAW = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [RS][32 tokens] q8_K blocks */
-    static constexpr uint32_t ARAW_T = 320u;                    /* 292 bytes + alignment */
-    static constexpr uint32_t OFF_SIDE = OFF_ARAW + PM_I8_RS * PM_I8_N * ARAW_T; /* [AC][NM][128] 2 x uint4 */
+    static constexpr uint32_t OFF_RAW = OFF_B + 2u * 4096u;     /* [RS][2 parts][128][PITCH] */
+    static constexpr uint32_t RAW_STAGE = 2u * 128u * PM_I8_PITCH;
+    static constexpr uint32_t OFF_ARAW = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [RS][2][32 tokens][4] 48 B */
+    static constexpr uint32_t ARAW_STAGE = 2u * PM_I8_N * 4u * 48u;
+    static constexpr uint32_t OFF_ASRAW = OFF_ARAW + PM_I8_RS * ARAW_STAGE; /* [RS][32 tokens] 64 B */
+    static constexpr uint32_t OFF_SIDE = OFF_ASRAW + PM_I8_RS * PM_I8_N * 64u; /* [AC][NM][128] 2 x uint4 */
     static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 32u; /* [AC][32] 9 words */
     static constexpr uint32_t ASIDE_T = 40u;                    /* yd, lo[4], hi[4] (+ pad) */
     static constexpr uint32_t TOTAL = OFF_ASIDE + PM_I8_AC * PM_I8_N * ASIDE_T;
@@ -183,7 +192,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     using SM = pm_i8_smem<NM>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023u) & ~(uintptr_t)1023u);
-    __shared__ uint64_t raw_full[PM_I8_RS], a_full[2], a_empty[2], acc_full[PM_I8_AC], acc_empty[PM_I8_AC], fin;
+    __shared__ uint64_t a_full[2], a_empty[2], acc_full[PM_I8_AC], acc_empty[PM_I8_AC], fin;
     __shared__ uint32_t tslot, s_fail;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t n_tiles = __ldcg(a.n_items + 7);
@@ -191,11 +200,10 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     const uint32_t nsb = (NM == 2 ? a.H : a.Fr) / 256u;
     const uint32_t n_tasks = n_tiles * nrb;
     if (blockIdx.x >= n_tasks) return;
-    if (warp == 8) pm_tmem_alloc(&tslot, 256);
+    if (warp == 12) pm_tmem_alloc(&tslot, 256);
     if (tid == 0) {
-        for (uint32_t i = 0; i < PM_I8_RS; i++) pm_mbar_init(&raw_full[i], 128);
         for (uint32_t i = 0; i < 2; i++) {
-            pm_mbar_init(&a_full[i], 128);
+            pm_mbar_init(&a_full[i], 256);
             pm_mbar_init(&a_empty[i], 1);
         }
         for (uint32_t i = 0; i < PM_I8_AC; i++) {
@@ -215,93 +223,99 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     const uint32_t my_tasks = (n_tasks - blockIdx.x + gridDim.x - 1) / gridDim.x;
     const uint32_t G = my_tasks * nsb;
 
-    if (warp < 4) {
-        /* ===== decode warps: thread r = weight row r of the block; threads 4 tk .. 4 tk + 3
-         * (one warp) also carry token tk's activation block ===== */
-        const uint32_t r = tid, tk = r >> 2, q = r & 3u;
-        uint32_t issued = 0;      /* super-blocks whose raw rows this thread has requested */
-        uint32_t iss_task = ~0u;  /* the task of the last request, its token count and pair */
+    if (warp < 8) {
+        /* ===== decode warps: thread (r, p) = weight row r, part p.  NM 2: part p takes
+         * matrix p; NM 1: part p takes K chunk p of the one matrix.  As token (tk, q) a thread
+         * also stages quarter q of token tk's chunk-p q8 values (B), and (p, q) = (0, 0) the
+         * token's scale and bsums.  Every thread copies exactly the bytes it later reads, with
+         * its own asynchronous-copy groups (one per super-block): no cross-thread hand-off. ===== */
+        const uint32_t r = tid & 127u, p = tid >> 7, tk = r >> 2, q = r & 3u;
+        const uint32_t m = NM == 2 ? p : 0u; /* the matrix this thread decodes */
+        uint32_t iss_task = ~0u;             /* the task of the last request and this thread's token block */
         pm_i8_task ti;
-        uint32_t iss_pair = 0;
+        uintptr_t iss_blk = 0;
         auto issue = [&](uint32_t g) {
             const uint32_t task = g / nsb, sb = g % nsb, slot = g % PM_I8_RS;
             if (task != iss_task) {
                 pm_i8_task_get<NM>(a, blockIdx.x + task * gridDim.x, nrb, n_tiles, ti);
-                iss_pair = tk < ti.nt ? __ldcg(a.pairs + ti.s0 + tk) : 0u;
+                iss_blk = tk < ti.nt ? (uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + ti.s0 + tk)) : 0;
                 iss_task = task;
             }
-            uint8_t *dst = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + r * PM_I8_PITCH;
-#pragma unroll
-            for (int m = 0; m < NM; m++) { /* the row's 84 bytes, rounded out to 16-byte pieces */
+            { /* the row's 84 bytes of matrix m, rounded out to 16-byte pieces */
+                uint8_t *dst = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + (p * 128u + r) * PM_I8_PITCH;
                 const uintptr_t src = (uintptr_t)(ti.w[m] + (uint64_t)r * ti.rb + (uint64_t)sb * PM_Q2_K_BYTES);
                 const uintptr_t s0 = src & ~(uintptr_t)15;
                 const uint32_t n16 = (uint32_t)((((src + PM_Q2_K_BYTES + 15u) & ~(uintptr_t)15) - s0) >> 4);
 #pragma unroll
                 for (uint32_t k = 0; k < 7; k++)
-                    if (k < n16) pm_cp_async16(dst + (uint32_t)m * 128u * PM_I8_PITCH + 16u * k, (const void *)(s0 + 16u * k));
+                    if (k < n16) pm_cp_async16(dst + 16u * k, (const void *)(s0 + 16u * k));
             }
-            if (tk < ti.nt) { /* token tk's q8_K block, a quarter per thread of the token */
-                const uintptr_t src = (uintptr_t)(pm_i8_xrow<NM>(a, iss_pair) + sb);
-                const uintptr_t s0 = src & ~(uintptr_t)15;
-                const uint32_t n16 = (uint32_t)((((src + PM_Q8_K_BYTES + 15u) & ~(uintptr_t)15) - s0) >> 4);
-                uint8_t *ad = sm + SM::OFF_ARAW + (slot * PM_I8_N + tk) * SM::ARAW_T;
+            if (tk < ti.nt) {
+                const uintptr_t blk = iss_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
+                { /* quarter q of chunk p's q8 values: 32 bytes from 4 + 128 p + 32 q */
+                    const uintptr_t src = blk + 4u + 128u * p + 32u * q, s0 = src & ~(uintptr_t)15;
+                    const uint32_t n16 = (uint32_t)((((src + 32u + 15u) & ~(uintptr_t)15) - s0) >> 4);
+                    uint8_t *dst = sm + SM::OFF_ARAW + slot * SM::ARAW_STAGE + ((p * PM_I8_N + tk) * 4u + q) * 48u;
 #pragma unroll
-                for (uint32_t k = q; k < 20; k += 4)
-                    if (k < n16) pm_cp_async16(ad + 16u * k, (const void *)(s0 + 16u * k));
+                    for (uint32_t k = 0; k < 3; k++)
+                        if (k < n16) pm_cp_async16(dst + 16u * k, (const void *)(s0 + 16u * k));
+                }
+                if (p == 0u && q == 0u) { /* the scale d (bytes 0-3) and bsums (260-291) */
+                    uint8_t *dst = sm + SM::OFF_ASRAW + (slot * PM_I8_N + tk) * 64u;
+                    pm_cp_async16(dst, (const void *)(blk & ~(uintptr_t)15));
+                    const uintptr_t src = blk + 260u, s0 = src & ~(uintptr_t)15;
+                    const uint32_t n16 = (uint32_t)((((src + 32u + 15u) & ~(uintptr_t)15) - s0) >> 4);
+#pragma unroll
+                    for (uint32_t k = 0; k < 3; k++)
+                        if (k < n16) pm_cp_async16(dst + 16u + 16u * k, (const void *)(s0 + 16u * k));
+                }
             }
-            pm_cp_async_arrive(&raw_full[slot]); /* arrives when this thread's copies have landed */
         };
-        while (issued < G && issued < PM_I8_RS) issue(issued++);
+#pragma unroll
+        for (uint32_t g = 0; g < PM_I8_RS; g++) {
+            if (g < G) issue(g);
+            pm_cp_async_commit(); /* one group per super-block (empty past the end) */
+        }
         bool fail = false;
         pm_i8_task t;
-        uint32_t a_off = 0; /* byte offset of token tk's block inside its 16-byte-aligned copy */
+        uintptr_t my_blk = 0; /* token tk's q8_K row (block 0) */
         for (uint32_t g = 0; g < G && !fail; g++) {
             const uint32_t sb = g % nsb;
             if (sb == 0) {
                 pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
-                a_off = tk < t.nt ? (uint32_t)((uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + t.s0 + tk)) & 15u) : 0u;
+                my_blk = tk < t.nt ? (uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + t.s0 + tk)) : 0;
             }
             const uint32_t slot = g % PM_I8_RS, x = g % PM_I8_AC;
-            if (!pm_mbar_wait_sleep(&raw_full[slot], (g / PM_I8_RS) & 1u, a.err, a.wait)) {
-                fail = true;
-                break;
-            }
+            pm_cp_async_wait<PM_I8_RS - 1>(); /* this thread's copies of super-block g have landed */
             /* side slot x is free once the epilogue finished super-block g - AC */
-            if (g >= PM_I8_AC && !pm_mbar_wait_sleep(&acc_empty[x], ((g / PM_I8_AC) - 1u) & 1u, a.err, a.wait)) {
+            if (g >= PM_I8_AC && !pm_mbar_wait(&acc_empty[x], ((g / PM_I8_AC) - 1u) & 1u, a.err, a.wait)) {
                 fail = true;
                 break;
             }
-            const uint8_t *raw = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + r * PM_I8_PITCH;
-            /* token tk's q8_K block (292 bytes; 292 * i = 4 mod 16, so blocks sit at 4-byte offsets) */
-            const uint8_t *araw = sm + SM::OFF_ARAW + (slot * PM_I8_N + tk) * SM::ARAW_T;
-            const uint32_t aoff = (a_off + (uint32_t)sb * PM_Q8_K_BYTES) & 15u;
-            uint32_t off[NM];
-#pragma unroll
-            for (int m = 0; m < NM; m++) {
-                const uintptr_t src = (uintptr_t)(t.w[m] + (uint64_t)r * t.rb + (uint64_t)sb * PM_Q2_K_BYTES);
-                off[m] = (uint32_t)m * 128u * PM_I8_PITCH + (uint32_t)(src & 15u);
-            }
-            /* side data of (row, super-block): d, dmin, and the 16 4-bit mins as bytes */
-            uint32_t scw[NM][4];
-#pragma unroll
-            for (int m = 0; m < NM; m++) {
-                pm_i8_lds<4>(raw, off[m], scw[m]);
+            const uint8_t *raw = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + (p * 128u + r) * PM_I8_PITCH;
+            const uint32_t off = (uint32_t)((uintptr_t)(t.w[m] + (uint64_t)r * t.rb + (uint64_t)sb * PM_Q2_K_BYTES) & 15u);
+            const uintptr_t blk = my_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
+            /* the row's 16 scale bytes (low nibble: scale, high nibble: min) */
+            uint32_t scw[4];
+            pm_i8_lds<4>(raw, off, scw);
+            if (NM == 2 || p == 0u) { /* side data of (row, super-block, matrix m): d, dmin, 16 mins as bytes */
                 uint32_t dd[1];
-                pm_i8_lds<1>(raw, off[m] + 80u, dd);
+                pm_i8_lds<1>(raw, off + 80u, dd);
                 uint4 sd;
                 sd.x = __float_as_uint(pm_h2f(dd[0] & 0xffffu));
                 sd.y = __float_as_uint(pm_h2f(dd[0] >> 16));
-                sd.z = ((scw[m][0] >> 4) & 0x0f0f0f0fu); /* mins 0-3 */
-                sd.w = ((scw[m][1] >> 4) & 0x0f0f0f0fu); /* mins 4-7 */
-                uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NM + (uint32_t)m) * 256u + 2u * r;
+                sd.z = ((scw[0] >> 4) & 0x0f0f0f0fu); /* mins 0-3 */
+                sd.w = ((scw[1] >> 4) & 0x0f0f0f0fu); /* mins 4-7 */
+                uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NM + m) * 256u + 2u * r;
                 side[0] = sd;
-                side[1] = make_uint4((scw[m][2] >> 4) & 0x0f0f0f0fu, (scw[m][3] >> 4) & 0x0f0f0f0fu, 0u, 0u);
+                side[1] = make_uint4((scw[2] >> 4) & 0x0f0f0f0fu, (scw[3] >> 4) & 0x0f0f0f0fu, 0u, 0u);
             }
             /* per (token, super-block): yd and the bsums split in low / high bytes */
-            if (q == 0u && tk < t.nt) {
+            if (p == 0u && q == 0u && tk < t.nt) {
+                const uint8_t *as_raw = sm + SM::OFF_ASRAW + (slot * PM_I8_N + tk) * 64u;
                 uint32_t bw[9];
-                pm_i8_lds<1>(araw, (aoff + 0u) & ~3u, bw);         /* d */
-                pm_i8_lds<8>(araw, (aoff + 260u) & ~3u, bw + 1);   /* bsums[16] */
+                pm_i8_lds<1>(as_raw, (uint32_t)(blk & 15u), bw);                      /* d */
+                pm_i8_lds<8>(as_raw + 16, (uint32_t)((blk + 260u) & 15u), bw + 1);  /* bsums[16] */
                 uint32_t lo[4], hi[4];
 #pragma unroll
                 for (int qq = 0; qq < 4; qq++) {
@@ -316,20 +330,24 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
 #pragma unroll
                 for (int qq = 0; qq < 4; qq++) as[1 + qq] = lo[qq], as[5 + qq] = hi[qq];
             }
+            /* B quarter of this thread's chunk p */
+            uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (tk < t.nt)
+                pm_i8_lds<8>(sm + SM::OFF_ARAW + slot * SM::ARAW_STAGE + ((p * PM_I8_N + tk) * 4u + q) * 48u,
+                             (uint32_t)((blk + 4u + 128u * p + 32u * q) & 15u), bv);
             /* the two 128-wide K chunks of the super-block */
 #pragma unroll 1
             for (uint32_t h = 0; h < 2; h++) {
                 const uint32_t c = 2u * g + h, ab = c & 1u;
-                if (c >= 2 && !pm_mbar_wait_sleep(&a_empty[ab], ((c >> 1) - 1u) & 1u, a.err, a.wait)) {
+                if (c >= 2 && !pm_mbar_wait(&a_empty[ab], ((c >> 1) - 1u) & 1u, a.err, a.wait)) {
                     fail = true;
                     break;
                 }
-#pragma unroll
-                for (int m = 0; m < NM; m++) {
+                if (NM == 2 || p == h) { /* A: this thread's row of matrix m, chunk h */
                     uint32_t qw[8];
-                    pm_i8_lds<8>(raw, off[m] + 16u + 32u * h, qw);
-                    const uint32_t sc4[2] = {scw[m][2 * h] & 0x0f0f0f0fu, scw[m][2 * h + 1] & 0x0f0f0f0fu};
-                    uint8_t *A = sm + SM::OFF_A + (ab * NM + (uint32_t)m) * SM::A + (r >> 3) * 1024u + (r & 7u) * 128u;
+                    pm_i8_lds<8>(raw, off + 16u + 32u * h, qw);
+                    const uint32_t sc4[2] = {scw[2 * h] & 0x0f0f0f0fu, scw[2 * h + 1] & 0x0f0f0f0fu};
+                    uint8_t *A = sm + SM::OFF_A + (ab * NM + m) * SM::A + (r >> 3) * 1024u + (r & 7u) * 128u;
 #pragma unroll
                     for (uint32_t j = 0; j < 8; j++) { /* 16-byte unit j: shift 2 (j / 2), qs words 4 (j % 2) .. + 3 */
                         const uint32_t sc = (sc4[j >> 2] >> (8u * (j & 3u))) & 0xffu;
@@ -342,27 +360,22 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                         *(uint4 *)(A + ((j ^ (r & 7u)) << 4)) = o;
                     }
                 }
-                /* B: 4 threads per token row, 32 q8 bytes each from the staged block; rows past nt zero */
-                uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                if (tk < t.nt) pm_i8_lds<8>(araw, aoff + 4u + 128u * h + 32u * q, bv);
-                uint8_t *B = sm + SM::OFF_B + ab * 4096u + (tk >> 3) * 1024u + (tk & 7u) * 128u;
-                *(uint4 *)(B + (((2u * q) ^ (tk & 7u)) << 4)) = make_uint4(bv[0], bv[1], bv[2], bv[3]);
-                *(uint4 *)(B + (((2u * q + 1u) ^ (tk & 7u)) << 4)) = make_uint4(bv[4], bv[5], bv[6], bv[7]);
+                if (p == h) { /* B of chunk h: 4 threads per token row, 32 q8 bytes each; rows past nt zero */
+                    uint8_t *B = sm + SM::OFF_B + ab * 4096u + (tk >> 3) * 1024u + (tk & 7u) * 128u;
+                    *(uint4 *)(B + (((2u * q) ^ (tk & 7u)) << 4)) = make_uint4(bv[0], bv[1], bv[2], bv[3]);
+                    *(uint4 *)(B + (((2u * q + 1u) ^ (tk & 7u)) << 4)) = make_uint4(bv[4], bv[5], bv[6], bv[7]);
+                }
                 pm_fence_proxy_async(); /* generic-proxy writes before the MMA reads them */
                 pm_mbar_arrive(&a_full[ab]);
             }
             if (fail) break;
-            /* the raw rows (and token blocks, read within this warp) of this super-block are
-             * consumed: request a later one into the slot */
-            __syncwarp();
-            if (issued < G) issue(issued++);
+            /* this thread's pieces of super-block g are consumed: request g + RS into the slot */
+            if (g + PM_I8_RS < G) issue(g + PM_I8_RS);
+            pm_cp_async_commit();
         }
         if (fail) atomicOr(&s_fail, 1u);
-        /* copies this thread requested and never consumed land before the CTA leaves */
-        const uint32_t first = issued > PM_I8_RS ? issued - PM_I8_RS : 0u;
-        if (fail)
-            for (uint32_t d = first; d < issued; d++) pm_mbar_wait(&raw_full[d % PM_I8_RS], (d / PM_I8_RS) & 1u, nullptr);
-    } else if (warp == 8) {
+        pm_cp_async_wait<0>(); /* every copy of this thread has landed before the CTA leaves */
+    } else if (warp == 12) {
         /* ===== MMA issue ===== */
         if (lane == 0) {
             bool ok = true;
@@ -405,7 +418,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             if (!ok) atomicOr(&s_fail, 1u);
         }
     } else {
-        /* ===== epilogue: warps 4-7 read tensor-memory lanes 32 (warp % 4) .. + 31 ===== */
+        /* ===== epilogue: warps 8-11 read tensor-memory lanes 32 (warp % 4) .. + 31 ===== */
         const uint32_t lq = warp & 3u, row = lq * 32u + lane;
         float acc[NM][PM_I8_N];
 #pragma unroll
@@ -416,7 +429,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
         for (uint32_t g = 0; g < G; g++) {
             const uint32_t sb = g % nsb, x = g % PM_I8_AC;
             if (sb == 0) pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
-            if (!pm_mbar_wait_sleep(&acc_full[x], (g / PM_I8_AC) & 1u, a.err, a.wait)) {
+            if (!pm_mbar_wait(&acc_full[x], (g / PM_I8_AC) & 1u, a.err, a.wait)) {
                 atomicOr(&s_fail, 1u);
                 break;
             }
@@ -434,7 +447,8 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 const uint32_t mw[4] = {s0.z, s0.w, s1.x, s1.y};
 #pragma unroll
                 for (uint32_t k = 0; k < PM_I8_N; k++) {
-                    if (k < t.nt) {
+                    if (k >= t.nt) break; /* uniform: only the tile's tokens */
+                    {
                         const uint32_t *as = (const uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + k) * SM::ASIDE_T);
                         const float yd = __uint_as_float(as[0]);
                         int lo = 0, hi = 0;
@@ -478,7 +492,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     pm_tc_fence_before();
     __syncthreads();
     pm_tc_fence_after();
-    if (warp == 8) {
+    if (warp == 12) {
         __syncwarp();
         pm_tmem_free(tmem, 256);
     }

@@ -30,7 +30,7 @@ def test_i8_equals_dp4a_and_oracle(oracle, H, F, E, k, T):
     dl = L.to_device()
     xd = torch.from_numpy(x).cuda()
     outs, mids = [], []
-    for flags in (0, 1):  # integer tensor cores, then the dp4a engine
+    for flags in (2, 1):  # integer tensor cores (PULSAR_LAYER_FORCE_I8), then the dp4a engine (NO_I8)
         dl.desc().path_flags = flags
         ws = torch.zeros(dl.workspace_bytes(T), dtype=torch.uint8, device="cuda")
         out = torch.zeros((T, H), dtype=torch.float32, device="cuda")
@@ -40,7 +40,7 @@ def test_i8_equals_dp4a_and_oracle(oracle, H, F, E, k, T):
         rd = reader(ws)
         n = rd(v.n_items, 8, np.uint32)
         assert rd(v.err, 1, np.uint32)[0] == 0
-        if flags == 0:
+        if flags == 2:
             assert n[7] > 0 and n[2] == 0, "routed experts expected on the integer tensor cores"
         mids.append(rd(v.mid, T * v.n_slot * v.f_max, np.float32).reshape(T, v.n_slot, v.f_max)[:, :k, :F])
         outs.append(out.cpu().numpy())
