@@ -10,7 +10,8 @@ crates/quant); hidden rows are fresh seeded N(0, 1) per step.  A step is one
 decode batch of T tokens through the whole stack (layer l+1 reads layer l's
 output: x + moe(rms_norm(x)), the residual add fused into the layer's
 combine).  The stack's expert bytes read per step exceed the 126 MB L2, so
-no flush is needed.  Decode batches 1, 32 and 256; the headline is T = 32.
+no flush is needed.  Decode batches 1, 32 and 256; the headline is T = 256
+(the routed experts then run on the tcgen05 integer tensor cores).
 
 Other workloads: c2-decode (configs[1], 40 layers, T 1/8/64), c1-decode
 (configs[0]: one layer, T = 1, four weight copies rotated so L2 cannot hold
@@ -20,10 +21,12 @@ value     tokens/s with inputs resident in HBM: K replays of a captured CUDA
           graph of the step, CUDA events on the launching stream, max over ranks.
 e2e       the same through the public API each step: pinned host x -> device,
           the stack, device -> pinned host of the final hidden rows.
-roofline  the dominant kernel (the stream-K gate/up pass, pm_layer_sk_kernel
-          <.., 2, 0>): algorithmic bytes per launch (distinct routed experts x
-          gate+up bytes + shared gate+up + q8_K activations) / its CUDA-event
-          duration on the launching stream, vs the measured HBM copy bandwidth.
+roofline  the dominant kernel, the gate/up pass (pm_tci8_kernel<Q2_K, 2> on
+          the integer tensor cores when the batch has >= 8 tokens per expert
+          on average, else the stream-K dp4a pm_layer_sk_kernel<.., 2, 0>):
+          algorithmic bytes per launch (distinct routed experts x gate+up
+          bytes + shared gate+up + q8_K activations) / its CUDA-event duration
+          on the launching stream, vs the measured HBM copy bandwidth.
 cpu_baseline  the C restatement of the reference CPU expert lane (oracle/,
           all host threads) on a bounded sample of the same workload.
 
@@ -61,7 +64,7 @@ import torch  # noqa: E402
 METRIC = "MoE-layer tokens/s and % of HBM/tensor roofline at 1/2/4/8 B200"
 UNIT = "tokens/s"
 WORKLOADS = {
-    "c4-decode": dict(cfg="C4", layers=94, batches=(1, 32, 256), batch=32, copies=1,
+    "c4-decode": dict(cfg="C4", layers=94, batches=(1, 32, 256), batch=256, copies=1,
                       label="C4 Q2_K expert stack, decode (BASELINE configs[3])"),
     "c2-decode": dict(cfg="C2", layers=40, batches=(1, 8, 64), batch=64, copies=1,
                       label="C2 shared-expert MoE stack, decode (BASELINE configs[1])"),
@@ -703,7 +706,10 @@ def main():
             layer_ms = float(st_ms.sum())
             graph_layer_ms = ms / n_layer_calls
             ratio = TRAFFIC_RATIO.get(args.workload)
-            roof = {"bound": "hbm", "kernel": "pm_layer_sk_kernel gate/up (dp4a stream-K: gate + up + glu -> mid)",
+            i8 = spec.quant == 0 and T * spec.n_used >= 8 * spec.n_expert
+            kname = ("pm_tci8_kernel<Q2_K, 2> gate/up (tcgen05 kind::i8, glu -> mid)" if i8 else
+                     "pm_layer_sk_kernel gate/up (dp4a stream-K: gate + up + glu -> mid)")
+            roof = {"bound": "hbm", "kernel": kname,
                     "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                     "peak_kind": peak_kind + " (STREAM-style copy)",
                     "traffic": ratio * gu_bytes if ratio else None,

@@ -275,8 +275,9 @@ typedef struct pulsar_moe_ws_view {
 } pulsar_moe_ws_view;
 /* pulsar_moe_layer that also records events[0..5] (cudaEvent_t, NULL
  * entries skipped) around its kernels: before the router, after the
- * logits, after q8_K(x), after selection, after gate/up, after down and
- * combine.  For per-kernel timing; otherwise identical to pulsar_moe_layer. */
+ * logits, after q8_K(x), after selection, after the gate/up weight passes,
+ * after the mid q8_K (large batches), down and combine.  For per-kernel
+ * timing; otherwise identical to pulsar_moe_layer. */
 int pulsar_moe_layer_profiled(const pulsar_moe_layer_desc *d, float *out, const float *x, const float *residual,
                               uint32_t n_tok, void *ws, size_t ws_bytes, void *stream, void *const *events);
 

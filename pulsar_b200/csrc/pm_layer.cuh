@@ -1031,12 +1031,12 @@ static int pm_layer_launch(pm_layer_args a, const pm_layout &L, cudaStream_t st,
     if (!g_gu) return 0;
     kgu<<<g_gu, 32u * pm_sk_warps(2), pg.smem, st>>>(a, pg);
     if (!pm_ok(cudaGetLastError(), "moe layer gate/up launch")) return 0;
+    pm_ev(ev, 4, st); /* the gate/up weight passes end here (mid of their pairs written) */
     if (tc) { /* tensor-core pairs: mid and its q8_K */
         if (!pm_launch_tc_mid(a, L, st)) return 0;
     }
     if constexpr (QR == PM_QUANT_Q2_K)
         if (a.i8 && !pm_i8_midq_launch(a, st)) return 0;
-    pm_ev(ev, 4, st);
     /* 5: down -> partial rows */
     if constexpr (TC)
         if (tc && !pm_tc_launch<QR, QS, 1>(a, L, st)) return 0;
