@@ -181,7 +181,24 @@ typedef struct pulsar_moe_layer_desc {
     const float *shared_gate_w;
     /* PULSAR_LAYER_* path flags (0 = the default paths) */
     uint32_t path_flags;
+    /* Q2_K tile-plane images of gate, up and down (pulsar_repack_q2k_tiles;
+     * based like gate/up/down: expert e's image at base + e x its GGUF
+     * bytes), or NULL.  The integer tensor-core passes read these; without
+     * them a Q2_K layer keeps to the dp4a and fp16 tensor-core paths. */
+    const void *gate_tiles, *up_tiles, *down_tiles;
 } pulsar_moe_layer_desc;
+
+/* Load-time repack of Q2_K expert matrices into tile planes (the GGUF
+ * bytes stay the interchange format; this is the device image the integer
+ * tensor-core passes stream).  src: n_mat matrices of `rows` GGUF Q2_K rows
+ * of `cols` values (row_bytes apart, mat_stride bytes between matrices);
+ * dst: n_mat x rows x row_bytes(cols) bytes, 16-byte aligned.  Per
+ * (matrix, 128-row block, 256-value super-block) one contiguous chunk of
+ * 10752 bytes: qs as [4 x 16-byte units][128 rows], then the 16 scale
+ * bytes of each row, then each row's d and dmin (f16).  rows % 128 == 0
+ * and cols % 256 == 0.  Returns 1 (launched on `stream`) or 0. */
+int pulsar_repack_q2k_tiles(void *dst, const void *src, uint32_t n_mat, uint32_t rows, uint32_t cols,
+                            uint64_t row_bytes, uint64_t mat_stride, void *stream);
 
 /* path_flags: keep routed Q2_K experts off the integer tensor-core passes
  * (dp4a engine / fp16 tensor-core tiles instead), or put them there even

@@ -56,6 +56,7 @@ class LayerDesc(ctypes.Structure):
         ("shared_row_bytes_gu", ctypes.c_uint64), ("shared_row_bytes_down", ctypes.c_uint64),
         ("shared_gate", ctypes.c_void_p), ("shared_up", ctypes.c_void_p), ("shared_down", ctypes.c_void_p),
         ("wait_cycles", ctypes.c_uint64), ("shared_gate_w", ctypes.c_void_p), ("path_flags", ctypes.c_uint32),
+        ("gate_tiles", ctypes.c_void_p), ("up_tiles", ctypes.c_void_p), ("down_tiles", ctypes.c_void_p),
     ]
 
 
@@ -93,6 +94,7 @@ _SIGS = {
                                   ctypes.POINTER(ctypes.c_void_p)],
     "pulsar_moe_layer_ws_view": [ctypes.POINTER(LayerDesc), _U32, _P, ctypes.POINTER(WsView)],
     "pulsar_quantize_rows": [_P, _P, _P, _U32, _U64, _U32, _P],
+    "pulsar_repack_q2k_tiles": [_P, _P, _U32, _U32, _U32, _U64, _U64, _P],
 }
 
 

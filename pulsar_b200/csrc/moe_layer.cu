@@ -61,7 +61,8 @@ static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
  * weights faster.  PULSAR_LAYER_NO_I8 / PULSAR_LAYER_FORCE_I8 override. */
 static bool pm_i8_on(const pulsar_moe_layer_desc *d, uint32_t T) {
     const uint64_t routed = (uint64_t)T * d->n_used;
-    const bool fits = d->quant == PM_QUANT_Q2_K && d->n_embd % 256u == 0 && d->n_ff % 256u == 0 &&
+    const bool fits = d->quant == PM_QUANT_Q2_K && d->gate_tiles && d->up_tiles && d->down_tiles &&
+                      d->n_embd % 256u == 0 && d->n_ff % 256u == 0 &&
                       routed < (1u << 19) && routed / PM_I8_N + d->n_expert < 4000u;
     if (!fits || (d->path_flags & PULSAR_LAYER_NO_I8)) return false;
     return (d->path_flags & PULSAR_LAYER_FORCE_I8) || routed >= 8ull * d->n_expert;
@@ -550,6 +551,46 @@ extern "C" size_t pulsar_moe_layer_workspace(const pulsar_moe_layer_desc *d, uin
 
 static void *pm_noalloc_ws();
 
+/* GGUF Q2_K rows -> tile planes (layout above); thread per (chunk, row) */
+static __global__ void pm_q2k_tiles_kernel(uint8_t *dst, const uint8_t *src, uint32_t n_mat, uint32_t rows,
+                                           uint32_t nsb, uint64_t row_bytes, uint64_t mat_stride) {
+    const uint32_t nrb = rows / 128u;
+    const uint64_t n = (uint64_t)n_mat * nrb * nsb * 128u;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(i % 128u);
+        const uint64_t chunk = i / 128u; /* (e nrb + b) nsb + sb */
+        const uint32_t sb = (uint32_t)(chunk % nsb);
+        const uint64_t eb = chunk / nsb;
+        const uint32_t b = (uint32_t)(eb % nrb), e = (uint32_t)(eb / nrb);
+        const uint32_t *blk = (const uint32_t *)(src + e * mat_stride + (uint64_t)(b * 128u + r) * row_bytes +
+                                                 (uint64_t)sb * PM_Q2_K_BYTES);
+        uint32_t w[21];
+#pragma unroll
+        for (int k = 0; k < 21; k++) w[k] = blk[k]; /* scales 0-3, qs 4-19, d dmin 20 */
+        uint8_t *c = dst + chunk * PM_I8_CHUNK;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; j++)
+            *(uint4 *)(c + (j * 128u + r) * 16u) = make_uint4(w[4 + 4 * j], w[5 + 4 * j], w[6 + 4 * j], w[7 + 4 * j]);
+        *(uint4 *)(c + 8192u + 16u * r) = make_uint4(w[0], w[1], w[2], w[3]);
+        *(uint32_t *)(c + 10240u + 4u * r) = w[20];
+    }
+}
+
+extern "C" int pulsar_repack_q2k_tiles(void *dst, const void *src, uint32_t n_mat, uint32_t rows, uint32_t cols,
+                                       uint64_t row_bytes, uint64_t mat_stride, void *stream) {
+    if (!dst || !src || !n_mat || !rows || rows % 128u || !cols || cols % 256u) return 0;
+    if (row_bytes < pm_row_bytes(PM_QUANT_Q2_K, cols) || row_bytes % 4u || mat_stride % 4u ||
+        (uintptr_t)src % 4u || (uintptr_t)dst % 16u)
+        return 0;
+    if (n_mat > 1 && mat_stride < (uint64_t)rows * row_bytes) return 0;
+    cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamPerThread;
+    const uint64_t n = (uint64_t)n_mat * rows * (cols / 256u);
+    const uint32_t grid = (uint32_t)((n + 255u) / 256u < 65536u ? (n + 255u) / 256u : 65536u);
+    pm_q2k_tiles_kernel<<<grid, 256, 0, st>>>((uint8_t *)dst, (const uint8_t *)src, n_mat, rows, cols / 256u,
+                                               row_bytes, mat_stride);
+    return pm_ok(cudaGetLastError(), "q2_K tile-plane repack launch");
+}
+
 extern "C" int pulsar_moe_layer_ws_view(const pulsar_moe_layer_desc *d, uint32_t n_tok, void *ws,
                                         pulsar_moe_ws_view *v) {
     if (!ws) ws = pm_noalloc_ws(); /* the built-in array of pulsar_moe_layer_noalloc on this device */
@@ -620,6 +661,8 @@ static void pm_fill_args(pm_layer_args &a, const pulsar_moe_layer_desc *d, const
     a.gate = (const uint8_t *)d->gate, a.up = (const uint8_t *)d->up, a.down = (const uint8_t *)d->down;
     a.sgate = (const uint8_t *)d->shared_gate, a.sup = (const uint8_t *)d->shared_up;
     a.sdown = (const uint8_t *)d->shared_down;
+    a.gate_t = (const uint8_t *)d->gate_tiles, a.up_t = (const uint8_t *)d->up_tiles;
+    a.down_t = (const uint8_t *)d->down_tiles;
     a.gate_b = d->gate_b, a.up_b = d->up_b, a.down_b = d->down_b, a.router_sel_b = d->router_select_b;
     a.logits = (float *)(b + L.logits);
     a.sel = (int32_t *)(b + L.sel);

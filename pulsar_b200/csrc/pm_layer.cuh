@@ -95,6 +95,7 @@ struct pm_layer_args {
     float scale;
     uint64_t rb_gu_r, rb_dn_r, st_gu_r, st_dn_r, rb_gu_s, rb_dn_s;
     const uint8_t *gate, *up, *down, *sgate, *sup, *sdown;
+    const uint8_t *gate_t, *up_t, *down_t; /* Q2_K tile-plane images (integer tensor-core passes) */
     const float *gate_b, *up_b, *down_b, *router_sel_b;
     /* workspace */
     float *logits;

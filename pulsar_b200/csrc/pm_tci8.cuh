@@ -20,24 +20,22 @@
  * kernel lists them); a task is (tile, 128-row block of the pass's
  * matrices).  Persistent CTAs take tasks round-robin and stream their
  * super-blocks through four pipelines:
- *   raw     every decode thread copies exactly the bytes it later reads
- *           (its row's 84 bytes of a matrix per super-block, a quarter of a
- *           token's q8 values, the token's scale and bsums) in 16-byte
- *           asynchronous copies (rounded out) into a 2-deep ring, one copy
- *           group per super-block, waited on by the thread itself: no
- *           cross-thread hand-off on the weight stream (the bulk-copy engine
- *           would serialize hundreds of 100-byte requests per super-block,
- *           and a CTA-wide barrier per super-block cost ~1 us);
- *   decode  8 warps turn raw rows into int8 A tiles (q sc, 128 rows x 128 K,
+ *   load    one producer warp fills a ring of super-block stages: per
+ *           matrix one bulk copy of the 10.5 KB tile-plane chunk (the
+ *           load-time image below: 128 rows of one super-block, contiguous
+ *           in HBM) and per lane one token's q8_K block in 16-byte
+ *           asynchronous copies, all landing on the stage's mbarrier;
+ *   decode  8 warps turn a stage into int8 A tiles (q sc, 128 rows x 128 K,
  *           128-byte swizzle), stage the tokens' q8 values as the B tile
  *           and the per-(row, super-block) scales / per-(token,
- *           super-block) bsums for the epilogue;
+ *           super-block) bsums for the epilogue, and free the stage as soon
+ *           as its bytes are in registers;
  *   mma     one thread issues 4 MMAs (K = 32) per matrix per 128-wide K
  *           chunk into a per-super-block tensor-memory slot (4 slots);
- *   epilog  4 warps read the slot (32 lanes each), form the f32 terms and
- *           add them in super-block order; at the task's last super-block
- *           they write mid = glu(g + gb, u + ub) w (gate/up) or the partial
- *           row (down).
+ *   epilog  8 warps (two per 32-lane quarter of tensor memory, 16 tokens
+ *           each) read the slot, form the f32 terms and add them in
+ *           super-block order; at the task's last super-block they write
+ *           mid = glu(g + gb, u + ub) w (gate/up) or the partial row (down).
  * Every wait is bounded; on a timeout the kernel records it in the layer's
  * error word, lets the copies and MMAs in flight land and returns.
  */
@@ -45,10 +43,11 @@
 #include "pm_tc.cuh"
 
 #define PM_I8_N 32u      /* tokens per tile (MMA N: 16 or 32) */
-#define PM_I8_RS 2u      /* raw ring depth (super-blocks) */
 #define PM_I8_AC 4u      /* tensor-memory / side-data slots (super-blocks) */
-#define PM_I8_PITCH 112u /* raw bytes per row per matrix per super-block (84 + alignment) */
-#define PM_I8_THREADS 416u /* 8 decode warps, 4 epilogue warps, 1 MMA warp */
+#define PM_I8_EPI_WARPS 8u
+#define PM_I8_MMA_WARP 16u
+#define PM_I8_PROD_WARP 17u
+#define PM_I8_THREADS 576u /* 8 decode warps, 8 epilogue warps, 1 MMA warp, 1 producer warp */
 
 /* kind::i8 instruction descriptor: A, B signed 8-bit, D s32, K-major */
 __host__ __device__ __forceinline__ uint32_t pm_idesc_i8(uint32_t M, uint32_t N) {
@@ -100,46 +99,51 @@ __device__ __forceinline__ void pm_cp_async_arrive(uint64_t *bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(pm_smem_addr(bar)) : "memory");
 }
 
-/* arrive on bar (count 1) after this thread's bulk copies of `bytes` */
-__device__ __forceinline__ void pm_mbar_arrive_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(pm_smem_addr(bar)), "r"(bytes)
-                 : "memory");
-}
-
 __device__ __forceinline__ int pm_dp4a_uu(uint32_t a, uint32_t b, int c) {
     int d;
     asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
 
+/* Q2_K tile planes: the load-time image of an expert matrix the integer
+ * passes stream.  Per (expert, 128-row block, super-block) one contiguous
+ * chunk of 128 x 84 bytes (the same bytes as the GGUF blocks, regrouped):
+ *     [0, 8192)      qs: [4 units][128 rows] x 16 bytes (unit j = qs bytes 16j..16j+15)
+ *     [8192, 10240)  scales: [128 rows] x 16 bytes
+ *     [10240, 10752) d, dmin: [128 rows] x 2 f16
+ * so one bulk copy brings a super-block of 128 rows, and every decode
+ * thread's reads of it are bank-conflict free.  Chunk (e, b, sb) sits at
+ * ((e nrb + b) nsb + sb) x 10752: an expert's image has the size of its
+ * GGUF rows. */
+#define PM_I8_CHUNK 10752u
+#define PM_I8_TOKB 304u /* per-token slot of a ring stage: a q8_K block rounded out to 16 bytes */
+
 /* shared-memory layout of the kernel (bytes; 1024-aligned tiles first) */
 template <int NM>
 struct pm_i8_smem {
+    static constexpr uint32_t RS = NM == 2 ? 3u : 8u;         /* ring stages (super-blocks) */
     static constexpr uint32_t A = 16384u;                      /* one 128 x 128 int8 tile */
     static constexpr uint32_t OFF_A = 0;                        /* [2 buffers][NM] */
     static constexpr uint32_t OFF_B = OFF_A + 2u * NM * A;      /* [2 buffers] 32 x 128 */
-    static constexpr uint32_t OFF_RAW = OFF_B + 2u * 4096u;     /* [RS][2 parts][128][PITCH] */
-    static constexpr uint32_t RAW_STAGE = 2u * 128u * PM_I8_PITCH;
-    static constexpr uint32_t OFF_ARAW = OFF_RAW + PM_I8_RS * RAW_STAGE; /* [RS][2][32 tokens][4] 48 B */
-    static constexpr uint32_t ARAW_STAGE = 2u * PM_I8_N * 4u * 48u;
-    static constexpr uint32_t OFF_ASRAW = OFF_ARAW + PM_I8_RS * ARAW_STAGE; /* [RS][32 tokens] 64 B */
-    static constexpr uint32_t OFF_SIDE = OFF_ASRAW + PM_I8_RS * PM_I8_N * 64u; /* [AC][NM][128] 2 x uint4 */
+    static constexpr uint32_t OFF_RING = OFF_B + 2u * 4096u;    /* [RS] stages */
+    static constexpr uint32_t STAGE = NM * PM_I8_CHUNK + PM_I8_N * PM_I8_TOKB; /* chunks, then token blocks */
+    static constexpr uint32_t OFF_SIDE = OFF_RING + RS * STAGE; /* [AC][NM][128] 2 x uint4 */
     static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 32u; /* [AC][32] 9 words */
     static constexpr uint32_t ASIDE_T = 40u;                    /* yd, lo[4], hi[4] (+ pad) */
     static constexpr uint32_t TOTAL = OFF_ASIDE + PM_I8_AC * PM_I8_N * ASIDE_T;
+    static_assert(STAGE % 16u == 0 && OFF_RING % 16u == 0, "bulk copies need 16-byte alignment");
     static_assert(TOTAL + 1024u <= 227u * 1024u, "integer tensor-core pass exceeds shared memory");
 };
 
 /* one task = (tile, 128-row block) */
 struct pm_i8_task {
-    const uint8_t *w[2]; /* row 0 of the block, per matrix */
-    uint64_t rb;         /* row bytes */
+    const uint8_t *w[2]; /* the block's first chunk (super-block 0), per matrix */
     uint32_t s0, nt, row0, e;
 };
 
 template <int NM>
-__device__ __forceinline__ bool pm_i8_task_get(const pm_layer_args &a, uint32_t j, uint32_t nrb, uint32_t n_tiles,
-                                               pm_i8_task &t) {
+__device__ __forceinline__ bool pm_i8_task_get(const pm_layer_args &a, uint32_t j, uint32_t nrb, uint32_t nsb,
+                                               uint32_t n_tiles, pm_i8_task &t) {
     const uint32_t tile = j / nrb, rbk = j % nrb;
     if (tile >= n_tiles) return false;
     const uint2 tt = __ldcg(a.i8_tile + tile);
@@ -149,13 +153,12 @@ __device__ __forceinline__ bool pm_i8_task_get(const pm_layer_args &a, uint32_t 
     t.s0 = s0 + tt.y;
     t.nt = cnt - tt.y < PM_I8_N ? cnt - tt.y : PM_I8_N;
     t.row0 = rbk * 128u;
+    const uint64_t chunk0 = ((uint64_t)e * nrb + rbk) * nsb * PM_I8_CHUNK;
     if (NM == 2) {
-        t.rb = a.rb_gu_r;
-        t.w[0] = a.gate + (uint64_t)e * a.st_gu_r + (uint64_t)t.row0 * t.rb;
-        t.w[1] = a.up + (uint64_t)e * a.st_gu_r + (uint64_t)t.row0 * t.rb;
+        t.w[0] = a.gate_t + chunk0;
+        t.w[1] = a.up_t + chunk0;
     } else {
-        t.rb = a.rb_dn_r;
-        t.w[0] = a.down + (uint64_t)e * a.st_dn_r + (uint64_t)t.row0 * t.rb;
+        t.w[0] = a.down_t + chunk0;
         t.w[1] = nullptr;
     }
     return true;
@@ -190,9 +193,10 @@ __device__ __forceinline__ void pm_i8_lds(const uint8_t *base, uint32_t off, uin
 template <int Q, int NM>
 __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_constant__ pm_layer_args a) {
     using SM = pm_i8_smem<NM>;
+    constexpr uint32_t RS = SM::RS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023u) & ~(uintptr_t)1023u);
-    __shared__ uint64_t a_full[2], a_empty[2], acc_full[PM_I8_AC], acc_empty[PM_I8_AC], fin;
+    __shared__ uint64_t full[RS], empty[RS], a_full[2], a_empty[2], acc_full[PM_I8_AC], acc_empty[PM_I8_AC], fin;
     __shared__ uint32_t tslot, s_fail;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t n_tiles = __ldcg(a.n_items + 7);
@@ -200,15 +204,19 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     const uint32_t nsb = (NM == 2 ? a.H : a.Fr) / 256u;
     const uint32_t n_tasks = n_tiles * nrb;
     if (blockIdx.x >= n_tasks) return;
-    if (warp == 12) pm_tmem_alloc(&tslot, 256);
+    if (warp == PM_I8_MMA_WARP) pm_tmem_alloc(&tslot, 256);
     if (tid == 0) {
+        for (uint32_t i = 0; i < RS; i++) {
+            pm_mbar_init(&full[i], 33);  /* the producer's 32 lanes (token copies) + its expect_tx arrive */
+            pm_mbar_init(&empty[i], 256); /* every decode thread */
+        }
         for (uint32_t i = 0; i < 2; i++) {
             pm_mbar_init(&a_full[i], 256);
             pm_mbar_init(&a_empty[i], 1);
         }
         for (uint32_t i = 0; i < PM_I8_AC; i++) {
             pm_mbar_init(&acc_full[i], 1);
-            pm_mbar_init(&acc_empty[i], 4);
+            pm_mbar_init(&acc_empty[i], PM_I8_EPI_WARPS);
         }
         pm_mbar_init(&fin, 1);
         s_fail = 0;
@@ -222,88 +230,103 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
      * runs across them: global index g -> (i = g / nsb, sb = g % nsb) */
     const uint32_t my_tasks = (n_tasks - blockIdx.x + gridDim.x - 1) / gridDim.x;
     const uint32_t G = my_tasks * nsb;
+    const uint32_t task0 = blockIdx.x;
 
-    if (warp < 8) {
+    if (warp == PM_I8_PROD_WARP) {
+        /* ===== producer: per super-block one bulk copy per matrix (the tile-plane chunk) and,
+         * per lane, its token's q8_K block in 16-byte asynchronous copies ===== */
+        pm_i8_task t;
+        uintptr_t blk0 = 0;
+        bool ok = true;
+        uint32_t g = 0;
+        for (; g < G; g++) {
+            const uint32_t sb = g % nsb, s = g % RS;
+            if (sb == 0) {
+                pm_i8_task_get<NM>(a, task0 + (g / nsb) * gridDim.x, nrb, nsb, n_tiles, t);
+                blk0 = lane < t.nt ? (uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + t.s0 + lane)) : 0;
+            }
+            if (g >= RS && !pm_mbar_wait(&empty[s], ((g / RS) - 1u) & 1u, a.err, a.wait)) {
+                ok = false;
+                break;
+            }
+            uint8_t *stage = sm + SM::OFF_RING + s * SM::STAGE;
+            if (lane == 0) {
+                pm_mbar_expect_tx(&full[s], NM * PM_I8_CHUNK);
+#pragma unroll
+                for (int m = 0; m < NM; m++)
+                    pm_bulk_g2s(stage + m * PM_I8_CHUNK, t.w[m] + (uint64_t)sb * PM_I8_CHUNK, PM_I8_CHUNK, &full[s]);
+            }
+            if (lane < t.nt) { /* a q8_K block (292 bytes at a 4-byte boundary) is 19 16-byte pieces */
+                const uintptr_t src = (blk0 + (uintptr_t)sb * PM_Q8_K_BYTES) & ~(uintptr_t)15;
+                uint8_t *dst = stage + NM * PM_I8_CHUNK + lane * PM_I8_TOKB;
+#pragma unroll
+                for (uint32_t k = 0; k < PM_I8_TOKB / 16u; k++) pm_cp_async16(dst + 16u * k, (const void *)(src + 16u * k));
+            }
+            pm_cp_async_arrive(&full[s]);
+        }
+        if (!ok) atomicOr(&s_fail, 1u);
+        /* the copies of the last stages issued have landed before the CTA leaves */
+        for (uint32_t h = g > RS ? g - RS : 0u; h < g; h++) pm_mbar_wait(&full[h % RS], (h / RS) & 1u, nullptr);
+        pm_cp_async_wait<0>();
+    } else if (warp < 8) {
         /* ===== decode warps: thread (r, p) = weight row r, part p.  NM 2: part p takes
          * matrix p; NM 1: part p takes K chunk p of the one matrix.  As token (tk, q) a thread
          * also stages quarter q of token tk's chunk-p q8 values (B), and (p, q) = (0, 0) the
-         * token's scale and bsums.  Every thread copies exactly the bytes it later reads, with
-         * its own asynchronous-copy groups (one per super-block): no cross-thread hand-off. ===== */
+         * token's scale and bsums for the epilogue. ===== */
         const uint32_t r = tid & 127u, p = tid >> 7, tk = r >> 2, q = r & 3u;
         const uint32_t m = NM == 2 ? p : 0u; /* the matrix this thread decodes */
-        uint32_t iss_task = ~0u;             /* the task of the last request and this thread's token block */
-        pm_i8_task ti;
-        uintptr_t iss_blk = 0;
-        auto issue = [&](uint32_t g) {
-            const uint32_t task = g / nsb, sb = g % nsb, slot = g % PM_I8_RS;
-            if (task != iss_task) {
-                pm_i8_task_get<NM>(a, blockIdx.x + task * gridDim.x, nrb, n_tiles, ti);
-                iss_blk = tk < ti.nt ? (uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + ti.s0 + tk)) : 0;
-                iss_task = task;
-            }
-            { /* the row's 84 bytes of matrix m, rounded out to 16-byte pieces */
-                uint8_t *dst = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + (p * 128u + r) * PM_I8_PITCH;
-                const uintptr_t src = (uintptr_t)(ti.w[m] + (uint64_t)r * ti.rb + (uint64_t)sb * PM_Q2_K_BYTES);
-                const uintptr_t s0 = src & ~(uintptr_t)15;
-                const uint32_t n16 = (uint32_t)((((src + PM_Q2_K_BYTES + 15u) & ~(uintptr_t)15) - s0) >> 4);
-#pragma unroll
-                for (uint32_t k = 0; k < 7; k++)
-                    if (k < n16) pm_cp_async16(dst + 16u * k, (const void *)(s0 + 16u * k));
-            }
-            if (tk < ti.nt) {
-                const uintptr_t blk = iss_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
-                { /* quarter q of chunk p's q8 values: 32 bytes from 4 + 128 p + 32 q */
-                    const uintptr_t src = blk + 4u + 128u * p + 32u * q, s0 = src & ~(uintptr_t)15;
-                    const uint32_t n16 = (uint32_t)((((src + 32u + 15u) & ~(uintptr_t)15) - s0) >> 4);
-                    uint8_t *dst = sm + SM::OFF_ARAW + slot * SM::ARAW_STAGE + ((p * PM_I8_N + tk) * 4u + q) * 48u;
-#pragma unroll
-                    for (uint32_t k = 0; k < 3; k++)
-                        if (k < n16) pm_cp_async16(dst + 16u * k, (const void *)(s0 + 16u * k));
-                }
-                if (p == 0u && q == 0u) { /* the scale d (bytes 0-3) and bsums (260-291) */
-                    uint8_t *dst = sm + SM::OFF_ASRAW + (slot * PM_I8_N + tk) * 64u;
-                    pm_cp_async16(dst, (const void *)(blk & ~(uintptr_t)15));
-                    const uintptr_t src = blk + 260u, s0 = src & ~(uintptr_t)15;
-                    const uint32_t n16 = (uint32_t)((((src + 32u + 15u) & ~(uintptr_t)15) - s0) >> 4);
-#pragma unroll
-                    for (uint32_t k = 0; k < 3; k++)
-                        if (k < n16) pm_cp_async16(dst + 16u + 16u * k, (const void *)(s0 + 16u * k));
-                }
-            }
-        };
-#pragma unroll
-        for (uint32_t g = 0; g < PM_I8_RS; g++) {
-            if (g < G) issue(g);
-            pm_cp_async_commit(); /* one group per super-block (empty past the end) */
-        }
         bool fail = false;
         pm_i8_task t;
         uintptr_t my_blk = 0; /* token tk's q8_K row (block 0) */
         for (uint32_t g = 0; g < G && !fail; g++) {
-            const uint32_t sb = g % nsb;
+            const uint32_t sb = g % nsb, s = g % RS, x = g % PM_I8_AC;
             if (sb == 0) {
-                pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
+                pm_i8_task_get<NM>(a, task0 + (g / nsb) * gridDim.x, nrb, nsb, n_tiles, t);
                 my_blk = tk < t.nt ? (uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + t.s0 + tk)) : 0;
             }
-            const uint32_t slot = g % PM_I8_RS, x = g % PM_I8_AC;
-            pm_cp_async_wait<PM_I8_RS - 1>(); /* this thread's copies of super-block g have landed */
+            if (!pm_mbar_wait(&full[s], (g / RS) & 1u, a.err, a.wait)) {
+                fail = true;
+                break;
+            }
+            /* everything this thread needs of the stage, into registers */
+            const uint8_t *W = sm + SM::OFF_RING + s * SM::STAGE + m * PM_I8_CHUNK;
+            const uint4 scv = *(const uint4 *)(W + 8192u + 16u * r);
+            const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+            const uint32_t dd = *(const uint32_t *)(W + 10240u + 4u * r);
+            uint32_t qw[2][8];
+#pragma unroll
+            for (uint32_t h = 0; h < 2; h++) {
+                if (NM == 2 || p == h) {
+                    const uint4 u0 = *(const uint4 *)(W + (2u * h * 128u + r) * 16u);
+                    const uint4 u1 = *(const uint4 *)(W + ((2u * h + 1u) * 128u + r) * 16u);
+                    qw[h][0] = u0.x, qw[h][1] = u0.y, qw[h][2] = u0.z, qw[h][3] = u0.w;
+                    qw[h][4] = u1.x, qw[h][5] = u1.y, qw[h][6] = u1.z, qw[h][7] = u1.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) qw[h][i] = 0u;
+                }
+            }
+            const uintptr_t blk = my_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
+            const uint8_t *tok = sm + SM::OFF_RING + s * SM::STAGE + NM * PM_I8_CHUNK + tk * PM_I8_TOKB;
+            const uint32_t tb = (uint32_t)(blk & 15u); /* the block's offset in its slot */
+            uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, bw[9];
+            if (tk < t.nt) {
+                pm_i8_lds<8>(tok, tb + 4u + 128u * p + 32u * q, bv);
+                if (p == 0u && q == 0u) {
+                    pm_i8_lds<1>(tok, tb, bw);             /* d */
+                    pm_i8_lds<8>(tok, tb + 260u, bw + 1);  /* bsums[16] */
+                }
+            }
+            pm_mbar_arrive(&empty[s]); /* the stage is consumed: the producer may refill it */
             /* side slot x is free once the epilogue finished super-block g - AC */
             if (g >= PM_I8_AC && !pm_mbar_wait(&acc_empty[x], ((g / PM_I8_AC) - 1u) & 1u, a.err, a.wait)) {
                 fail = true;
                 break;
             }
-            const uint8_t *raw = sm + SM::OFF_RAW + slot * SM::RAW_STAGE + (p * 128u + r) * PM_I8_PITCH;
-            const uint32_t off = (uint32_t)((uintptr_t)(t.w[m] + (uint64_t)r * t.rb + (uint64_t)sb * PM_Q2_K_BYTES) & 15u);
-            const uintptr_t blk = my_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
-            /* the row's 16 scale bytes (low nibble: scale, high nibble: min) */
-            uint32_t scw[4];
-            pm_i8_lds<4>(raw, off, scw);
             if (NM == 2 || p == 0u) { /* side data of (row, super-block, matrix m): d, dmin, 16 mins as bytes */
-                uint32_t dd[1];
-                pm_i8_lds<1>(raw, off + 80u, dd);
                 uint4 sd;
-                sd.x = __float_as_uint(pm_h2f(dd[0] & 0xffffu));
-                sd.y = __float_as_uint(pm_h2f(dd[0] >> 16));
+                sd.x = __float_as_uint(pm_h2f(dd & 0xffffu));
+                sd.y = __float_as_uint(pm_h2f(dd >> 16));
                 sd.z = ((scw[0] >> 4) & 0x0f0f0f0fu); /* mins 0-3 */
                 sd.w = ((scw[1] >> 4) & 0x0f0f0f0fu); /* mins 4-7 */
                 uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NM + m) * 256u + 2u * r;
@@ -312,10 +335,6 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             }
             /* per (token, super-block): yd and the bsums split in low / high bytes */
             if (p == 0u && q == 0u && tk < t.nt) {
-                const uint8_t *as_raw = sm + SM::OFF_ASRAW + (slot * PM_I8_N + tk) * 64u;
-                uint32_t bw[9];
-                pm_i8_lds<1>(as_raw, (uint32_t)(blk & 15u), bw);                      /* d */
-                pm_i8_lds<8>(as_raw + 16, (uint32_t)((blk + 260u) & 15u), bw + 1);  /* bsums[16] */
                 uint32_t lo[4], hi[4];
 #pragma unroll
                 for (int qq = 0; qq < 4; qq++) {
@@ -330,13 +349,8 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
 #pragma unroll
                 for (int qq = 0; qq < 4; qq++) as[1 + qq] = lo[qq], as[5 + qq] = hi[qq];
             }
-            /* B quarter of this thread's chunk p */
-            uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (tk < t.nt)
-                pm_i8_lds<8>(sm + SM::OFF_ARAW + slot * SM::ARAW_STAGE + ((p * PM_I8_N + tk) * 4u + q) * 48u,
-                             (uint32_t)((blk + 4u + 128u * p + 32u * q) & 15u), bv);
             /* the two 128-wide K chunks of the super-block */
-#pragma unroll 1
+#pragma unroll
             for (uint32_t h = 0; h < 2; h++) {
                 const uint32_t c = 2u * g + h, ab = c & 1u;
                 if (c >= 2 && !pm_mbar_wait(&a_empty[ab], ((c >> 1) - 1u) & 1u, a.err, a.wait)) {
@@ -344,19 +358,17 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                     break;
                 }
                 if (NM == 2 || p == h) { /* A: this thread's row of matrix m, chunk h */
-                    uint32_t qw[8];
-                    pm_i8_lds<8>(raw, off + 16u + 32u * h, qw);
                     const uint32_t sc4[2] = {scw[2 * h] & 0x0f0f0f0fu, scw[2 * h + 1] & 0x0f0f0f0fu};
                     uint8_t *A = sm + SM::OFF_A + (ab * NM + m) * SM::A + (r >> 3) * 1024u + (r & 7u) * 128u;
 #pragma unroll
                     for (uint32_t j = 0; j < 8; j++) { /* 16-byte unit j: shift 2 (j / 2), qs words 4 (j % 2) .. + 3 */
                         const uint32_t sc = (sc4[j >> 2] >> (8u * (j & 3u))) & 0xffu;
-                        const uint32_t s = 2u * (j >> 1);
+                        const uint32_t sh = 2u * (j >> 1);
                         uint4 o;
-                        o.x = ((qw[4 * (j & 1) + 0] >> s) & 0x03030303u) * sc;
-                        o.y = ((qw[4 * (j & 1) + 1] >> s) & 0x03030303u) * sc;
-                        o.z = ((qw[4 * (j & 1) + 2] >> s) & 0x03030303u) * sc;
-                        o.w = ((qw[4 * (j & 1) + 3] >> s) & 0x03030303u) * sc;
+                        o.x = ((qw[h][4 * (j & 1) + 0] >> sh) & 0x03030303u) * sc;
+                        o.y = ((qw[h][4 * (j & 1) + 1] >> sh) & 0x03030303u) * sc;
+                        o.z = ((qw[h][4 * (j & 1) + 2] >> sh) & 0x03030303u) * sc;
+                        o.w = ((qw[h][4 * (j & 1) + 3] >> sh) & 0x03030303u) * sc;
                         *(uint4 *)(A + ((j ^ (r & 7u)) << 4)) = o;
                     }
                 }
@@ -368,14 +380,9 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 pm_fence_proxy_async(); /* generic-proxy writes before the MMA reads them */
                 pm_mbar_arrive(&a_full[ab]);
             }
-            if (fail) break;
-            /* this thread's pieces of super-block g are consumed: request g + RS into the slot */
-            if (g + PM_I8_RS < G) issue(g + PM_I8_RS);
-            pm_cp_async_commit();
         }
         if (fail) atomicOr(&s_fail, 1u);
-        pm_cp_async_wait<0>(); /* every copy of this thread has landed before the CTA leaves */
-    } else if (warp == 12) {
+    } else if (warp == PM_I8_MMA_WARP) {
         /* ===== MMA issue ===== */
         if (lane == 0) {
             bool ok = true;
@@ -384,7 +391,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             for (uint32_t g = 0; g < G && ok; g++) {
                 const uint32_t sb = g % nsb, x = g % PM_I8_AC;
                 if (sb == 0) {
-                    pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
+                    pm_i8_task_get<NM>(a, task0 + (g / nsb) * gridDim.x, nrb, nsb, n_tiles, t);
                     N = t.nt > 16u ? 32u : 16u;
                 }
                 if (g >= PM_I8_AC && !pm_mbar_wait(&acc_empty[x], ((g / PM_I8_AC) - 1u) & 1u, a.err, a.wait)) {
@@ -402,9 +409,9 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                     pm_tc_fence_after();
                     const uint64_t bd = pm_desc_sw128(sm + SM::OFF_B + ab * 4096u);
 #pragma unroll
-                    for (int m = 0; m < NM; m++) {
-                        const uint64_t ad = pm_desc_sw128(sm + SM::OFF_A + (ab * NM + (uint32_t)m) * SM::A);
-                        const uint32_t d = tmem + x * (NM * 32u) + (uint32_t)m * 32u;
+                    for (int mm = 0; mm < NM; mm++) {
+                        const uint64_t ad = pm_desc_sw128(sm + SM::OFF_A + (ab * NM + (uint32_t)mm) * SM::A);
+                        const uint32_t d = tmem + x * (NM * 32u) + (uint32_t)mm * 32u;
 #pragma unroll
                         for (uint32_t kk = 0; kk < 4; kk++)
                             pm_mma_i8(d, ad + 2 * kk, bd + 2 * kk, idesc, (h > 0 || kk > 0) ? 1u : 0u);
@@ -418,62 +425,61 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             if (!ok) atomicOr(&s_fail, 1u);
         }
     } else {
-        /* ===== epilogue: warps 8-11 read tensor-memory lanes 32 (warp % 4) .. + 31 ===== */
-        const uint32_t lq = warp & 3u, row = lq * 32u + lane;
-        float acc[NM][PM_I8_N];
+        /* ===== epilogue: warps 8-15; warp w reads tensor-memory lanes 32 (w % 4) .. + 31 and
+         * tokens 16 ((w - 8) / 4) .. + 15 of the tile ===== */
+        const uint32_t lq = warp & 3u, row = lq * 32u + lane, k0 = 16u * ((warp - 8u) >> 2);
+        float acc[NM][16];
 #pragma unroll
-        for (int m = 0; m < NM; m++)
+        for (int mm = 0; mm < NM; mm++)
 #pragma unroll
-            for (uint32_t k = 0; k < PM_I8_N; k++) acc[m][k] = 0.0f;
+            for (uint32_t k = 0; k < 16; k++) acc[mm][k] = 0.0f;
         pm_i8_task t;
         for (uint32_t g = 0; g < G; g++) {
             const uint32_t sb = g % nsb, x = g % PM_I8_AC;
-            if (sb == 0) pm_i8_task_get<NM>(a, blockIdx.x + (g / nsb) * gridDim.x, nrb, n_tiles, t);
+            if (sb == 0) pm_i8_task_get<NM>(a, task0 + (g / nsb) * gridDim.x, nrb, nsb, n_tiles, t);
             if (!pm_mbar_wait(&acc_full[x], (g / PM_I8_AC) & 1u, a.err, a.wait)) {
                 atomicOr(&s_fail, 1u);
                 break;
             }
             pm_tc_fence_after();
-            const uint32_t ncol = t.nt > 16u ? 32u : 16u;
+            const bool active = k0 < t.nt; /* warp-uniform */
+            if (active) {
 #pragma unroll
-            for (int m = 0; m < NM; m++) {
-                int32_t v[PM_I8_N];
-                const uint32_t base = tmem + ((lq * 32u) << 16) + x * (NM * 32u) + (uint32_t)m * 32u;
-                pm_tmem_ld16i(base, v);
-                if (ncol > 16u) pm_tmem_ld16i(base + 16u, v + 16);
-                const uint4 *side = (const uint4 *)(sm + SM::OFF_SIDE) + (x * NM + (uint32_t)m) * 256u + 2u * row;
-                const uint4 s0 = side[0], s1 = side[1];
-                const float d = __uint_as_float(s0.x), dm = __uint_as_float(s0.y);
-                const uint32_t mw[4] = {s0.z, s0.w, s1.x, s1.y};
+                for (int mm = 0; mm < NM; mm++) {
+                    int32_t v[16];
+                    pm_tmem_ld16i(tmem + ((lq * 32u) << 16) + x * (NM * 32u) + (uint32_t)mm * 32u + k0, v);
+                    const uint4 *side = (const uint4 *)(sm + SM::OFF_SIDE) + (x * NM + (uint32_t)mm) * 256u + 2u * row;
+                    const uint4 s0 = side[0], s1 = side[1];
+                    const float d = __uint_as_float(s0.x), dm = __uint_as_float(s0.y);
+                    const uint32_t mw[4] = {s0.z, s0.w, s1.x, s1.y};
 #pragma unroll
-                for (uint32_t k = 0; k < PM_I8_N; k++) {
-                    if (k >= t.nt) break; /* uniform: only the tile's tokens */
-                    {
-                        const uint32_t *as = (const uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + k) * SM::ASIDE_T);
+                    for (uint32_t k = 0; k < 16; k++) {
+                        if (k0 + k >= t.nt) break; /* uniform: only the tile's tokens */
+                        const uint32_t *as = (const uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + k0 + k) * SM::ASIDE_T);
                         const float yd = __uint_as_float(as[0]);
                         int lo = 0, hi = 0;
 #pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            lo = pm_dp4a_uu(mw[q], as[1 + q], lo);
-                            hi = pm_dp4a_us(mw[q], (int)as[5 + q], hi);
+                        for (int qq = 0; qq < 4; qq++) {
+                            lo = pm_dp4a_uu(mw[qq], as[1 + qq], lo);
+                            hi = pm_dp4a_us(mw[qq], (int)as[5 + qq], hi);
                         }
                         const int msum = lo + 256 * hi;
                         /* total += yd xd isum - yd xmin msum (cpu_dot.rs:732-767, q2_K) */
                         const float term = __fsub_rn(__fmul_rn(__fmul_rn(yd, d), (float)v[k]),
                                                      __fmul_rn(__fmul_rn(yd, dm), (float)msum));
-                        acc[m][k] = __fadd_rn(acc[m][k], term);
+                        acc[mm][k] = __fadd_rn(acc[mm][k], term);
                     }
                 }
             }
             pm_tc_fence_before();
             __syncwarp();
             if (lane == 0) pm_mbar_arrive(&acc_empty[x]);
-            if (sb == nsb - 1u) { /* the task's rows are complete: outputs, in the CPU lane's order */
+            if (sb == nsb - 1u && active) { /* the task's rows are complete: outputs, in the CPU lane's order */
                 const uint32_t grow = t.row0 + row;
 #pragma unroll
-                for (uint32_t k = 0; k < PM_I8_N; k++) {
-                    if (k < t.nt) {
-                        const uint32_t pr = __ldcg(a.pairs + t.s0 + k);
+                for (uint32_t k = 0; k < 16; k++) {
+                    if (k0 + k < t.nt) {
+                        const uint32_t pr = __ldcg(a.pairs + t.s0 + k0 + k);
                         if (NM == 2) {
                             float gg = acc[0][k], uu = acc[NM - 1][k];
                             if (a.gate_b) gg = __fadd_rn(gg, a.gate_b[(uint64_t)t.e * a.Fr + grow]);
@@ -484,7 +490,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                         }
                     }
 #pragma unroll
-                    for (int m = 0; m < NM; m++) acc[m][k] = 0.0f;
+                    for (int mm = 0; mm < NM; mm++) acc[mm][k] = 0.0f;
                 }
             }
         }
@@ -492,7 +498,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     pm_tc_fence_before();
     __syncthreads();
     pm_tc_fence_after();
-    if (warp == 12) {
+    if (warp == PM_I8_MMA_WARP) {
         __syncwarp();
         pm_tmem_free(tmem, 256);
     }

@@ -17,7 +17,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from ._lib import LayerDesc, WsView, check, lib, ptr, row_bytes
+from ._lib import QUANT_Q2_K, LayerDesc, WsView, check, lib, ptr, row_bytes
 from .ops import quantize_rows
 
 SLAB_SLACK = 256  # tail slack after every slab (crates/engine/src/lib.rs:594-600)
@@ -65,6 +65,10 @@ class MoeLayer:
     expert_lo: int = 0
     expert_hi: int = 0
     slab_lo: int = 0              # first expert held in the routed slabs (shards hold [slab_lo, expert_hi))
+    # Q2_K tile-plane images of gate / up / down (pulsar_repack_q2k_tiles), for the integer tensor-core passes
+    gate_tiles: torch.Tensor | None = None
+    up_tiles: torch.Tensor | None = None
+    down_tiles: torch.Tensor | None = None
     _desc: LayerDesc | None = field(default=None, repr=False)
 
     # ---------------------------------------------------------- geometry
@@ -114,8 +118,33 @@ class MoeLayer:
             d.shared_gate, d.shared_up, d.shared_down = ptr(self.shared_gate), ptr(self.shared_up), ptr(self.shared_down)
             d.shared_gate_w = ptr(self.shared_gate_w)
         d.expert_lo, d.expert_hi = self.expert_lo, self.expert_hi
+        if self.gate_tiles is not None:
+            d.gate_tiles = ptr(self.gate_tiles) - self.slab_lo * d.expert_stride_gu
+            d.up_tiles = ptr(self.up_tiles) - self.slab_lo * d.expert_stride_gu
+            d.down_tiles = ptr(self.down_tiles) - self.slab_lo * d.expert_stride_down
         self._desc = d
         return d
+
+    def build_tiles(self) -> bool:
+        """Load-time repack of Q2_K routed slabs into tile planes (the device
+        image the integer tensor-core passes stream; the GGUF slabs stay).
+        False (nothing built) for other formats or shapes the planes do not
+        cover (rows % 128, columns % 256)."""
+        s = self.spec
+        if s.quant != QUANT_Q2_K or s.n_ff % 256 or s.n_embd % 256:
+            return False
+        n = (self.expert_hi or s.n_expert) - self.slab_lo
+        st = torch.cuda.current_stream().cuda_stream
+        out = []
+        for slab, rows, cols, rb in ((self.gate, s.n_ff, s.n_embd, self.rb_gu), (self.up, s.n_ff, s.n_embd, self.rb_gu),
+                                     (self.down, s.n_embd, s.n_ff, self.rb_down)):
+            t = torch.empty(n * rows * rb, dtype=torch.uint8, device=slab.device)
+            check(lib().pulsar_repack_q2k_tiles(ptr(t), ptr(slab), n, rows, cols, rb, rows * rb, st),
+                  "repack_q2k_tiles")
+            out.append(t)
+        self.gate_tiles, self.up_tiles, self.down_tiles = out
+        self._desc = None
+        return True
 
     def workspace_bytes(self, max_tok: int) -> int:
         n = int(lib().pulsar_moe_layer_workspace(ctypes.byref(self.desc()), max_tok))
@@ -278,6 +307,7 @@ def make_layer(spec: LayerSpec, seed: int, device="cuda", lo: int = 0, hi: int =
         layer.shared_down = _quantized(s.n_embd, s.shared_n_ff, sq, s.weight_std, gen(11), dev, qw=qsf)
         if s.shared_gate:
             layer.shared_gate_w = (torch.randn((s.n_embd,), generator=gen(12), device=dev) * s.weight_std).contiguous()
+    layer.build_tiles()
     return layer
 
 

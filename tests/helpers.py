@@ -129,6 +129,7 @@ class HostLayer:
             L.gate_b, L.up_b, L.down_b = up_(self.gate_b), up_(self.up_b), up_(self.down_b)
         if self.shared is not None:
             L.shared_gate, L.shared_up, L.shared_down = (up_(self.shared[n]) for n in ("gate", "up", "down"))
+        L.build_tiles()
         return L
 
 
