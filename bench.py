@@ -22,7 +22,7 @@ value     tokens/s with inputs resident in HBM: K replays of a captured CUDA
 e2e       the same through the public API each step: pinned host x -> device,
           the stack, device -> pinned host of the final hidden rows.
 roofline  the dominant kernel, the gate/up pass (pm_tci8_kernel<Q2_K, 2> on
-          the integer tensor cores when the batch has >= 8 tokens per expert
+          the integer tensor cores when the batch has >= 1 routed token per expert
           on average, else the stream-K dp4a pm_layer_sk_kernel<.., 2, 0>):
           algorithmic bytes per launch (distinct routed experts x gate+up
           bytes + shared gate+up + q8_K activations) / its CUDA-event duration
@@ -254,14 +254,24 @@ class Runner:
             self.graph.replay()
 
 
-def launches_per_layer(T: int, world: int = 1, tc_fmt: bool = True) -> int:
+def i8_on(spec, T: int, world: int = 1) -> bool:
+    """routed Q2_K experts on the integer tensor-core passes (the library's rule: at least one
+    routed token per expert on average, over every rank's tokens)"""
+    return spec.quant == 0 and T * world * spec.n_used >= spec.n_expert
+
+
+def launches_per_layer(T: int, world: int = 1, tc_fmt: bool = True, i8: bool = False) -> int:
     """this library's kernels one layer step launches for a layer call over T tokens per rank:
     rms_norm, router (+ q8_K of x), selection (two launches under expert parallelism: top-k, then
-    the CSR after the dispatch), gate/up, down, combine, and when an expert can reach 192 tokens
-    (counted over every rank's tokens) the tensor-core passes - per pass (gate/up, down) the
-    token-image pack plus one expand + one gemm (these workloads fit one expert wave) - and the
-    tensor-core mid kernel.  NCCL's own kernels are not counted."""
-    return 6 + (1 if world > 1 else 0) + (7 if T * world >= 192 and tc_fmt else 0)
+    the CSR after the dispatch), the dp4a gate/up and down passes, combine; with the integer
+    tensor-core passes on, their gate/up, mid q8_K and down kernels; otherwise, when an expert
+    can reach 192 tokens (counted over every rank's tokens), the fp16 tensor-core passes - per
+    pass (gate/up, down) the token-image pack plus one expand + one gemm (these workloads fit one
+    expert wave) - and the tensor-core mid kernel.  NCCL's own kernels are not counted."""
+    n = 6 + (1 if world > 1 else 0)
+    if i8:
+        return n + 3
+    return n + (7 if T * world >= 192 and tc_fmt else 0)
 
 
 def max_over_ranks(ms: float, world: int) -> float:
@@ -634,6 +644,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-profile", action="store_true", help="skip the per-kernel roofline leg")
     ap.add_argument("--all-batches", action="store_true", help="also time the workload's other decode batches")
+    ap.add_argument("--path-flags", type=int, default=0, help="layer descriptor path_flags (diagnostics only: "
+                    "1 keeps routed Q2_K off the integer tensor cores, 2 forces them on)")
     args = ap.parse_args()
     if args.workload == "c3-prefill":
         return prefill_c3(args)
@@ -664,6 +676,8 @@ def main():
     H = spec.n_embd
     t0 = time.time()
     stack = build_stack(wl, world, rank, dev)
+    for L in stack:
+        L.desc().path_flags = args.path_flags
     log(f"[rank {rank}] built {len(stack)} layers in {time.time() - t0:.1f}s "
         f"({sum(L.gate.numel() + L.up.numel() + L.down.numel() for L in stack) / 1e9:.1f} GB)")
 
@@ -709,7 +723,7 @@ def main():
             layer_ms = float(st_ms.sum())
             graph_layer_ms = ms / n_layer_calls
             ratio = TRAFFIC_RATIO.get(args.workload)
-            i8 = spec.quant == 0 and T * spec.n_used >= 8 * spec.n_expert
+            i8 = i8_on(spec, T)
             kname = ("pm_tci8_kernel<Q2_K, 2> gate/up (tcgen05 kind::i8, glu -> mid)" if i8 else
                      "pm_layer_sk_kernel gate/up (dp4a stream-K: gate + up + glu -> mid)")
             roof = {"bound": "hbm", "kernel": kname,
@@ -738,11 +752,12 @@ def main():
             config["placement"] = "experts in snake order over Zipf popularity, E/N contiguous slots per rank"
         line = {"metric": METRIC, "value": tok / (ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "int8 dp4a dots, f32 accumulate", "data": "synthetic (seeded)",
+                "vs_baseline": None, "dtype": ("int8 x int8 -> s32 on tcgen05 kind::i8, f32 terms" if i8_on(spec, T, world)
+                                                    else "int8 dp4a dots, f32 accumulate"), "data": "synthetic (seeded)",
                 "config": config,
                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
-                "gpu_launches": launches_per_layer(T, world) * n_layer_calls * args.steps, "clocks": clocks,
+                "gpu_launches": launches_per_layer(T, world, i8=i8_on(spec, T, world)) * n_layer_calls * args.steps, "clocks": clocks,
                 "roofline": roof, "cpu_baseline": cpu, "per_batch": {str(k): v for k, v in results.items()}}
     if line is not None:
         print(json.dumps(line), flush=True)

@@ -202,7 +202,7 @@ int pulsar_repack_q2k_tiles(void *dst, const void *src, uint32_t n_mat, uint32_t
 
 /* path_flags: keep routed Q2_K experts off the integer tensor-core passes
  * (dp4a engine / fp16 tensor-core tiles instead), or put them there even
- * below the default threshold of 8 tokens per expert on average; for
+ * below the default threshold of one routed token per expert on average; for
  * comparisons and tests */
 #define PULSAR_LAYER_NO_I8 1u
 #define PULSAR_LAYER_FORCE_I8 2u

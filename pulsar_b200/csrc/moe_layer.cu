@@ -56,16 +56,18 @@ static size_t pm_al(size_t v) { return (v + 255) & ~(size_t)255; }
 
 /* routed Q2_K experts on the integer tensor cores (pm_tci8.cuh): whole
  * super-blocks, the select kernel's 20-bit cost / 12-bit tile packing, and
- * enough tokens per expert on average (T k >= 8 E) for the tiles to pay for
- * their fixed per-super-block cost; below that the dp4a engine streams the
- * weights faster.  PULSAR_LAYER_NO_I8 / PULSAR_LAYER_FORCE_I8 override. */
+ * at least one routed token per expert on average (T k >= E) for the tiles
+ * to pay for their fixed per-super-block cost; below that the dp4a engine
+ * streams the weights faster (measured on B200 at config 4's shapes: T 32,
+ * T k = 2 E, integer passes 0.32 ms per layer against 0.45 ms; T 8 even;
+ * T 1 dp4a ahead).  PULSAR_LAYER_NO_I8 / PULSAR_LAYER_FORCE_I8 override. */
 static bool pm_i8_on(const pulsar_moe_layer_desc *d, uint32_t T) {
     const uint64_t routed = (uint64_t)T * d->n_used;
     const bool fits = d->quant == PM_QUANT_Q2_K && d->gate_tiles && d->up_tiles && d->down_tiles &&
                       d->n_embd % 256u == 0 && d->n_ff % 256u == 0 &&
                       routed < (1u << 19) && routed / PM_I8_N + d->n_expert < 4000u;
     if (!fits || (d->path_flags & PULSAR_LAYER_NO_I8)) return false;
-    return (d->path_flags & PULSAR_LAYER_FORCE_I8) || routed >= 8ull * d->n_expert;
+    return (d->path_flags & PULSAR_LAYER_FORCE_I8) || routed >= (uint64_t)d->n_expert;
 }
 
 /* tensor-core path available for the routed / shared experts */

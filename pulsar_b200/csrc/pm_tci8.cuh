@@ -31,11 +31,21 @@
  *           super-block) bsums for the epilogue, and free the stage as soon
  *           as its bytes are in registers;
  *   mma     one thread issues 4 MMAs (K = 32) per matrix per 128-wide K
- *           chunk into a per-super-block tensor-memory slot (4 slots);
+ *           chunk into a per-super-block tensor-memory slot (4 slots), and
+ *           per matrix one more u8 MMA (K = 32) for the mins sum below;
  *   epilog  8 warps (two per 32-lane quarter of tensor memory, 16 tokens
  *           each) read the slot, form the f32 terms and add them in
  *           super-block order; at the task's last super-block they write
  *           mid = glu(g + gb, u + ub) w (gate/up) or the partial row (down).
+ *
+ * The mins sum on the tensor cores.  msum = sum_j m_j bsum_j (16 sub-blocks,
+ * m_j in 0..15, |bsum_j| <= 16 * 127) is exact as one unsigned 8-bit MMA:
+ * write bsum_j + 2048 = l_j + 16 h_j with l_j in 0..15 and h_j in 1..255;
+ * the A row is [m_0..m_15 | 16 m_0..16 m_15] (the mins as bytes, and the
+ * scale bytes' high nibbles in place), the B row [l_0..l_15 | h_0..h_15],
+ * so the s32 result is msum + 2048 sum_j m_j, and the epilogue subtracts
+ * the row's 2048 sum_j m_j.  Both 32-byte-wide tiles use the 32-byte
+ * swizzle.  Barriers the decode warps signal take one arrival per warp.
  * Every wait is bounded; on a timeout the kernel records it in the layer's
  * error word, lets the copies and MMAs in flight land and returns.
  */
@@ -49,13 +59,32 @@
 #define PM_I8_PROD_WARP 17u
 #define PM_I8_THREADS 576u /* 8 decode warps, 8 epilogue warps, 1 MMA warp, 1 producer warp */
 
-/* kind::i8 instruction descriptor: A, B signed 8-bit, D s32, K-major */
+/* kind::i8 instruction descriptor: A, B signed 8-bit (u8: unsigned), D s32, K-major */
 __host__ __device__ __forceinline__ uint32_t pm_idesc_i8(uint32_t M, uint32_t N) {
     return (2u << 4)               /* D format: s32 */
            | (1u << 7)             /* A format: s8 */
            | (1u << 10)            /* B format: s8 */
            | ((N >> 3) << 17)      /* N / 8 */
            | ((M >> 4) << 24);     /* M / 16 */
+}
+__host__ __device__ __forceinline__ uint32_t pm_idesc_u8(uint32_t M, uint32_t N) {
+    return (2u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24); /* s32 = u8 x u8 */
+}
+
+/* shared-memory descriptor of a K-major tile 32 bytes wide (one K = 32 MMA
+ * slice) in the 32-byte swizzle: 8-row groups of 256 bytes, row r at
+ * 32 (r % 8), its 16-byte unit u at (u ^ ((r >> 2) & 1)) 16 */
+__device__ __forceinline__ uint64_t pm_desc_sw32(const void *tile) {
+    const uint64_t a = pm_smem_addr(tile);
+    uint64_t d = (a >> 4) & 0x3fffull;
+    d |= (uint64_t)1 << 16;           /* leading byte offset (unused for swizzled K-major) */
+    d |= (uint64_t)(256 >> 4) << 32;  /* stride byte offset: next 8-row group */
+    d |= (uint64_t)1 << 46;           /* descriptor version (sm_100) */
+    d |= (uint64_t)6 << 61;           /* layout: 32-byte swizzle */
+    return d;
+}
+__device__ __forceinline__ uint32_t pm_sw32_off(uint32_t r, uint32_t u) {
+    return (r >> 3) * 256u + (r & 7u) * 32u + ((u ^ ((r >> 2) & 1u)) << 4);
 }
 
 __device__ __forceinline__ void pm_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -68,18 +97,24 @@ __device__ __forceinline__ void pm_mma_i8(uint32_t d_tmem, uint64_t adesc, uint6
         : "memory");
 }
 
-/* 16 consecutive s32 columns of this thread's lane */
-__device__ __forceinline__ void pm_tmem_ld16i(uint32_t taddr, int32_t *v) {
-    uint32_t r[16];
+/* 16 consecutive s32 columns of this thread's lane, at ta and at tb, one wait */
+__device__ __forceinline__ void pm_tmem_ld16i2(uint32_t ta, uint32_t tb, int32_t *va, int32_t *vb) {
+    uint32_t r[16], q[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
+        : "r"(ta));
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
+          "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]), "=r"(q[15])
+        : "r"(tb));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = (int32_t)r[i];
+    for (int i = 0; i < 16; i++) va[i] = (int32_t)r[i], vb[i] = (int32_t)q[i];
 }
 
 /* close this thread's group of asynchronous copies / wait until at most N
@@ -123,15 +158,19 @@ template <int NM>
 struct pm_i8_smem {
     static constexpr uint32_t RS = NM == 2 ? 3u : 8u;         /* ring stages (super-blocks) */
     static constexpr uint32_t A = 16384u;                      /* one 128 x 128 int8 tile */
-    static constexpr uint32_t OFF_A = 0;                        /* [2 buffers][NM] */
-    static constexpr uint32_t OFF_B = OFF_A + 2u * NM * A;      /* [2 buffers] 32 x 128 */
-    static constexpr uint32_t OFF_RING = OFF_B + 2u * 4096u;    /* [RS] stages */
+    static constexpr uint32_t NAB = 2u;                         /* A / B tile buffers (128-wide K chunks) */
+    static constexpr uint32_t OFF_A = 0;                        /* [NAB buffers][NM] */
+    static constexpr uint32_t OFF_B = OFF_A + NAB * NM * A;     /* [NAB buffers] 32 x 128 */
+    static constexpr uint32_t OFF_RING = OFF_B + NAB * 4096u;   /* [RS] stages */
     static constexpr uint32_t STAGE = NM * PM_I8_CHUNK + PM_I8_N * PM_I8_TOKB; /* chunks, then token blocks */
-    static constexpr uint32_t OFF_SIDE = OFF_RING + RS * STAGE; /* [AC][NM][128] 2 x uint4 */
-    static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 32u; /* [AC][32] 9 words */
-    static constexpr uint32_t ASIDE_T = 40u;                    /* yd, lo[4], hi[4] (+ pad) */
-    static constexpr uint32_t TOTAL = OFF_ASIDE + PM_I8_AC * PM_I8_N * ASIDE_T;
+    static constexpr uint32_t OFF_AM = OFF_RING + RS * STAGE;  /* [2 (super-block parity)][NM] 128 x 32 mins tiles */
+    static constexpr uint32_t OFF_BM = OFF_AM + 2u * NM * 4096u; /* [2] 32 x 32 bsum split tiles */
+    static constexpr uint32_t OFF_SIDE = OFF_BM + 2u * 1024u;   /* [AC][NM][128] uint4: d, dmin, 2048 sum m */
+    static constexpr uint32_t OFF_ASIDE = OFF_SIDE + PM_I8_AC * NM * 128u * 16u; /* [AC][32] yd */
+    static constexpr uint32_t TMEM_COLS = NM * 64u * PM_I8_AC;  /* per slot and matrix: 32 isum + 32 msum */
+    static constexpr uint32_t TOTAL = OFF_ASIDE + PM_I8_AC * PM_I8_N * 4u;
     static_assert(STAGE % 16u == 0 && OFF_RING % 16u == 0, "bulk copies need 16-byte alignment");
+    static_assert(OFF_AM % 256u == 0 && OFF_BM % 256u == 0, "32-byte swizzle tiles need 256-byte alignment");
     static_assert(TOTAL + 1024u <= 227u * 1024u, "integer tensor-core pass exceeds shared memory");
 };
 
@@ -196,7 +235,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     constexpr uint32_t RS = SM::RS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023u) & ~(uintptr_t)1023u);
-    __shared__ uint64_t full[RS], empty[RS], a_full[2], a_empty[2], acc_full[PM_I8_AC], acc_empty[PM_I8_AC], fin;
+    __shared__ uint64_t full[RS], empty[RS], a_full[SM::NAB], a_empty[SM::NAB], acc_full[PM_I8_AC], acc_empty[PM_I8_AC], fin;
     __shared__ uint32_t tslot, s_fail;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t n_tiles = __ldcg(a.n_items + 7);
@@ -204,14 +243,14 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     const uint32_t nsb = (NM == 2 ? a.H : a.Fr) / 256u;
     const uint32_t n_tasks = n_tiles * nrb;
     if (blockIdx.x >= n_tasks) return;
-    if (warp == PM_I8_MMA_WARP) pm_tmem_alloc(&tslot, 256);
+    if (warp == PM_I8_MMA_WARP) pm_tmem_alloc(&tslot, SM::TMEM_COLS);
     if (tid == 0) {
         for (uint32_t i = 0; i < RS; i++) {
             pm_mbar_init(&full[i], 33);  /* the producer's 32 lanes (token copies) + its expect_tx arrive */
-            pm_mbar_init(&empty[i], 256); /* every decode thread */
+            pm_mbar_init(&empty[i], 8); /* every decode warp */
         }
-        for (uint32_t i = 0; i < 2; i++) {
-            pm_mbar_init(&a_full[i], 256);
+        for (uint32_t i = 0; i < SM::NAB; i++) {
+            pm_mbar_init(&a_full[i], 8);
             pm_mbar_init(&a_empty[i], 1);
         }
         for (uint32_t i = 0; i < PM_I8_AC; i++) {
@@ -284,7 +323,8 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 pm_i8_task_get<NM>(a, task0 + (g / nsb) * gridDim.x, nrb, nsb, n_tiles, t);
                 my_blk = tk < t.nt ? (uintptr_t)pm_i8_xrow<NM>(a, __ldcg(a.pairs + t.s0 + tk)) : 0;
             }
-            if (!pm_mbar_wait(&full[s], (g / RS) & 1u, a.err, a.wait)) {
+            /* waits decide per warp (one arrival per warp on the barriers below) */
+            if (__any_sync(0xffffffffu, !pm_mbar_wait(&full[s], (g / RS) & 1u, a.err, a.wait))) {
                 fail = true;
                 break;
             }
@@ -309,51 +349,55 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             const uintptr_t blk = my_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
             const uint8_t *tok = sm + SM::OFF_RING + s * SM::STAGE + NM * PM_I8_CHUNK + tk * PM_I8_TOKB;
             const uint32_t tb = (uint32_t)(blk & 15u); /* the block's offset in its slot */
-            uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, bw[9];
+            uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, bw[2] = {0u, 0u}, ydw = 0u;
             if (tk < t.nt) {
                 pm_i8_lds<8>(tok, tb + 4u + 128u * p + 32u * q, bv);
-                if (p == 0u && q == 0u) {
-                    pm_i8_lds<1>(tok, tb, bw);             /* d */
-                    pm_i8_lds<8>(tok, tb + 260u, bw + 1);  /* bsums[16] */
+                if (p == 0u) {
+                    pm_i8_lds<2>(tok, tb + 260u + 8u * q, bw); /* bsums 4q .. 4q + 3 */
+                    if (q == 0u) pm_i8_lds<1>(tok, tb, &ydw);  /* d */
                 }
             }
-            pm_mbar_arrive(&empty[s]); /* the stage is consumed: the producer may refill it */
+            /* the stage is consumed: the producer may refill it */
+            __syncwarp();
+            if (lane == 0) pm_mbar_arrive(&empty[s]);
             /* side slot x is free once the epilogue finished super-block g - AC */
-            if (g >= PM_I8_AC && !pm_mbar_wait(&acc_empty[x], ((g / PM_I8_AC) - 1u) & 1u, a.err, a.wait)) {
+            if (g >= PM_I8_AC &&
+                __any_sync(0xffffffffu, !pm_mbar_wait(&acc_empty[x], ((g / PM_I8_AC) - 1u) & 1u, a.err, a.wait))) {
                 fail = true;
                 break;
             }
-            if (NM == 2 || p == 0u) { /* side data of (row, super-block, matrix m): d, dmin, 16 mins as bytes */
-                uint4 sd;
-                sd.x = __float_as_uint(pm_h2f(dd & 0xffffu));
-                sd.y = __float_as_uint(pm_h2f(dd >> 16));
-                sd.z = ((scw[0] >> 4) & 0x0f0f0f0fu); /* mins 0-3 */
-                sd.w = ((scw[1] >> 4) & 0x0f0f0f0fu); /* mins 4-7 */
-                uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NM + m) * 256u + 2u * r;
-                side[0] = sd;
-                side[1] = make_uint4((scw[2] >> 4) & 0x0f0f0f0fu, (scw[3] >> 4) & 0x0f0f0f0fu, 0u, 0u);
+            /* the row's mins (bytes) and 16 x mins (the scale bytes' high nibbles in place) */
+            uint32_t mn[4], m16[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) mn[i] = (scw[i] >> 4) & 0x0f0f0f0fu, m16[i] = scw[i] & 0xf0f0f0f0u;
+            if (NM == 2 || p == 0u) { /* side data of (row, super-block, matrix m): d, dmin, 2048 sum m */
+                int msum = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) msum = pm_dp4a_uu(mn[i], 0x01010101u, msum);
+                uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NM + m) * 128u + r;
+                *side = make_uint4(__float_as_uint(pm_h2f(dd & 0xffffu)), __float_as_uint(pm_h2f(dd >> 16)),
+                                   (uint32_t)(2048 * msum), 0u);
             }
-            /* per (token, super-block): yd and the bsums split in low / high bytes */
-            if (p == 0u && q == 0u && tk < t.nt) {
-                uint32_t lo[4], hi[4];
+            /* per (token, super-block): yd, and the token's bsums as l + 16 h (bsum + 2048, l 0..15,
+             * h 1..255), four per quarter q; rows past nt stay zero */
+            uint32_t bl = 0u, bh = 0u;
+            if (p == 0u && tk < t.nt) {
 #pragma unroll
-                for (int qq = 0; qq < 4; qq++) {
-                    const uint32_t b01 = bw[1 + 2 * qq], b23 = bw[2 + 2 * qq];
-                    /* bsums j = 4qq .. 4qq + 3 as int16; low bytes unsigned, high bytes signed */
-                    lo[qq] = (b01 & 0xffu) | ((b01 >> 8) & 0xff00u) | ((b23 & 0xffu) << 16) | ((b23 << 8) & 0xff000000u);
-                    hi[qq] = ((b01 >> 8) & 0xffu) | ((b01 >> 16) & 0xff00u) | (((b23 >> 8) & 0xffu) << 16) |
-                             (b23 & 0xff000000u);
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t w = bw[j >> 1];
+                    const int b = (j & 1) ? ((int)w >> 16) : (int)(int16_t)(w & 0xffffu);
+                    const uint32_t v = (uint32_t)(b + 2048);
+                    bl |= (v & 15u) << (8 * j);
+                    bh |= (v >> 4) << (8 * j);
                 }
-                uint32_t *as = (uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + tk) * SM::ASIDE_T);
-                as[0] = bw[0];
-#pragma unroll
-                for (int qq = 0; qq < 4; qq++) as[1 + qq] = lo[qq], as[5 + qq] = hi[qq];
+                if (q == 0u) ((float *)(sm + SM::OFF_ASIDE))[x * PM_I8_N + tk] = __uint_as_float(ydw);
             }
             /* the two 128-wide K chunks of the super-block */
 #pragma unroll
             for (uint32_t h = 0; h < 2; h++) {
-                const uint32_t c = 2u * g + h, ab = c & 1u;
-                if (c >= 2 && !pm_mbar_wait(&a_empty[ab], ((c >> 1) - 1u) & 1u, a.err, a.wait)) {
+                const uint32_t c = 2u * g + h, ab = c % SM::NAB;
+                if (c >= SM::NAB &&
+                    __any_sync(0xffffffffu, !pm_mbar_wait(&a_empty[ab], ((c / SM::NAB) - 1u) & 1u, a.err, a.wait))) {
                     fail = true;
                     break;
                 }
@@ -377,8 +421,22 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                     *(uint4 *)(B + (((2u * q) ^ (tk & 7u)) << 4)) = make_uint4(bv[0], bv[1], bv[2], bv[3]);
                     *(uint4 *)(B + (((2u * q + 1u) ^ (tk & 7u)) << 4)) = make_uint4(bv[4], bv[5], bv[6], bv[7]);
                 }
+                if (h == 0u) { /* the mins-sum operands ride with K chunk 0: buffer g % 2, free once the
+                                * MMAs of chunk 2g - NAB (issued after super-block g - 2's) are done */
+                    if (NM == 2 || p == 0u) {
+                        uint8_t *AM = sm + SM::OFF_AM + ((g & 1u) * NM + m) * 4096u;
+                        *(uint4 *)(AM + pm_sw32_off(r, 0)) = make_uint4(mn[0], mn[1], mn[2], mn[3]);
+                        *(uint4 *)(AM + pm_sw32_off(r, 1)) = make_uint4(m16[0], m16[1], m16[2], m16[3]);
+                    }
+                    if (p == 0u) { /* word q of the token's l and h units */
+                        uint8_t *BM = sm + SM::OFF_BM + (g & 1u) * 1024u;
+                        *(uint32_t *)(BM + pm_sw32_off(tk, 0) + 4u * q) = bl;
+                        *(uint32_t *)(BM + pm_sw32_off(tk, 1) + 4u * q) = bh;
+                    }
+                }
                 pm_fence_proxy_async(); /* generic-proxy writes before the MMA reads them */
-                pm_mbar_arrive(&a_full[ab]);
+                __syncwarp();
+                if (lane == 0) pm_mbar_arrive(&a_full[ab]);
             }
         }
         if (fail) atomicOr(&s_fail, 1u);
@@ -399,10 +457,10 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                     break;
                 }
                 pm_tc_fence_after();
-                const uint32_t idesc = pm_idesc_i8(128, N);
+                const uint32_t idesc = pm_idesc_i8(128, N), udesc = pm_idesc_u8(128, N);
                 for (uint32_t h = 0; h < 2; h++) {
-                    const uint32_t c = 2u * g + h, ab = c & 1u;
-                    if (!pm_mbar_wait(&a_full[ab], (c >> 1) & 1u, a.err, a.wait)) {
+                    const uint32_t c = 2u * g + h, ab = c % SM::NAB;
+                    if (!pm_mbar_wait(&a_full[ab], (c / SM::NAB) & 1u, a.err, a.wait)) {
                         ok = false;
                         break;
                     }
@@ -411,10 +469,13 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
 #pragma unroll
                     for (int mm = 0; mm < NM; mm++) {
                         const uint64_t ad = pm_desc_sw128(sm + SM::OFF_A + (ab * NM + (uint32_t)mm) * SM::A);
-                        const uint32_t d = tmem + x * (NM * 32u) + (uint32_t)mm * 32u;
+                        const uint32_t d = tmem + x * (NM * 64u) + (uint32_t)mm * 64u;
 #pragma unroll
                         for (uint32_t kk = 0; kk < 4; kk++)
                             pm_mma_i8(d, ad + 2 * kk, bd + 2 * kk, idesc, (h > 0 || kk > 0) ? 1u : 0u);
+                        if (h == 0u) /* msum + 2048 sum m into the slot's second 32 columns */
+                            pm_mma_i8(d + 32u, pm_desc_sw32(sm + SM::OFF_AM + ((g & 1u) * NM + (uint32_t)mm) * 4096u),
+                                      pm_desc_sw32(sm + SM::OFF_BM + (g & 1u) * 1024u), udesc, 0u);
                     }
                     pm_mma_commit(&a_empty[ab]);
                 }
@@ -437,7 +498,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
         for (uint32_t g = 0; g < G; g++) {
             const uint32_t sb = g % nsb, x = g % PM_I8_AC;
             if (sb == 0) pm_i8_task_get<NM>(a, task0 + (g / nsb) * gridDim.x, nrb, nsb, n_tiles, t);
-            if (!pm_mbar_wait(&acc_full[x], (g / PM_I8_AC) & 1u, a.err, a.wait)) {
+            if (__any_sync(0xffffffffu, !pm_mbar_wait(&acc_full[x], (g / PM_I8_AC) & 1u, a.err, a.wait))) {
                 atomicOr(&s_fail, 1u);
                 break;
             }
@@ -446,24 +507,25 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             if (active) {
 #pragma unroll
                 for (int mm = 0; mm < NM; mm++) {
-                    int32_t v[16];
-                    pm_tmem_ld16i(tmem + ((lq * 32u) << 16) + x * (NM * 32u) + (uint32_t)mm * 32u + k0, v);
-                    const uint4 *side = (const uint4 *)(sm + SM::OFF_SIDE) + (x * NM + (uint32_t)mm) * 256u + 2u * row;
-                    const uint4 s0 = side[0], s1 = side[1];
+                    int32_t v[16], mv[16];
+                    const uint32_t tc = tmem + ((lq * 32u) << 16) + x * (NM * 64u) + (uint32_t)mm * 64u + k0;
+                    pm_tmem_ld16i2(tc, tc + 32u, v, mv);
+                    const uint4 s0 = ((const uint4 *)(sm + SM::OFF_SIDE))[(x * NM + (uint32_t)mm) * 128u + row];
                     const float d = __uint_as_float(s0.x), dm = __uint_as_float(s0.y);
-                    const uint32_t mw[4] = {s0.z, s0.w, s1.x, s1.y};
+                    const int corr = (int)s0.z;
+                    const float4 *yq = (const float4 *)(sm + SM::OFF_ASIDE) + (x * PM_I8_N + k0) / 4u;
+                    float yds[16];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float4 f = yq[i];
+                        yds[4 * i] = f.x, yds[4 * i + 1] = f.y, yds[4 * i + 2] = f.z, yds[4 * i + 3] = f.w;
+                    }
+                    /* all 16 columns, branch-free (independent chains): the terms of tokens past
+                     * nt are never written out */
 #pragma unroll
                     for (uint32_t k = 0; k < 16; k++) {
-                        if (k0 + k >= t.nt) break; /* uniform: only the tile's tokens */
-                        const uint32_t *as = (const uint32_t *)(sm + SM::OFF_ASIDE + (x * PM_I8_N + k0 + k) * SM::ASIDE_T);
-                        const float yd = __uint_as_float(as[0]);
-                        int lo = 0, hi = 0;
-#pragma unroll
-                        for (int qq = 0; qq < 4; qq++) {
-                            lo = pm_dp4a_uu(mw[qq], as[1 + qq], lo);
-                            hi = pm_dp4a_us(mw[qq], (int)as[5 + qq], hi);
-                        }
-                        const int msum = lo + 256 * hi;
+                        const float yd = yds[k];
+                        const int msum = mv[k] - corr;
                         /* total += yd xd isum - yd xmin msum (cpu_dot.rs:732-767, q2_K) */
                         const float term = __fsub_rn(__fmul_rn(__fmul_rn(yd, d), (float)v[k]),
                                                      __fmul_rn(__fmul_rn(yd, dm), (float)msum));
@@ -500,7 +562,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     pm_tc_fence_after();
     if (warp == PM_I8_MMA_WARP) {
         __syncwarp();
-        pm_tmem_free(tmem, 256);
+        pm_tmem_free(tmem, SM::TMEM_COLS);
     }
     if (tid == 0 && s_fail) atomicOr(a.err, PM_ERR_TIMEOUT);
 }
