@@ -17,8 +17,8 @@
  * instructions per 64 weights per token.
  *
  * Work.  A tile is up to 32 tokens of one routed expert (the selection
- * kernel lists them); a task is (tile, 128-row block of the pass's
- * matrices).  Persistent CTAs take tasks round-robin and stream their
+ * kernel lists them); a task is (tile, two 128-row A matrices: gate and
+ * up of one block, or two consecutive blocks of down).  Persistent CTAs take tasks round-robin and stream their
  * super-blocks through four pipelines:
  *   load    one producer warp fills a ring of super-block stages: per
  *           matrix one bulk copy of the 10.5 KB tile-plane chunk (the
@@ -174,7 +174,7 @@ struct pm_i8_smem {
     static_assert(TOTAL + 1024u <= 227u * 1024u, "integer tensor-core pass exceeds shared memory");
 };
 
-/* one task = (tile, 128-row block) */
+/* one task = (tile, 128-row block of gate and up, or 256 rows of down) */
 struct pm_i8_task {
     const uint8_t *w[2]; /* the block's first chunk (super-block 0), per matrix */
     uint32_t s0, nt, row0, e;
@@ -191,14 +191,16 @@ __device__ __forceinline__ bool pm_i8_task_get(const pm_layer_args &a, uint32_t 
     t.e = e;
     t.s0 = s0 + tt.y;
     t.nt = cnt - tt.y < PM_I8_N ? cnt - tt.y : PM_I8_N;
-    t.row0 = rbk * 128u;
-    const uint64_t chunk0 = ((uint64_t)e * nrb + rbk) * nsb * PM_I8_CHUNK;
-    if (NM == 2) {
+    if (NM == 2) { /* gate and up rows of one 128-row block */
+        const uint64_t chunk0 = ((uint64_t)e * nrb + rbk) * nsb * PM_I8_CHUNK;
+        t.row0 = rbk * 128u;
         t.w[0] = a.gate_t + chunk0;
         t.w[1] = a.up_t + chunk0;
-    } else {
+    } else { /* down: two consecutive 128-row blocks (nrb counts block pairs) */
+        const uint64_t chunk0 = ((uint64_t)e * 2u * nrb + 2u * rbk) * nsb * PM_I8_CHUNK;
+        t.row0 = rbk * 256u;
         t.w[0] = a.down_t + chunk0;
-        t.w[1] = nullptr;
+        t.w[1] = t.w[0] + (uint64_t)nsb * PM_I8_CHUNK;
     }
     return true;
 }
@@ -231,7 +233,10 @@ __device__ __forceinline__ void pm_i8_lds(const uint8_t *base, uint32_t off, uin
 
 template <int Q, int NM>
 __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_constant__ pm_layer_args a) {
-    using SM = pm_i8_smem<NM>;
+    /* NM: the pass (2 gate/up, 1 down); every task streams NMA = 2 matrices - gate and up
+     * of one 128-row block, or two consecutive 128-row blocks of down */
+    constexpr int NMA = 2;
+    using SM = pm_i8_smem<NMA>;
     constexpr uint32_t RS = SM::RS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = (uint8_t *)(((uintptr_t)smem_raw + 1023u) & ~(uintptr_t)1023u);
@@ -239,7 +244,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
     __shared__ uint32_t tslot, s_fail;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t n_tiles = __ldcg(a.n_items + 7);
-    const uint32_t rows = NM == 2 ? a.Fr : a.H, nrb = rows / 128u;
+    const uint32_t nrb = NM == 2 ? a.Fr / 128u : a.H / 256u; /* tasks per tile */
     const uint32_t nsb = (NM == 2 ? a.H : a.Fr) / 256u;
     const uint32_t n_tasks = n_tiles * nrb;
     if (blockIdx.x >= n_tasks) return;
@@ -290,14 +295,14 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             }
             uint8_t *stage = sm + SM::OFF_RING + s * SM::STAGE;
             if (lane == 0) {
-                pm_mbar_expect_tx(&full[s], NM * PM_I8_CHUNK);
+                pm_mbar_expect_tx(&full[s], NMA * PM_I8_CHUNK);
 #pragma unroll
-                for (int m = 0; m < NM; m++)
+                for (int m = 0; m < NMA; m++)
                     pm_bulk_g2s(stage + m * PM_I8_CHUNK, t.w[m] + (uint64_t)sb * PM_I8_CHUNK, PM_I8_CHUNK, &full[s]);
             }
             if (lane < t.nt) { /* a q8_K block (292 bytes at a 4-byte boundary) is 19 16-byte pieces */
                 const uintptr_t src = (blk0 + (uintptr_t)sb * PM_Q8_K_BYTES) & ~(uintptr_t)15;
-                uint8_t *dst = stage + NM * PM_I8_CHUNK + lane * PM_I8_TOKB;
+                uint8_t *dst = stage + NMA * PM_I8_CHUNK + lane * PM_I8_TOKB;
 #pragma unroll
                 for (uint32_t k = 0; k < PM_I8_TOKB / 16u; k++) pm_cp_async16(dst + 16u * k, (const void *)(src + 16u * k));
             }
@@ -308,12 +313,12 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
         for (uint32_t h = g > RS ? g - RS : 0u; h < g; h++) pm_mbar_wait(&full[h % RS], (h / RS) & 1u, nullptr);
         pm_cp_async_wait<0>();
     } else if (warp < 8) {
-        /* ===== decode warps: thread (r, p) = weight row r, part p.  NM 2: part p takes
-         * matrix p; NM 1: part p takes K chunk p of the one matrix.  As token (tk, q) a thread
-         * also stages quarter q of token tk's chunk-p q8 values (B), and (p, q) = (0, 0) the
-         * token's scale and bsums for the epilogue. ===== */
+        /* ===== decode warps: thread (r, p) = row r of the task's matrix p (gate / up, or the
+         * first / second 128-row block of down).  As token (tk, q) a thread also stages
+         * quarter q of token tk's chunk-p q8 values (B), and p = 0 threads the token's scale
+         * and bsums for the epilogue. ===== */
         const uint32_t r = tid & 127u, p = tid >> 7, tk = r >> 2, q = r & 3u;
-        const uint32_t m = NM == 2 ? p : 0u; /* the matrix this thread decodes */
+        const uint32_t m = NMA == 2 ? p : 0u; /* the matrix this thread decodes */
         bool fail = false;
         pm_i8_task t;
         uintptr_t my_blk = 0; /* token tk's q8_K row (block 0) */
@@ -336,7 +341,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             uint32_t qw[2][8];
 #pragma unroll
             for (uint32_t h = 0; h < 2; h++) {
-                if (NM == 2 || p == h) {
+                if (NMA == 2 || p == h) {
                     const uint4 u0 = *(const uint4 *)(W + (2u * h * 128u + r) * 16u);
                     const uint4 u1 = *(const uint4 *)(W + ((2u * h + 1u) * 128u + r) * 16u);
                     qw[h][0] = u0.x, qw[h][1] = u0.y, qw[h][2] = u0.z, qw[h][3] = u0.w;
@@ -347,7 +352,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 }
             }
             const uintptr_t blk = my_blk + (uintptr_t)sb * PM_Q8_K_BYTES;
-            const uint8_t *tok = sm + SM::OFF_RING + s * SM::STAGE + NM * PM_I8_CHUNK + tk * PM_I8_TOKB;
+            const uint8_t *tok = sm + SM::OFF_RING + s * SM::STAGE + NMA * PM_I8_CHUNK + tk * PM_I8_TOKB;
             const uint32_t tb = (uint32_t)(blk & 15u); /* the block's offset in its slot */
             uint32_t bv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, bw[2] = {0u, 0u}, ydw = 0u;
             if (tk < t.nt) {
@@ -370,11 +375,11 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             uint32_t mn[4], m16[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) mn[i] = (scw[i] >> 4) & 0x0f0f0f0fu, m16[i] = scw[i] & 0xf0f0f0f0u;
-            if (NM == 2 || p == 0u) { /* side data of (row, super-block, matrix m): d, dmin, 2048 sum m */
+            if (NMA == 2 || p == 0u) { /* side data of (row, super-block, matrix m): d, dmin, 2048 sum m */
                 int msum = 0;
 #pragma unroll
                 for (int i = 0; i < 4; i++) msum = pm_dp4a_uu(mn[i], 0x01010101u, msum);
-                uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NM + m) * 128u + r;
+                uint4 *side = (uint4 *)(sm + SM::OFF_SIDE) + (x * NMA + m) * 128u + r;
                 *side = make_uint4(__float_as_uint(pm_h2f(dd & 0xffffu)), __float_as_uint(pm_h2f(dd >> 16)),
                                    (uint32_t)(2048 * msum), 0u);
             }
@@ -401,9 +406,9 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                     fail = true;
                     break;
                 }
-                if (NM == 2 || p == h) { /* A: this thread's row of matrix m, chunk h */
+                if (NMA == 2 || p == h) { /* A: this thread's row of matrix m, chunk h */
                     const uint32_t sc4[2] = {scw[2 * h] & 0x0f0f0f0fu, scw[2 * h + 1] & 0x0f0f0f0fu};
-                    uint8_t *A = sm + SM::OFF_A + (ab * NM + m) * SM::A + (r >> 3) * 1024u + (r & 7u) * 128u;
+                    uint8_t *A = sm + SM::OFF_A + (ab * NMA + m) * SM::A + (r >> 3) * 1024u + (r & 7u) * 128u;
 #pragma unroll
                     for (uint32_t j = 0; j < 8; j++) { /* 16-byte unit j: shift 2 (j / 2), qs words 4 (j % 2) .. + 3 */
                         const uint32_t sc = (sc4[j >> 2] >> (8u * (j & 3u))) & 0xffu;
@@ -423,8 +428,8 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                 }
                 if (h == 0u) { /* the mins-sum operands ride with K chunk 0: buffer g % 2, free once the
                                 * MMAs of chunk 2g - NAB (issued after super-block g - 2's) are done */
-                    if (NM == 2 || p == 0u) {
-                        uint8_t *AM = sm + SM::OFF_AM + ((g & 1u) * NM + m) * 4096u;
+                    if (NMA == 2 || p == 0u) {
+                        uint8_t *AM = sm + SM::OFF_AM + ((g & 1u) * NMA + m) * 4096u;
                         *(uint4 *)(AM + pm_sw32_off(r, 0)) = make_uint4(mn[0], mn[1], mn[2], mn[3]);
                         *(uint4 *)(AM + pm_sw32_off(r, 1)) = make_uint4(m16[0], m16[1], m16[2], m16[3]);
                     }
@@ -467,14 +472,14 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
                     pm_tc_fence_after();
                     const uint64_t bd = pm_desc_sw128(sm + SM::OFF_B + ab * 4096u);
 #pragma unroll
-                    for (int mm = 0; mm < NM; mm++) {
-                        const uint64_t ad = pm_desc_sw128(sm + SM::OFF_A + (ab * NM + (uint32_t)mm) * SM::A);
-                        const uint32_t d = tmem + x * (NM * 64u) + (uint32_t)mm * 64u;
+                    for (int mm = 0; mm < NMA; mm++) {
+                        const uint64_t ad = pm_desc_sw128(sm + SM::OFF_A + (ab * NMA + (uint32_t)mm) * SM::A);
+                        const uint32_t d = tmem + x * (NMA * 64u) + (uint32_t)mm * 64u;
 #pragma unroll
                         for (uint32_t kk = 0; kk < 4; kk++)
                             pm_mma_i8(d, ad + 2 * kk, bd + 2 * kk, idesc, (h > 0 || kk > 0) ? 1u : 0u);
                         if (h == 0u) /* msum + 2048 sum m into the slot's second 32 columns */
-                            pm_mma_i8(d + 32u, pm_desc_sw32(sm + SM::OFF_AM + ((g & 1u) * NM + (uint32_t)mm) * 4096u),
+                            pm_mma_i8(d + 32u, pm_desc_sw32(sm + SM::OFF_AM + ((g & 1u) * NMA + (uint32_t)mm) * 4096u),
                                       pm_desc_sw32(sm + SM::OFF_BM + (g & 1u) * 1024u), udesc, 0u);
                     }
                     pm_mma_commit(&a_empty[ab]);
@@ -489,9 +494,9 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
         /* ===== epilogue: warps 8-15; warp w reads tensor-memory lanes 32 (w % 4) .. + 31 and
          * tokens 16 ((w - 8) / 4) .. + 15 of the tile ===== */
         const uint32_t lq = warp & 3u, row = lq * 32u + lane, k0 = 16u * ((warp - 8u) >> 2);
-        float acc[NM][16];
+        float acc[NMA][16];
 #pragma unroll
-        for (int mm = 0; mm < NM; mm++)
+        for (int mm = 0; mm < NMA; mm++)
 #pragma unroll
             for (uint32_t k = 0; k < 16; k++) acc[mm][k] = 0.0f;
         pm_i8_task t;
@@ -506,11 +511,11 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             const bool active = k0 < t.nt; /* warp-uniform */
             if (active) {
 #pragma unroll
-                for (int mm = 0; mm < NM; mm++) {
+                for (int mm = 0; mm < NMA; mm++) {
                     int32_t v[16], mv[16];
-                    const uint32_t tc = tmem + ((lq * 32u) << 16) + x * (NM * 64u) + (uint32_t)mm * 64u + k0;
+                    const uint32_t tc = tmem + ((lq * 32u) << 16) + x * (NMA * 64u) + (uint32_t)mm * 64u + k0;
                     pm_tmem_ld16i2(tc, tc + 32u, v, mv);
-                    const uint4 s0 = ((const uint4 *)(sm + SM::OFF_SIDE))[(x * NM + (uint32_t)mm) * 128u + row];
+                    const uint4 s0 = ((const uint4 *)(sm + SM::OFF_SIDE))[(x * NMA + (uint32_t)mm) * 128u + row];
                     const float d = __uint_as_float(s0.x), dm = __uint_as_float(s0.y);
                     const int corr = (int)s0.z;
                     const float4 *yq = (const float4 *)(sm + SM::OFF_ASIDE) + (x * PM_I8_N + k0) / 4u;
@@ -537,22 +542,23 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
             __syncwarp();
             if (lane == 0) pm_mbar_arrive(&acc_empty[x]);
             if (sb == nsb - 1u && active) { /* the task's rows are complete: outputs, in the CPU lane's order */
-                const uint32_t grow = t.row0 + row;
+                const uint32_t grow = t.row0 + row; /* gate/up; down rows are grow + 128 mm */
 #pragma unroll
                 for (uint32_t k = 0; k < 16; k++) {
                     if (k0 + k < t.nt) {
                         const uint32_t pr = __ldcg(a.pairs + t.s0 + k0 + k);
                         if (NM == 2) {
-                            float gg = acc[0][k], uu = acc[NM - 1][k];
+                            float gg = acc[0][k], uu = acc[1][k];
                             if (a.gate_b) gg = __fadd_rn(gg, a.gate_b[(uint64_t)t.e * a.Fr + grow]);
                             if (a.up_b) uu = __fadd_rn(uu, a.up_b[(uint64_t)t.e * a.Fr + grow]);
                             a.mid[(uint64_t)pr * a.Fmax + grow] = __fmul_rn(pm_glu(gg, uu, a.act), __ldcg(a.w + pr));
                         } else {
-                            a.partial[(uint64_t)pr * a.H + grow] = acc[0][k];
+#pragma unroll
+                            for (int mm = 0; mm < NMA; mm++) a.partial[(uint64_t)pr * a.H + grow + 128u * mm] = acc[mm][k];
                         }
                     }
 #pragma unroll
-                    for (int mm = 0; mm < NM; mm++) acc[mm][k] = 0.0f;
+                    for (int mm = 0; mm < NMA; mm++) acc[mm][k] = 0.0f;
                 }
             }
         }
@@ -591,7 +597,7 @@ template <int Q, int NM>
 static int pm_i8_launch(const pm_layer_args &a, cudaStream_t st) {
     static uint64_t done = 0;
     auto k = pm_tci8_kernel<Q, NM>;
-    const uint32_t smem = pm_i8_smem<NM>::TOTAL + 1024u;
+    const uint32_t smem = pm_i8_smem<2>::TOTAL + 1024u;
     if (!pm_smem_attr(k, smem, &done)) return 0;
     k<<<a.n_sm, PM_I8_THREADS, smem, st>>>(a);
     return pm_ok(cudaGetLastError(), "moe layer integer tensor-core launch");
