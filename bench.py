@@ -74,7 +74,7 @@ WORKLOADS = {
 # DRAM bytes (read + write) per gate/up launch over the launch's algorithmic bytes, from one
 # ncu capture per workload (committed summaries under profiles/); the reported traffic scales
 # it to this run's launch.  None where no capture of that workload exists.
-TRAFFIC_RATIO = {"c2-decode": (228.40 + 13.16) / 221.2}
+TRAFFIC_RATIO = {"c2-decode": (228.40 + 13.16) / 221.2, "c4-decode": (387.09 + 16.27) / 398.9}
 
 
 def log(*a):

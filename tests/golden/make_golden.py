@@ -21,7 +21,9 @@ def parse(src: str, name: str):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("PULSAR_REFERENCE")
+    if not ref:  # BASELINE.json names the reference tree
+        ref = json.load(open(os.path.join(os.path.dirname(__file__), "..", "..", "BASELINE.json")))["reference_path"]
     src = open(os.path.join(ref, "crates/kernels/cuda/iq2_tables.inc")).read()
     grid = parse(src, "cuda_iq2xxs_grid[256]")
     ks = parse(src, "cuda_ksigns_iq2xs[128]")
