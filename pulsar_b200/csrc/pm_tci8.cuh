@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(PM_I8_THREADS, 1) pm_tci8_kernel(const __grid_
 }
 
 /* q8_K of the mid rows of every tile pair (the down pass's B operand), the
- * CPU lane's quantizer (cpu_dot.rs:26-50); block = tile, warp per (token,
+ * CPU lane's quantizer (cpu_dot.rs:26-50); blocks (tile, y), warp per (token,
  * 256-block) */
 static __global__ void __launch_bounds__(256) pm_i8_midq_kernel(const __grid_constant__ pm_layer_args a) {
     const uint32_t tile = blockIdx.x;
@@ -583,7 +583,8 @@ static __global__ void __launch_bounds__(256) pm_i8_midq_kernel(const __grid_con
     const uint32_t s0 = __ldcg(a.item_start + tt.x), cnt = __ldcg(a.item_start + tt.x + 1) - s0;
     const uint32_t nt = cnt - tt.y < PM_I8_N ? cnt - tt.y : PM_I8_N;
     const uint32_t nb = (a.Fr + 255u) / 256u;
-    for (uint32_t job = threadIdx.x >> 5; job < nt * nb; job += blockDim.x >> 5) {
+    const uint32_t nw = (blockDim.x >> 5) * gridDim.y; /* the tile's jobs spread over gridDim.y blocks */
+    for (uint32_t job = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5); job < nt * nb; job += nw) {
         const uint32_t k = job / nb, b = job % nb;
         const uint32_t pr = __ldcg(a.pairs + s0 + tt.y + k);
         const uint32_t valid = a.Fr - b * 256u < 256u ? a.Fr - b * 256u : 256u;
@@ -604,6 +605,6 @@ static int pm_i8_launch(const pm_layer_args &a, cudaStream_t st) {
 }
 
 static int pm_i8_midq_launch(const pm_layer_args &a, cudaStream_t st) {
-    pm_i8_midq_kernel<<<a.max_i8, 256, 0, st>>>(a);
+    pm_i8_midq_kernel<<<dim3(a.max_i8, 8), 256, 0, st>>>(a);
     return pm_ok(cudaGetLastError(), "moe layer integer tensor-core mid q8_K launch");
 }
